@@ -1,0 +1,197 @@
+// Shared device/host helpers for the Z-Image B200 kernels (sm_100a only).
+//
+// Rounding helpers restate the reference's bf16 rounding points
+// (src/zimage_triton/quantization/int8_linear.py:114-138 and the Triton
+// kernels under src/zimage_triton/kernels/): every elementwise bf16 op is an
+// fp32 op rounded once to bf16 (RNE).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/zimage_b200.h"
+
+#define ZIB_HOST_CHECK(cond, status, ...)             \
+  do {                                                \
+    if (!(cond)) {                                    \
+      zib_set_error(__VA_ARGS__);                     \
+      return (status);                                \
+    }                                                 \
+  } while (0)
+
+// thread-local last-error message (defined in zib_api.cu)
+void zib_set_error(const char* fmt, ...);
+int zib_check_launch(const char* what);
+
+namespace zib {
+
+constexpr int kGroup = 128;                      // Hadamard block (int8_linear.py:28)
+constexpr float kHBf16 = 0.08837890625f;         // bf16(1/sqrt(128)), int8_linear.py:120-123
+constexpr float kHFp32 = 0.0883883461356163f;    // fp32 1/sqrt(128), hadamard.py:40-41
+
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float(((uint32_t)b) << 16);
+}
+
+__device__ __forceinline__ uint16_t float_to_bf16_bits(float v) {
+  __nv_bfloat16 h = __float2bfloat16_rn(v);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// Correctly rounded bf16 of the exact product s * h, given fp32 s.
+// p = RN32(s*h); e = s*h - p exactly (FMA).  A bf16 midpoint strictly between
+// s*h and p cannot exist, so only p sitting exactly on a midpoint needs the
+// sign of e to pick the direction.
+__device__ __forceinline__ float mul_round_bf16(float s, float h) {
+  float p = __fmul_rn(s, h);
+  float e = __fmaf_rn(s, h, -p);
+  uint32_t b = __float_as_uint(p);
+  if ((b & 0xFFFFu) == 0x8000u && e != 0.0f) {
+    uint32_t t = b & 0xFFFF0000u;
+    bool away = (e > 0.0f) == (p > 0.0f);
+    return __uint_as_float(away ? t + 0x10000u : t);
+  }
+  return bf16_round(p);
+}
+
+// q = clamp(rne(bf16(v / s)), -128, 127) for bf16-valued v and scale s
+// (int8_linear.py:130).  v / s is formed as v * rcp with rcp = RN(1/s); that
+// product is within 2 ulp of RN(v/s), so the bf16 rounding can only differ when
+// the product's low 16 bits are within a few ulp of the bf16 midpoint 0x8000;
+// those (rare) lanes recompute the quotient with an IEEE division.
+__device__ __forceinline__ int quant_i8(float v, float s, float rcp) {
+  float q0 = __fmul_rn(v, rcp);
+  uint32_t lo = __float_as_uint(q0) & 0xFFFFu;
+  if (lo - 0x7FFAu <= 12u) q0 = __fdiv_rn(v, s);
+  float r = rintf(bf16_round(q0));
+  r = fminf(fmaxf(r, -128.0f), 127.0f);
+  return (int)r;
+}
+
+// x_scale = bf16( bf16(max(amax, 1e-5)) / 127 )   (int8_linear.py:129)
+__device__ __forceinline__ float act_scale(float amax_bf16) {
+  float a = bf16_round(fmaxf(amax_bf16, 1e-5f));
+  return bf16_round(__fdiv_rn(a, 127.0f));
+}
+
+// rstd = 1 / sqrt(RN32(sum)/n + eps), IEEE fp32 ops
+__device__ __forceinline__ float rstd_from_sum(double ss, int n, float eps) {
+  float ms = __fdiv_rn((float)ss, (float)n);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+}
+
+// --- 16-byte vector I/O --------------------------------------------------
+
+struct alignas(16) bf16x8 { uint16_t h[8]; };
+
+__device__ __forceinline__ void load_bf16x8(const void* p, float v[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ void load_bf16x8_nc(const void* p, float v[8]) {
+  uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// v[] must already hold bf16-exact values
+__device__ __forceinline__ void store_bf16x8(void* p, const float v[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    w[i] = (__float_as_uint(v[2 * i]) >> 16) | (__float_as_uint(v[2 * i + 1]) & 0xFFFF0000u);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void store_i8x8(void* p, const int q[8]) {
+  uint32_t a = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+  uint32_t b = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+  *reinterpret_cast<uint2*>(p) = make_uint2(a, b);
+}
+
+// --- Walsh-Hadamard transform over 128 (Sylvester order) ------------------
+// A 128-group lives in 16 consecutive lanes x 8 values (lane bits 0..3 are
+// index bits 3..6).  Index bits 0..2 are combined in-thread, bits 3..6 with
+// xor shuffles.  All adds are exact for bf16-derived data in all practical
+// cases (see the oracle's exactness notes).
+
+__device__ __forceinline__ void fwht8(float v[8]) {
+#pragma unroll
+  for (int h = 1; h < 8; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if ((i & h) == 0) {
+        float a = v[i], b = v[i + h];
+        v[i] = __fadd_rn(a, b);
+        v[i + h] = __fsub_rn(a, b);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void fwht_cross16(float v[8], int lane) {
+#pragma unroll
+  for (int m = 1; m < 16; m <<= 1) {
+    bool upper = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float o = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
+      v[i] = upper ? __fsub_rn(o, v[i]) : __fadd_rn(v[i], o);
+    }
+  }
+}
+
+// --- block reductions -----------------------------------------------------
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// scratch must hold >= 32 entries; result broadcast to all threads
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) scratch[wid] = v;
+  __syncthreads();
+  float r = lane < nw ? scratch[lane] : 0.0f;
+  return warp_max(r);
+}
+
+__device__ __forceinline__ double block_sum_f64(double v, double* scratch) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_sum_f64(v);
+  __syncthreads();
+  if (lane == 0) scratch[wid] = v;
+  __syncthreads();
+  double r = lane < nw ? scratch[lane] : 0.0;
+  return warp_sum_f64(r);
+}
+
+}  // namespace zib

@@ -1,0 +1,470 @@
+"""Patch a ComfyUI NextDiT (Lumina-2 / Z-Image) model with the sm_100a kernels.
+
+Same surface as ``src/zimage_triton/models/patching_comfyui.py`` of the
+reference: RMSNorm modules become ``TritonRMSNorm`` (weight shared,
+``_original_module`` kept), ``FeedForward._forward_silu_gating`` becomes the
+SwiGLU kernel (``_original_silu_gating`` kept), ``JointAttention.forward`` and
+``JointTransformerBlock.forward`` are replaced (``_original_forward`` kept),
+and ``apply_triton_kernels_comfyui`` returns the same stats dict.
+
+The block forward has two paths with identical arithmetic:
+
+* fused (all five block linears W8A8+Hadamard, no bias, 128-wide heads, no
+  GQA): per block 6 row kernels, 4 tcgen05 GEMMs (w1 and w3 run as one
+  3840 -> 2x10240 GEMM: they quantise the same activation, int8_linear.py:129-130)
+  and SDPA.  Norm -> modulate -> rotate -> quantise, residual -> norm ->
+  modulate -> rotate -> quantise and SwiGLU -> rotate -> quantise each run as
+  one pass; QK-norm + RoPE run in place on the QKV GEMM output.
+* composed: the reference's sequence of module calls, each on a kernel.
+"""
+
+from __future__ import annotations
+
+import logging
+import types
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import _lib
+from ..kernels.fused_qknorm_rope import qknorm_rope_into, rope_tables
+from ..kernels.rms_norm import TritonRMSNorm
+from ..kernels.swiglu import triton_swiglu_forward
+
+logger = logging.getLogger(__name__)
+
+# The fused block executor and the composed module path compute the same
+# values; tests flip this to compare them.
+ENABLE_FUSED_BLOCK = True
+
+
+def _eps(mod: nn.Module) -> float:
+    """getattr(mod, 'eps', 1e-5) or 1e-5 (patching_comfyui.py:157-158, :324-327)."""
+    return getattr(mod, "eps", 1e-5) or 1e-5
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm replacement (patching_comfyui.py:31-68)
+# ---------------------------------------------------------------------------
+
+def _replace_all_rms_norm_comfyui(model: nn.Module, stats: dict) -> None:
+    for name, module in list(model.named_modules()):
+        if isinstance(module, TritonRMSNorm):
+            continue
+        if type(module).__name__ != "RMSNorm":
+            continue
+        if not hasattr(module, "weight") or module.weight is None:
+            continue
+        parts = name.split(".")
+        parent = model
+        for part in parts[:-1]:
+            parent = getattr(parent, part)
+        attr = parts[-1]
+        old = getattr(parent, attr)
+        new_norm = TritonRMSNorm(old.weight.shape[0], eps=_eps(old))
+        new_norm.weight = old.weight
+        new_norm._original_module = old
+        setattr(parent, attr, new_norm)
+        stats["rms_norm"] += 1
+
+
+# ---------------------------------------------------------------------------
+# FFN SwiGLU (patching_comfyui.py:76-107)
+# ---------------------------------------------------------------------------
+
+def _make_ffn_forward_comfyui(ffn: nn.Module):
+    def _forward_silu_gating(self, x1: torch.Tensor, x3: torch.Tensor) -> torch.Tensor:
+        return triton_swiglu_forward(x1, x3)
+
+    return types.MethodType(_forward_silu_gating, ffn)
+
+
+def _patch_all_ffn_comfyui(model: nn.Module, stats: dict) -> None:
+    for module in model.modules():
+        if (type(module).__name__ == "FeedForward" and hasattr(module, "w1") and hasattr(module, "w2")
+                and hasattr(module, "w3")):
+            if not hasattr(module, "_original_silu_gating"):
+                module._original_silu_gating = module._forward_silu_gating
+            module._forward_silu_gating = _make_ffn_forward_comfyui(module)
+            stats["swiglu"] += 1
+
+
+# ---------------------------------------------------------------------------
+# RoPE tables and attention
+# ---------------------------------------------------------------------------
+
+def _convert_rope_matrix_to_complex(freqs_cis: torch.Tensor) -> torch.Tensor:
+    """2x2 rotation matrices (b, n, [1,] d//2, 2, 2) -> complex64 (patching_comfyui.py:115-134)."""
+    cos = freqs_cis[..., 0, 0]
+    sin = freqs_cis[..., 1, 0]
+    if cos.ndim == 4 and cos.shape[2] == 1:
+        cos = cos.squeeze(2)
+        sin = sin.squeeze(2)
+    return torch.complex(cos.float(), sin.float())
+
+
+_TABLE_CACHE: dict = {}
+
+
+def _cos_sin(freqs_cis: torch.Tensor, batch: int):
+    """(cos, sin, batch_stride) fp32 tables from the 2x2-matrix or complex64 form.
+
+    The 30 blocks of one step receive the same ``freqs_cis``; the conversion is
+    cached on (pointer, shape, version) so it runs once per step.
+    """
+    key = (freqs_cis.data_ptr(), tuple(freqs_cis.shape), freqs_cis._version, freqs_cis.dtype, batch)
+    hit = _TABLE_CACHE.get("k")
+    if hit == key:
+        return _TABLE_CACHE["v"]
+    if freqs_cis.is_complex():
+        fc = freqs_cis
+    else:
+        fc = _convert_rope_matrix_to_complex(freqs_cis)
+    val = rope_tables(fc, batch)
+    _TABLE_CACHE["k"] = key
+    _TABLE_CACHE["v"] = val
+    return val
+
+
+def _attention_bshd(xq: torch.Tensor, xk: torch.Tensor, xv: torch.Tensor,
+                    x_mask: Optional[torch.Tensor]) -> torch.Tensor:
+    """SDPA on [B,S,H,d] views -> [B,S,H*d] (stand-in for comfy's optimized_attention_masked,
+    patching_comfyui.py:197-205, which resolves to torch SDPA by default)."""
+    B, S, H, d = xq.shape
+    mask = None
+    if x_mask is not None:
+        mask = x_mask
+        if mask.dim() == 2:
+            mask = mask[:, None, None, :]
+        elif mask.dim() == 3:
+            mask = mask[:, None]
+    o = F.scaled_dot_product_attention(xq.transpose(1, 2), xk.transpose(1, 2), xv.transpose(1, 2),
+                                       attn_mask=mask)
+    return o.transpose(1, 2).reshape(B, S, H * d)
+
+
+def _make_fused_attention_forward(attn: nn.Module):
+    """JointAttention.forward with fused QK-norm + RoPE (patching_comfyui.py:137-209).
+
+    Q and K are normalised and rotated in place inside the fresh QKV output.
+    """
+    n_heads = attn.n_local_heads
+    n_kv = attn.n_local_kv_heads
+    head_dim = attn.head_dim
+    n_rep = n_heads // n_kv
+    split_sizes = [n_heads * head_dim, n_kv * head_dim, n_kv * head_dim]
+    qn, kn = attn.q_norm, attn.k_norm
+    q_eps, k_eps = _eps(qn), _eps(kn)
+
+    def _forward(self, x: torch.Tensor, x_mask: torch.Tensor, freqs_cis: torch.Tensor,
+                 transformer_options: dict = {}) -> torch.Tensor:
+        bsz, seqlen, _ = x.shape
+        qkv = self.qkv(x)
+        xq, xk, xv = torch.split(qkv, split_sizes, dim=-1)
+        xq = xq.view(bsz, seqlen, n_heads, head_dim)
+        xk = xk.view(bsz, seqlen, n_kv, head_dim)
+        xv = xv.view(bsz, seqlen, n_kv, head_dim)
+        cos, sin, cs_b = _cos_sin(freqs_cis, bsz)
+        qknorm_rope_into(xq, xq, qn.weight.detach().float().contiguous(), cos, sin, cs_b, q_eps)
+        qknorm_rope_into(xk, xk, kn.weight.detach().float().contiguous(), cos, sin, cs_b, k_eps)
+        if n_rep > 1:
+            xk = xk.unsqueeze(3).repeat(1, 1, 1, n_rep, 1).flatten(2, 3)
+            xv = xv.unsqueeze(3).repeat(1, 1, 1, n_rep, 1).flatten(2, 3)
+        return self.out(_attention_bshd(xq, xk, xv, x_mask))
+
+    return types.MethodType(_forward, attn)
+
+
+def _make_plain_rope_attention_forward(attn: nn.Module):
+    """RoPE-only variant used when fused QK-norm is off (patching_comfyui.py:212-272)."""
+    n_heads = attn.n_local_heads
+    n_kv = attn.n_local_kv_heads
+    head_dim = attn.head_dim
+    n_rep = n_heads // n_kv
+    split_sizes = [n_heads * head_dim, n_kv * head_dim, n_kv * head_dim]
+
+    def _forward(self, x, x_mask, freqs_cis, transformer_options={}):
+        bsz, seqlen, _ = x.shape
+        xq, xk, xv = torch.split(self.qkv(x), split_sizes, dim=-1)
+        xq = self.q_norm(xq.reshape(bsz, seqlen, n_heads, head_dim))
+        xk = self.k_norm(xk.reshape(bsz, seqlen, n_kv, head_dim))
+        xv = xv.view(bsz, seqlen, n_kv, head_dim)
+        cos, sin, cs_b = _cos_sin(freqs_cis, bsz)
+        xq = xq.contiguous()
+        xk = xk.contiguous()
+        qknorm_rope_into(xq, xq, None, cos, sin, cs_b, 0.0)
+        qknorm_rope_into(xk, xk, None, cos, sin, cs_b, 0.0)
+        if n_rep > 1:
+            xk = xk.unsqueeze(3).repeat(1, 1, 1, n_rep, 1).flatten(2, 3)
+            xv = xv.unsqueeze(3).repeat(1, 1, 1, n_rep, 1).flatten(2, 3)
+        return self.out(_attention_bshd(xq, xk, xv, x_mask))
+
+    return types.MethodType(_forward, attn)
+
+
+def _patch_attention_comfyui(model: nn.Module, stats: dict, fused: bool = True) -> None:
+    for module in model.modules():
+        if type(module).__name__ != "JointAttention" or not hasattr(module, "qkv"):
+            continue
+        if not hasattr(module, "q_norm") or not hasattr(module.q_norm, "weight"):
+            continue
+        if not hasattr(module, "_original_forward"):
+            module._original_forward = module.forward
+        if fused:
+            module.forward = _make_fused_attention_forward(module)
+            stats["fused_qknorm_rope"] += 1
+        else:
+            module.forward = _make_plain_rope_attention_forward(module)
+            stats["rope_3d"] += 1
+
+
+# ---------------------------------------------------------------------------
+# fused block executor
+# ---------------------------------------------------------------------------
+
+def _lin_ok(lin: nn.Module) -> bool:
+    return (getattr(lin, "_int8_quantized", False) and getattr(lin, "_int8_use_hadamard", False)
+            and getattr(lin, "bias", None) is None and hasattr(lin, "_w_int8") and lin._w_int8.is_cuda)
+
+
+def _f32(w: torch.Tensor) -> torch.Tensor:
+    return w.detach().to(torch.float32).contiguous()
+
+
+def _block_cache(block: nn.Module):
+    """Per-block tensors of the fused path, or None when the block does not qualify.
+
+    w1/w3 int8 weights are concatenated once into one [2F, D] operand and the
+    modules' buffers are re-pointed at views of it (no extra memory).
+    """
+    attn, ff = block.attention, block.feed_forward
+    lins = (attn.qkv, attn.out, ff.w1, ff.w2, ff.w3)
+    if not all(_lin_ok(l) for l in lins):
+        return None
+    if attn.head_dim != 128 or attn.n_local_heads != attn.n_local_kv_heads:
+        return None
+    norms = (block.attention_norm1, block.attention_norm2, block.ffn_norm1, block.ffn_norm2,
+             attn.q_norm, attn.k_norm)
+    if not all(getattr(n, "weight", None) is not None for n in norms):
+        return None
+    key = tuple((n.weight.data_ptr(), n.weight._version) for n in norms) + tuple(
+        (l._w_int8.data_ptr(), l._w_scale.data_ptr()) for l in lins)
+    c = block.__dict__.get("_zib_cache")
+    if c is not None and c["key"] == key:
+        return c
+    w1, w3 = ff.w1, ff.w3
+    F_ = w1._w_int8.shape[0]
+    if w3._w_int8.data_ptr() == w1._w_int8.data_ptr() + w1._w_int8.numel() and \
+            w3._w_scale.data_ptr() == w1._w_scale.data_ptr() + 2 * F_:
+        w13 = torch.as_strided(w1._w_int8, (2 * F_, w1._w_int8.shape[1]), w1._w_int8.stride())
+        s13 = torch.as_strided(w1._w_scale, (2 * F_,), (1,))
+    else:
+        w13 = torch.cat([w1._w_int8, w3._w_int8], 0)
+        s13 = torch.cat([w1._w_scale, w3._w_scale], 0)
+        w1._buffers["_w_int8"], w3._buffers["_w_int8"] = w13[:F_], w13[F_:]
+        w1._buffers["_w_scale"], w3._buffers["_w_scale"] = s13[:F_], s13[F_:]
+    c = {
+        "an1": _f32(block.attention_norm1.weight), "an2": _f32(block.attention_norm2.weight),
+        "fn1": _f32(block.ffn_norm1.weight), "fn2": _f32(block.ffn_norm2.weight),
+        "qn": _f32(attn.q_norm.weight), "kn": _f32(attn.k_norm.weight),
+        "eps_an1": _eps(block.attention_norm1), "eps_an2": _eps(block.attention_norm2),
+        "eps_fn1": _eps(block.ffn_norm1), "eps_fn2": _eps(block.ffn_norm2),
+        "eps_q": _eps(attn.q_norm), "eps_k": _eps(attn.k_norm),
+        "w13": w13, "s13": s13, "F": F_,
+    }
+    c["key"] = tuple((n.weight.data_ptr(), n.weight._version) for n in norms) + tuple(
+        (l._w_int8.data_ptr(), l._w_scale.data_ptr()) for l in lins)
+    block.__dict__["_zib_cache"] = c
+    return c
+
+
+# When a list, every fused-path GEMM appends (start_event, end_event, 2*M*N*K)
+# recorded on its launch stream (used by the benchmark's roofline figures).
+GEMM_EVENTS: list | None = None
+
+
+def _gemm(q8, sx, lin_w, lin_s, y, M, N, K, stream):
+    ev = GEMM_EVENTS
+    if ev is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    _lib.call("zib_gemm_w8a8", q8.data_ptr(), K, lin_w.data_ptr(), lin_w.stride(0), sx.data_ptr(),
+              lin_s.data_ptr(), None, y.data_ptr(), y.stride(0), M, N, K, stream)
+    if ev is not None:
+        e1.record()
+        ev.append((e0, e1, 2 * M * N * K))
+
+
+def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freqs_cis: torch.Tensor,
+                        adaln_input: torch.Tensor) -> torch.Tensor:
+    """One S3-DiT block on the fused kernels; arithmetic of patching_comfyui.py:340-415."""
+    B, S, D = x.shape
+    M = B * S
+    dev = x.device
+    _lib.require_device(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"fused block computes in bfloat16; got {x.dtype}")
+    x = x.contiguous()
+    stream = _lib.stream_of(x)
+    bf, i8 = torch.bfloat16, torch.int8
+    attn, ff = block.attention, block.feed_forward
+    H = attn.n_local_heads
+    hd = H * 128
+    F_ = c["F"]
+
+    # adaLN: raw [B, 4D]; gates tanh'd once (patching_comfyui.py:368-372)
+    raw = block.adaLN_modulation(adaln_input).reshape(B, 4 * D).contiguous()
+    gates = torch.empty(B, 2, D, dtype=bf, device=dev)
+    _lib.call("zib_adaln_gates", raw.data_ptr(), 4 * D, gates.data_ptr(), B, D, stream)
+    esz = 2  # bf16 bytes
+
+    # attention_norm1 -> *(1+scale_msa) -> rotate -> quantise            (:378)
+    q8 = torch.empty(M, D, dtype=i8, device=dev)
+    sx = torch.empty(M, dtype=bf, device=dev)
+    _lib.call("zib_rmsnorm_mod_quant", x.data_ptr(), D, c["an1"].data_ptr(), raw.data_ptr(), None, 4 * D, S,
+              q8.data_ptr(), D, sx.data_ptr(), M, D, float(c["eps_an1"]), 1, stream)
+    # QKV projection (tcgen05 GEMM)                                       (:180)
+    nqkv = attn.qkv._w_int8.shape[0]
+    qkv = torch.empty(M, nqkv, dtype=bf, device=dev)
+    _gemm(q8, sx, attn.qkv._w_int8, attn.qkv._w_scale, qkv, M, nqkv, D, stream)
+    qkv5 = qkv.view(B, S, 3, H, 128)
+    xq, xk, xv = qkv5[:, :, 0], qkv5[:, :, 1], qkv5[:, :, 2]
+    cos, sin, cs_b = _cos_sin(freqs_cis, B)
+    qknorm_rope_into(xq, xq, c["qn"], cos, sin, cs_b, c["eps_q"])          # :189
+    qknorm_rope_into(xk, xk, c["kn"], cos, sin, cs_b, c["eps_k"])          # :190
+    o = _attention_bshd(xq, xk, xv, x_mask).reshape(M, hd)                  # :197-205
+    # out projection: rotate + quantise + GEMM                            (:207)
+    if o.stride(-1) != 1 or o.stride(0) % 8 != 0:
+        o = o.contiguous()
+    q8o = torch.empty(M, hd, dtype=i8, device=dev)
+    sxo = torch.empty(M, dtype=bf, device=dev)
+    _lib.call("zib_act_quant", o.data_ptr(), o.stride(0), q8o.data_ptr(), hd, sxo.data_ptr(), None, M, hd, 1,
+              stream)
+    attn_out = torch.empty(M, D, dtype=bf, device=dev)
+    _gemm(q8o, sxo, attn.out._w_int8, attn.out._w_scale, attn_out, M, D, hd, stream)
+    # x + g_msa * norm2(attn_out); then ffn_norm1 * (1+scale_mlp) -> quantise   (:386-401)
+    x1 = torch.empty(M, D, dtype=bf, device=dev)
+    q8f = torch.empty(M, D, dtype=i8, device=dev)
+    sxf = torch.empty(M, dtype=bf, device=dev)
+    _lib.call("zib_norm_gate_residual_mod_quant", attn_out.data_ptr(), D, x.data_ptr(), D, gates.data_ptr(),
+              2 * D, S, c["an2"].data_ptr(), x1.data_ptr(), D, c["fn1"].data_ptr(),
+              raw.data_ptr() + 2 * D * esz, None, 4 * D, q8f.data_ptr(), D, sxf.data_ptr(), M, D,
+              float(c["eps_an2"]), float(c["eps_fn1"]), 1, stream)
+    # w1 || w3 in one GEMM, then SwiGLU -> rotate -> quantise, then w2
+    h = torch.empty(M, 2 * F_, dtype=bf, device=dev)
+    _gemm(q8f, sxf, c["w13"], c["s13"], h, M, 2 * F_, D, stream)
+    q8h = torch.empty(M, F_, dtype=i8, device=dev)
+    sxh = torch.empty(M, dtype=bf, device=dev)
+    _lib.call("zib_swiglu_quant", h.data_ptr(), 2 * F_, h.data_ptr() + F_ * esz, 2 * F_, q8h.data_ptr(), F_,
+              sxh.data_ptr(), M, F_, 1, stream)
+    ffn_out = torch.empty(M, D, dtype=bf, device=dev)
+    _gemm(q8h, sxh, ff.w2._w_int8, ff.w2._w_scale, ffn_out, M, D, F_, stream)
+    # x1 + g_mlp * ffn_norm2(ffn_out)                                     (:404-411)
+    x2 = torch.empty(M, D, dtype=bf, device=dev)
+    _lib.call("zib_norm_gate_residual", ffn_out.data_ptr(), D, x1.data_ptr(), D, gates.data_ptr() + D * esz,
+              2 * D, S, c["fn2"].data_ptr(), x2.data_ptr(), D, M, D, float(c["eps_fn2"]), stream)
+    return x2.view(B, S, D)
+
+
+def _modulated_norm(norm: nn.Module, x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """norm(x) * (1 + scale) with one kernel when the norm is a TritonRMSNorm."""
+    if isinstance(norm, TritonRMSNorm) and x.dtype == torch.bfloat16 and scale.dtype == torch.bfloat16:
+        B, S, D = x.shape
+        x2 = x.contiguous()
+        sc = scale.reshape(B, D).contiguous()
+        y = torch.empty_like(x2)
+        _lib.call("zib_rmsnorm_mod", x2.data_ptr(), D, _f32(norm.weight).data_ptr(), sc.data_ptr(), None, D, S,
+                  y.data_ptr(), D, B * S, D, float(_eps(norm)), _lib.stream_of(x))
+        return y
+    return norm(x) * (1 + scale.unsqueeze(1))
+
+
+def _make_block_forward(block: nn.Module, dim: int, use_adaln: bool, use_fused_nr: bool):
+    """Patched JointTransformerBlock.forward (patching_comfyui.py:315-417)."""
+    from ..kernels.adaln_modulation import triton_adaln_modulation
+    from ..kernels.fused_norm_residual import triton_fused_norm_gate_residual
+
+    an2_w = block.attention_norm2.weight
+    an2_eps = _eps(block.attention_norm2)
+    fn2_w = block.ffn_norm2.weight
+    fn2_eps = _eps(block.ffn_norm2)
+
+    def _forward(self, x: torch.Tensor, x_mask: torch.Tensor, freqs_cis: torch.Tensor,
+                 adaln_input: Optional[torch.Tensor] = None, timestep_zero_index=None,
+                 transformer_options={}) -> torch.Tensor:
+        if timestep_zero_index is not None:  # omni mode (:350-358)
+            return self._original_forward(x, x_mask, freqs_cis, adaln_input, timestep_zero_index,
+                                          transformer_options)
+        assert adaln_input is not None
+        if ENABLE_FUSED_BLOCK and not use_adaln and use_fused_nr and x.is_cuda:
+            c = _block_cache(self)
+            if c is not None:
+                return fused_block_forward(self, c, x, x_mask, freqs_cis, adaln_input)
+
+        if use_adaln:
+            raw = self.adaLN_modulation(adaln_input)
+            s_msa, g_msa, s_mlp, g_mlp = triton_adaln_modulation(raw, dim)
+            attn_in = self.attention_norm1(x) * s_msa.unsqueeze(1)
+        else:
+            s_msa, g_msa, s_mlp, g_mlp = self.adaLN_modulation(adaln_input).chunk(4, dim=1)
+            g_msa = g_msa.tanh()
+            g_mlp = g_mlp.tanh()
+            attn_in = _modulated_norm(self.attention_norm1, x, s_msa)
+        attn_out = self.attention(attn_in, x_mask, freqs_cis, transformer_options=transformer_options)
+        if use_fused_nr:
+            x = triton_fused_norm_gate_residual(attn_out, x, g_msa.unsqueeze(1), an2_w, an2_eps)
+        else:
+            x = x + g_msa.unsqueeze(1) * self.attention_norm2(attn_out)
+        if use_adaln:
+            ffn_in = self.ffn_norm1(x) * s_mlp.unsqueeze(1)
+        else:
+            ffn_in = _modulated_norm(self.ffn_norm1, x, s_mlp)
+        ffn_out = self.feed_forward(ffn_in)
+        if use_fused_nr:
+            x = triton_fused_norm_gate_residual(ffn_out, x, g_mlp.unsqueeze(1), fn2_w, fn2_eps)
+        else:
+            x = x + g_mlp.unsqueeze(1) * self.ffn_norm2(ffn_out)
+        return x
+
+    return types.MethodType(_forward, block)
+
+
+def _patch_block_forward_comfyui(model: nn.Module, stats: dict, enable_adaln: bool = True,
+                                 enable_fused_norm_residual: bool = True) -> None:
+    for module in model.modules():
+        if type(module).__name__ != "JointTransformerBlock":
+            continue
+        if not getattr(module, "modulation", False) or not hasattr(module, "dim"):
+            continue
+        if not hasattr(module, "_original_forward"):
+            module._original_forward = module.forward
+        module.forward = _make_block_forward(module, module.dim, enable_adaln, enable_fused_norm_residual)
+        if enable_adaln:
+            stats["adaln_modulation"] += 1
+        if enable_fused_norm_residual:
+            stats["fused_norm_gate_residual"] += 1
+
+
+def apply_triton_kernels_comfyui(model: nn.Module, enable_fused_norm: bool = True, enable_swiglu: bool = True,
+                                 enable_fused_qknorm_rope: bool = True, enable_fused_adaln: bool = True,
+                                 enable_fused_norm_residual: bool = True) -> dict[str, int]:
+    """Apply the kernel replacements (patching_comfyui.py:457-517); returns replacement counts."""
+    stats: dict[str, int] = {
+        "rms_norm": 0,
+        "swiglu": 0,
+        "rope_3d": 0,
+        "fused_qknorm_rope": 0,
+        "adaln_modulation": 0,
+        "fused_norm_gate_residual": 0,
+    }
+    if enable_fused_norm:
+        _replace_all_rms_norm_comfyui(model, stats)
+    if enable_swiglu:
+        _patch_all_ffn_comfyui(model, stats)
+    _patch_attention_comfyui(model, stats, fused=enable_fused_qknorm_rope)
+    if enable_fused_adaln or enable_fused_norm_residual:
+        _patch_block_forward_comfyui(model, stats, enable_fused_adaln, enable_fused_norm_residual)
+    logger.info("ComfyUI sm_100a patching complete: %s", stats)
+    return stats

@@ -1,0 +1,276 @@
+"""W8A8 (+ block Hadamard) INT8 linear layers on sm_100a.
+
+Replaces ``src/zimage_triton/quantization/int8_linear.py`` of the reference
+with the same module-replacement surface, so ComfyUI glue written against it
+keeps working:
+
+* per quantised ``nn.Linear``: buffers ``_w_int8`` (int8 [out, in], weight
+  pre-rotated by the block Hadamard when ``in % 128 == 0``) and ``_w_scale``
+  (per-output-channel scale in the weight dtype); attributes
+  ``_int8_quantized``, ``_int8_use_hadamard``, ``_int8_layer_name``,
+  ``_int8_sd_hook``; instance ``forward`` and ``_apply`` overrides; the bf16
+  ``weight`` moved to CPU (int8_linear.py:273-308);
+* the same layer-selection policy and stats keys (int8_linear.py:27-64,
+  :209-321) and the same restore path (int8_linear.py:324-384).
+
+The forward is two kernel launches: ``zib_act_quant`` (rotation + per-token
+absmax + int8, int8_linear.py:119-130) and ``zib_gemm_w8a8`` (tcgen05 int8
+GEMM with the dequant/bias epilogue fused, int8_linear.py:133-137).  Weight
+prep runs on the GPU (``zib_weight_prep``) even when the module sits on the
+CPU at patch time; the buffers are then placed on the weight's device.
+"""
+
+from __future__ import annotations
+
+import logging
+import re
+import types
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import _lib
+
+logger = logging.getLogger(__name__)
+
+_MIN_DIM = 1024
+_HADAMARD_GROUP_SIZE = 128  # Z-Image head_dim; 3840/128 = 30, 10240/128 = 80
+
+# Layers kept in the source dtype by the reference policy (int8_linear.py:30-38).
+_SENSITIVE_PATTERNS: list[str] = [
+    "cap_embedder",
+    "t_embedder",
+    "x_embedder",
+    "adaLN_modulation",
+    "context_refiner",
+    "noise_refiner",
+    "final_layer",
+]
+
+_FIRST_BLOCK_RE = re.compile(r"layers\.0\.")
+
+
+def _is_sensitive_layer(name: str, n_blocks: int) -> bool:
+    """int8_linear.py:44-56.  The last-two-blocks pattern is derived from this
+    model's block count on every call (the reference caches the first model's)."""
+    for pattern in _SENSITIVE_PATTERNS:
+        if pattern in name:
+            return True
+    if _FIRST_BLOCK_RE.search(name):
+        return True
+    if n_blocks > 2:
+        last = "|".join(str(i) for i in range(n_blocks - 2, n_blocks))
+        if re.search(rf"layers\.({last})\.", name):
+            return True
+    return False
+
+
+def _count_blocks(model: nn.Module) -> int:
+    return sum(1 for m in model.modules() if type(m).__name__ == "JointTransformerBlock")
+
+
+def _prep_device(weight: torch.Tensor) -> torch.device:
+    if weight.is_cuda:
+        return weight.device
+    if not torch.cuda.is_available():
+        raise RuntimeError("zimage_b200 INT8 weight prep needs an sm_100 CUDA device; none is visible")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def quantize_weight(weight: torch.Tensor, hadamard: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Rotate (optional) + per-channel int8 quantisation on the GPU.
+
+    Returns (w_int8 [out, in] int8, w_scale [out] bf16) on the GPU; the same
+    arithmetic as rotate_weight + _quantize_weight_per_channel
+    (hadamard.py:47-75, int8_linear.py:67-73), rotation exact then rounded to fp32.
+    """
+    dev = _prep_device(weight)
+    w = weight.detach()
+    wb = w.to(device=dev, dtype=torch.bfloat16)
+    if w.dtype != torch.bfloat16 and not torch.equal(wb.float(), w.to(dev).float()):
+        raise ValueError(f"INT8 weight prep expects bf16-representable weights, got {w.dtype}")
+    wb = wb.contiguous()
+    N, K = wb.shape
+    _lib.require_device(wb)
+    wq = torch.empty(N, K, dtype=torch.int8, device=dev)
+    sw = torch.empty(N, dtype=torch.bfloat16, device=dev)
+    _lib.call("zib_weight_prep", wb.data_ptr(), K, wq.data_ptr(), K, sw.data_ptr(), None, None, 0, N, K,
+              1 if hadamard else 0, _lib.stream_of(wb))
+    return wq, sw
+
+
+# --- forward builders --------------------------------------------------------
+
+def w8a8_forward_2d(x2: torch.Tensor, w_int8: torch.Tensor, w_scale: torch.Tensor,
+                    bias: torch.Tensor | None, hadamard: bool) -> torch.Tensor:
+    """[M, K] bf16 -> [M, N] bf16 through act_quant + tcgen05 GEMM."""
+    _lib.require_device(x2)
+    if x2.dtype != torch.bfloat16:
+        raise ValueError(f"W8A8 forward computes in bfloat16; got {x2.dtype}")
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+        x2 = x2.contiguous()
+    M, K = x2.shape
+    N = w_int8.shape[0]
+    stream = _lib.stream_of(x2)
+    q = torch.empty(M, K, dtype=torch.int8, device=x2.device)
+    sx = torch.empty(M, dtype=torch.bfloat16, device=x2.device)
+    _lib.call("zib_act_quant", x2.data_ptr(), x2.stride(0), q.data_ptr(), K, sx.data_ptr(), None, M, K,
+              1 if hadamard else 0, stream)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=x2.device)
+    fused_bias = bias if (bias is not None and bias.dtype == torch.bfloat16 and bias.is_cuda) else None
+    _lib.call("zib_gemm_w8a8", q.data_ptr(), K, w_int8.data_ptr(), w_int8.stride(0), sx.data_ptr(),
+              w_scale.data_ptr(), _lib.ptr(fused_bias), y.data_ptr(), N, M, N, K, stream)
+    if bias is not None and fused_bias is None:
+        y = y + bias
+    return y
+
+
+def _make_w8a8_forward(module: nn.Linear, hadamard: bool):
+    """W8A8 forward (int8_linear.py:79-99 / :102-140), kernels on sm_100a."""
+    bias = module.bias
+    out_f = module.out_features
+
+    def _forward(self, x: torch.Tensor) -> torch.Tensor:
+        orig_shape = x.shape
+        y = w8a8_forward_2d(x.reshape(-1, orig_shape[-1]), self._w_int8, self._w_scale, bias, hadamard)
+        return y.view(*orig_shape[:-1], out_f)
+
+    return types.MethodType(_forward, module)
+
+
+def _make_w8a16_forward(module: nn.Linear):
+    """Weight-only INT8 (int8_linear.py:143-151); not selected by the node, plain torch ops."""
+    bias = module.bias
+
+    def _forward(self, x: torch.Tensor) -> torch.Tensor:
+        w_deq = self._w_int8.to(x.dtype) * self._w_scale.unsqueeze(1).to(x.dtype)
+        return F.linear(x, w_deq, bias)
+
+    return types.MethodType(_forward, module)
+
+
+def _int8_state_dict_hook(module, state_dict, prefix, local_metadata) -> None:
+    """Hide the CPU weight from state_dict (int8_linear.py:154-170)."""
+    key = prefix + "weight"
+    if key in state_dict:
+        del state_dict[key]
+
+
+def _int8_apply(self, fn, recurse=True):
+    """Custom _apply (int8_linear.py:173-200): weight stays on CPU; INT8 buffers
+    may move to the GPU but never back."""
+    if recurse:
+        for module in self.children():
+            module._apply(fn)
+    for key, param in self._parameters.items():
+        if param is None or key == "weight":
+            continue
+        self.register_parameter(key, torch.nn.Parameter(fn(param), requires_grad=False))
+    for key, buf in self._buffers.items():
+        if buf is not None:
+            if key in ("_w_int8", "_w_scale") and buf.device.type == "cuda":
+                continue
+            self._buffers[key] = fn(buf)
+    return self
+
+
+_VALID_MODES = ("w8a8", "w8a8_hadamard", "w8a16")
+
+
+def select_layers(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
+                  skip_sensitive: bool = True):
+    """Layer-selection policy of apply_int8_quantization (int8_linear.py:242-271), no side effects.
+
+    Returns ([(name, module, use_hadamard), ...], stats).
+    """
+    if mode not in _VALID_MODES:
+        raise ValueError(f"Unknown mode: {mode!r}. Use one of {_VALID_MODES}")
+    use_hadamard = mode == "w8a8_hadamard"
+    n_blocks = _count_blocks(model)
+    stats = {"quantized": 0, "skipped": 0, "sensitive": 0, "had_skipped": 0}
+    plan = []
+    for name, module in list(model.named_modules()):
+        if not isinstance(module, nn.Linear):
+            continue
+        in_f, out_f = module.in_features, module.out_features
+        if in_f < min_dim or out_f < min_dim:
+            stats["skipped"] += 1
+            continue
+        if skip_sensitive and _is_sensitive_layer(name, n_blocks):
+            stats["sensitive"] += 1
+            continue
+        if mode != "w8a16" and in_f % 16 != 0:
+            # the tcgen05 GEMM streams K in 16-byte TMA rows
+            stats["skipped"] += 1
+            logger.debug("INT8 skip %s: in=%d not a multiple of 16", name, in_f)
+            continue
+        had = use_hadamard and in_f % _HADAMARD_GROUP_SIZE == 0
+        if use_hadamard and not had:
+            stats["had_skipped"] += 1
+            logger.debug("Hadamard skip %s: in=%d not divisible by %d", name, in_f, _HADAMARD_GROUP_SIZE)
+        plan.append((name, module, had))
+        stats["quantized"] += 1
+    return plan, stats
+
+
+def apply_int8_quantization(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
+                            skip_sensitive: bool = True) -> dict[str, int]:
+    """Quantise qualifying nn.Linear layers in place (int8_linear.py:209-321).
+
+    ``skip_sensitive=False`` quantises every linear with in/out >= ``min_dim``
+    (the all-linears policy); the default reproduces the reference policy.
+    Returns {"quantized", "skipped", "sensitive", "had_skipped"}.
+    """
+    plan, stats = select_layers(model, min_dim, mode, skip_sensitive)
+    for name, module, had in plan:
+        in_f, out_f = module.in_features, module.out_features
+        w_int8, w_scale = quantize_weight(module.weight.data, had)
+        target = module.weight.device
+        module.register_buffer("_w_int8", w_int8.to(target))
+        module.register_buffer("_w_scale", w_scale.to(device=target, dtype=module.weight.dtype))
+        module.weight.data = module.weight.data.to(device="cpu")
+
+        if mode == "w8a16":
+            fwd = _make_w8a16_forward(module)
+        else:
+            fwd = _make_w8a8_forward(module, had)
+        module.forward = fwd
+        module._int8_quantized = True
+        module._int8_use_hadamard = had
+        module._int8_layer_name = name
+        module._apply = types.MethodType(_int8_apply, module)
+        module._int8_sd_hook = module._register_state_dict_hook(_int8_state_dict_hook)
+        logger.debug("INT8 [%s] %s (%d->%d)", mode, name, in_f, out_f)
+
+    logger.info("INT8 [%s]: %d quantized, %d skipped, %d sensitive, %d had_skip", mode,
+                stats["quantized"], stats["skipped"], stats["sensitive"], stats["had_skipped"])
+    return stats
+
+
+def restore_int8_quantization(model: nn.Module) -> int:
+    """Undo apply_int8_quantization (int8_linear.py:324-384); returns the module count."""
+    restored = 0
+    for _name, module in list(model.named_modules()):
+        if not getattr(module, "_int8_quantized", False) or not isinstance(module, nn.Linear):
+            continue
+        target = module._w_int8.device if hasattr(module, "_w_int8") else torch.device("cpu")
+        module.weight = nn.Parameter(module.weight.data.to(device=target), requires_grad=False)
+        for buf in ("_w_int8", "_w_scale"):
+            if buf in module._buffers:
+                del module._buffers[buf]
+        hook = getattr(module, "_int8_sd_hook", None)
+        if hook is not None:
+            hook.remove()
+        for attr in ("forward", "_apply", "_int8_quantized", "_int8_use_hadamard", "_int8_layer_name",
+                     "_int8_sd_hook"):
+            module.__dict__.pop(attr, None)
+        restored += 1
+    for attr in ("_int8_quantized", "_int8_stats"):
+        if hasattr(model, attr):
+            delattr(model, attr)
+    # fused block caches hold views of the removed buffers
+    for m in model.modules():
+        m.__dict__.pop("_zib_cache", None)
+    logger.info("INT8 restore: %d modules restored.", restored)
+    return restored

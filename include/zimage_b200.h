@@ -1,0 +1,183 @@
+/*
+ * zimage_b200.h - C ABI of libzimage_b200.so, the sm_100a (B200) kernels of
+ * the Z-Image S3-DiT W8A8 forward path.
+ *
+ * Conventions for every entry point:
+ *   - Plain device pointers, element counts and row strides (in ELEMENTS);
+ *     no framework types.  `stream` is a cudaStream_t passed as void*.
+ *   - The caller allocates every output.  Kernels never allocate, free or
+ *     synchronise; work is enqueued on `stream`.
+ *   - Return 0 (ZIB_OK) or a zib_status code; zib_last_error() gives a
+ *     thread-local message.  Shape/dtype/alignment problems are detected on
+ *     the host before any launch (the Python layer maps them to ValueError /
+ *     RuntimeError like the reference: kernels/swiglu.py:82-86,
+ *     kernels/utils.py:33-37).
+ *   - bf16 tensors are raw uint16 bf16 bit patterns; "f32" tensors are float.
+ *
+ * Each declaration names the reference interface it replaces (file:line
+ * within newgrit1004/ComfyUI-ZImage-Triton).
+ */
+#ifndef ZIMAGE_B200_H_
+#define ZIMAGE_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ZIB_API __attribute__((visibility("default")))
+#else
+#define ZIB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum zib_status {
+  ZIB_OK = 0,
+  ZIB_ERR_INVALID_ARG = 1, /* bad shape / null pointer       -> ValueError   */
+  ZIB_ERR_ALIGNMENT = 2,   /* pointer or stride misaligned   -> ValueError   */
+  ZIB_ERR_UNSUPPORTED = 3, /* no sm_100 device / feature     -> RuntimeError */
+  ZIB_ERR_LAUNCH = 4,      /* CUDA launch/driver error       -> RuntimeError */
+  ZIB_ERR_TOO_LARGE = 5,   /* row longer than supported      -> RuntimeError */
+  ZIB_ERR_TIMEOUT = 6      /* a bounded device wait expired  -> RuntimeError */
+} zib_status;
+
+/* Library version (major*10000 + minor*100 + patch). */
+ZIB_API int zib_version(void);
+/* Human-readable text of a zib_status. */
+ZIB_API const char* zib_status_string(int status);
+/* Message of the last failing call on this host thread ("" if none). */
+ZIB_API const char* zib_last_error(void);
+/* 0 if device `dev` is an sm_100 part this library can run on, else a zib_status. */
+ZIB_API int zib_device_check(int dev);
+/* Reads and clears the device-side error word of the current device (set by a
+ * kernel whose bounded wait expired: ZIB_ERR_TIMEOUT).  Synchronising; not for
+ * the hot path.  Returns 0 when no kernel reported an error. */
+ZIB_API int zib_device_error_read_clear(void);
+
+/* ---------------------------------------------------------------------------
+ * W8A8 + Hadamard linear (replaces _make_w8a8_hadamard_forward._forward,
+ * src/zimage_triton/quantization/int8_linear.py:114-138)
+ * ------------------------------------------------------------------------- */
+
+/* Activation rotation + per-token int8 quantisation
+ * (int8_linear.py:119-130; hadamard.py:78-107).
+ * x: bf16 [M,K] row stride ldx; q: int8 [M,K] row stride ldq; sx: bf16 [M].
+ * hadamard!=0 applies the block-128 Walsh-Hadamard rotation (K % 128 == 0);
+ * hadamard==0 is the plain W8A8 quantisation (int8_linear.py:87-88).
+ * x_rot (nullable): bf16 [M,K] stride ldq, the rotated activations (debug). */
+ZIB_API int zib_act_quant(const void* x, int64_t ldx, void* q, int64_t ldq, void* sx,
+                  void* x_rot, int64_t M, int64_t K, int hadamard, void* stream);
+
+/* int8 GEMM + dequant epilogue on tcgen05 tensor cores
+ * (torch._int_mm + epilogue, int8_linear.py:133-137):
+ *   y[m,n] = bf16( bf16(acc) * bf16(sx[m]*sw[n]) ) (+ bias[n], bf16 add)
+ *   acc[m,n] = sum_k q[m,k] * wq[n,k]   (int32, exact)
+ * q: int8 [M,K] stride ldq; wq: int8 [N,K] stride ldw (nn.Linear layout);
+ * sx: bf16 [M]; sw: bf16 [N]; bias: bf16 [N] or NULL; y: bf16 [M,N] stride ldy.
+ * Requires K % 16 == 0, ldq/ldw % 16 == 0, ldy % 8 == 0, 16-byte aligned bases. */
+ZIB_API int zib_gemm_w8a8(const void* q, int64_t ldq, const void* wq, int64_t ldw,
+                  const void* sx, const void* sw, const void* bias,
+                  void* y, int64_t ldy, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Same GEMM writing the raw int32 accumulators (debug / bit-exactness checks of
+ * torch._int_mm, int8_linear.py:133).  acc: int32 [M,N] stride ldacc (% 4 == 0). */
+ZIB_API int zib_gemm_w8a8_acc_i32(const void* q, int64_t ldq, const void* wq, int64_t ldw,
+                          void* acc, int64_t ldacc, int64_t M, int64_t N, int64_t K,
+                          void* stream);
+
+/* Offline weight prep: rotate_weight (hadamard.py:47-75) in exact arithmetic
+ * rounded to fp32, then _quantize_weight_per_channel (int8_linear.py:67-73).
+ * w: bf16 [N,K] stride ldw -> wq int8 [N,K] stride ldq, sw bf16 [N]
+ * (the `_w_scale` buffer), sw_f32 fp32 [N] (nullable), w_rot fp32 [N,K]
+ * stride ld_rot (nullable: the rotated weight itself).  hadamard as above. */
+ZIB_API int zib_weight_prep(const void* w, int64_t ldw, void* wq, int64_t ldq, void* sw,
+                    void* sw_f32, float* w_rot, int64_t ld_rot, int64_t N, int64_t K,
+                    int hadamard, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Bandwidth-bound row kernels (replace the Triton kernels)
+ * ------------------------------------------------------------------------- */
+
+/* RMSNorm: y = bf16(bf16(x*rstd)*w) (kernels/rms_norm.py:18-59, :62-102).
+ * x, y: bf16 [rows, n] strides ldx/ldy; w: fp32 [n]. */
+ZIB_API int zib_rms_norm(const void* x, int64_t ldx, const float* w, void* y, int64_t ldy,
+                 int64_t rows, int64_t n, float eps, void* stream);
+
+/* RMSNorm + adaLN modulation, bf16 output (rms_norm.py:47-57 then
+ * patching_comfyui.py:378/:401): y = bf16( rmsnorm(x) * bf16(1 + scale[b]) )
+ * (+ shift[b] if shift != NULL).  scale/shift: bf16 rows of length n with row
+ * stride ld_mod, batch index b = row / rows_per_batch. */
+ZIB_API int zib_rmsnorm_mod(const void* x, int64_t ldx, const float* w, const void* scale,
+                    const void* shift, int64_t ld_mod, int64_t rows_per_batch,
+                    void* y, int64_t ldy, int64_t rows, int64_t n, float eps, void* stream);
+
+/* RMSNorm + adaLN modulation fused with the next W8A8 linear's activation
+ * rotation + quantisation (same math as zib_rmsnorm_mod followed by
+ * zib_act_quant).  q int8 [rows,n] stride ldq, sx bf16 [rows]. */
+ZIB_API int zib_rmsnorm_mod_quant(const void* x, int64_t ldx, const float* w, const void* scale,
+                          const void* shift, int64_t ld_mod, int64_t rows_per_batch,
+                          void* q, int64_t ldq, void* sx, int64_t rows, int64_t n,
+                          float eps, int hadamard, void* stream);
+
+/* Fused RMSNorm + gate + residual (kernels/fused_norm_residual.py:23-74, :77-126):
+ * y = bf16( r + bf16( gate[b] * bf16(bf16(x*rstd)*w) ) ); gate: bf16 rows
+ * (stride ld_gate) indexed by b = row / rows_per_batch (no expand copy). */
+ZIB_API int zib_norm_gate_residual(const void* x, int64_t ldx, const void* r, int64_t ldr,
+                           const void* gate, int64_t ld_gate, int64_t rows_per_batch,
+                           const float* w, void* y, int64_t ldy, int64_t rows, int64_t n,
+                           float eps, void* stream);
+
+/* zib_norm_gate_residual fused with the following RMSNorm + modulation +
+ * W8A8 activation quantisation (patching_comfyui.py:386-401 then
+ * int8_linear.py:119-130): writes y (the new residual stream) and q/sx of
+ * bf16(rmsnorm(y; w2) * bf16(1 + scale[b])) (+ shift). */
+ZIB_API int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, const void* r, int64_t ldr,
+                                     const void* gate, int64_t ld_gate, int64_t rows_per_batch,
+                                     const float* w, void* y, int64_t ldy,
+                                     const float* w2, const void* scale, const void* shift,
+                                     int64_t ld_mod, void* q, int64_t ldq, void* sx,
+                                     int64_t rows, int64_t n, float eps, float eps2,
+                                     int hadamard, void* stream);
+
+/* SwiGLU: out = bf16( bf16(silu_fp32(gate)) * up ) (kernels/swiglu.py:20-59, :62-110).
+ * gate/up/out: bf16 [rows, n] with strides ldg/ldu/ldo. */
+ZIB_API int zib_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out,
+               int64_t ldo, int64_t rows, int64_t n, void* stream);
+
+/* SwiGLU fused with the down projection's activation rotation + quantisation
+ * (swiglu.py:51-58 then int8_linear.py:119-130). */
+ZIB_API int zib_swiglu_quant(const void* gate, int64_t ldg, const void* up, int64_t ldu,
+                     void* q, int64_t ldq, void* sx, int64_t rows, int64_t n,
+                     int hadamard, void* stream);
+
+/* Fused per-head RMSNorm + interleaved-pair RoPE
+ * (kernels/fused_qknorm_rope.py:38-151, :154-235), or RoPE alone when
+ * w == NULL (kernels/rope_3d.py:22-89, :92-163).
+ * x/out: bf16 [B,S,H,d] with element strides (sb, ss, sh), last dim contiguous
+ * (out may alias x); cos/sin: fp32 [Bf,S,d/2] contiguous per batch with batch
+ * stride cs_b (0 = shared across batch); w: fp32 [d] or NULL.  d == 128. */
+ZIB_API int zib_qknorm_rope(const void* x, int64_t x_sb, int64_t x_ss, int64_t x_sh,
+                    void* out, int64_t o_sb, int64_t o_ss, int64_t o_sh,
+                    const float* cos, const float* sin, int64_t cs_b,
+                    const float* w, int64_t B, int64_t S, int64_t H, int64_t d,
+                    float eps, void* stream);
+
+/* adaLN modulation, Triton variant (kernels/adaln_modulation.py:28-88, :91-155):
+ * raw bf16 [rows, 4*dim] stride ldr -> (1+scale_msa, tanh(gate_msa),
+ * 1+scale_mlp, tanh(gate_mlp)), each bf16 [rows, dim] contiguous. */
+ZIB_API int zib_adaln_modulation(const void* raw, int64_t ldr, void* scale_msa, void* gate_msa,
+                         void* scale_mlp, void* gate_mlp, int64_t rows, int64_t dim,
+                         void* stream);
+
+/* Gates of the eager default path (patching_comfyui.py:368-372): from raw bf16
+ * [rows, 4*dim], writes tanh(gate_msa) and tanh(gate_mlp) into gates
+ * bf16 [rows, 2, dim] contiguous. */
+ZIB_API int zib_adaln_gates(const void* raw, int64_t ldr, void* gates, int64_t rows, int64_t dim,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZIMAGE_B200_H_ */

@@ -1,0 +1,396 @@
+"""CPU restatement of every op on the Z-Image W8A8 hot path (TEST INFRASTRUCTURE ONLY).
+
+Only tests, ``__graft_entry__.smoke()`` and the CPU legs of ``bench.py`` use
+this module.  All tensors are CPU torch tensors.  Each function cites the
+reference file:line it restates (paths relative to the reference project).
+
+Rounding conventions (the reference's, made explicit):
+
+* torch elementwise ops on bf16 compute in fp32 and round once to bf16 (RNE).
+* Row reductions (sum of squares) are restated with an exactly-rounded fp32
+  sum (fp64 accumulation, then one rounding).  The reference's Triton
+  ``tl.sum`` uses an implementation-defined tree order, so no order is
+  canonical; the CUDA kernels use the same exactly-rounded convention.
+* ``rsqrt`` is restated as IEEE ``1 / sqrt(v)`` in fp32.  The reference's
+  libdevice ``rsqrt`` is an approximation; outputs are compared with
+  tolerances for that reason.
+* The Hadamard rotation of activations is restated as the correctly rounded
+  bf16 of the exact product ``h * sum(+-x)`` with ``h = bf16(1/sqrt(128))``.
+  The reference computes it as a bf16 matmul (``int8_linear.py:124-126``),
+  whose fp32 accumulation order is a BLAS detail; ``act_quant_had128_matmul``
+  restates that form so tests can measure the (tiny) difference.
+* Divisions by the Python scalar 127.0 are true divisions (torch CPU).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+GROUP = 128  # int8_linear.py:28 _HADAMARD_GROUP_SIZE
+
+# hadamard.py:40-41: torch.tensor(H_np, float32) / (size ** 0.5); entries are
+# +-1 divided by sqrt(128) in fp32.
+H_FP32 = float((torch.ones(1, dtype=torch.float32) / (GROUP ** 0.5)).item())
+# int8_linear.py:120-123 casts H to the activation dtype (bf16).
+H_BF16 = float(torch.tensor(H_FP32, dtype=torch.float32).to(torch.bfloat16).float().item())
+
+
+# ---------------------------------------------------------------------------
+# bit-level helpers
+# ---------------------------------------------------------------------------
+
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """RNE fp32 -> bf16 on raw bits (finite inputs)."""
+    b = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    b = (b + 0x7FFF + ((b >> 16) & 1)) >> 16
+    return b.astype(np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def round_f64_to_bf16(v: np.ndarray) -> torch.Tensor:
+    """Correctly rounded (single RNE) bf16 of an fp64 value.
+
+    Rounds to fp32 first; when the fp32 value sits exactly on a bf16
+    midpoint, the sign of the (exact) fp64 residual decides the direction.
+    A midpoint strictly between the exact value and its fp32 rounding cannot
+    exist, so this is a single correct rounding.
+    """
+    v = np.asarray(v, dtype=np.float64)
+    f = v.astype(np.float32)
+    err = v - f.astype(np.float64)
+    bits = f.view(np.uint32).astype(np.uint64)
+    tie = ((bits & 0xFFFF) == 0x8000) & (err != 0)
+    away = tie & (np.sign(err) == np.sign(f))
+    rne = (bits + 0x7FFF + ((bits >> 16) & 1)) >> 16
+    trunc = bits >> 16
+    out = np.where(tie, np.where(away, trunc + 1, trunc), rne).astype(np.uint16)
+    return torch.from_numpy(bf16_bits_to_f32(out).copy()).to(torch.bfloat16)
+
+
+def bf16(t: torch.Tensor) -> torch.Tensor:
+    return t.to(torch.bfloat16)
+
+
+# ---------------------------------------------------------------------------
+# Hadamard (hadamard.py)
+# ---------------------------------------------------------------------------
+
+def sylvester_signs(n: int) -> np.ndarray:
+    """Sylvester Hadamard sign matrix, H[i, j] = (-1)^popcount(i & j).
+
+    Same ordering as ``scipy.linalg.hadamard`` used by ``hadamard.py:40``.
+    """
+    if n & (n - 1):
+        raise ValueError(f"Hadamard size must be power of 2, got {n}")
+    i = np.arange(n)
+    pc = np.vectorize(lambda v: bin(v).count("1"))(i[:, None] & i[None, :])
+    return np.where(pc % 2 == 0, 1, -1).astype(np.int8)
+
+
+def fwht_f64(x: np.ndarray) -> np.ndarray:
+    """Exact (fp64) unnormalised Walsh-Hadamard transform over the last axis of 128."""
+    y = np.array(x, dtype=np.float64, copy=True)
+    n = y.shape[-1]
+    h = 1
+    while h < n:
+        y = y.reshape(*y.shape[:-1], n // (2 * h), 2, h)
+        a = y[..., 0, :].copy()
+        b = y[..., 1, :]
+        y = np.stack([a + b, a - b], axis=-2).reshape(*y.shape[:-3], n)
+        h *= 2
+    return y
+
+
+def rotate_activation_exact(x: torch.Tensor) -> torch.Tensor:
+    """x_rot = bf16( x[m, 128g:128g+128] @ H_bf16 ), exact sum, one rounding.
+
+    Restates ``int8_linear.py:119-126`` / ``hadamard.py:78-107``.
+    """
+    M, K = x.shape
+    if K % GROUP:
+        raise ValueError(f"features {K} not divisible by group_size {GROUP}")
+    s = fwht_f64(x.float().numpy().reshape(M, K // GROUP, GROUP)) * H_BF16
+    return round_f64_to_bf16(s.reshape(M, K))
+
+
+def rotate_activation_matmul(x: torch.Tensor) -> torch.Tensor:
+    """The reference's own form: bf16 batched matmul against H in bf16 (int8_linear.py:124-126)."""
+    M, K = x.shape
+    H = torch.from_numpy(sylvester_signs(GROUP).astype(np.float32)) * H_FP32
+    Hb = H.to(torch.bfloat16)
+    return torch.matmul(x.view(M, K // GROUP, GROUP), Hb).reshape(M, K)
+
+
+# ---------------------------------------------------------------------------
+# activation quantisation (int8_linear.py:129-130)
+# ---------------------------------------------------------------------------
+
+def quantize_rotated(x_rot: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token symmetric int8 quantisation of a bf16 row block (int8_linear.py:129-130)."""
+    x_scale = x_rot.abs().amax(dim=-1, keepdim=True).clamp(min=1e-5) / 127.0
+    x_int8 = (x_rot / x_scale).round().clamp(-128, 127).to(torch.int8)
+    return x_int8, x_scale
+
+
+def act_quant_had128(x: torch.Tensor):
+    """Rotate (exact) + quantise: returns (q int8 [M,K], sx bf16 [M,1], x_rot bf16 [M,K])."""
+    x_rot = rotate_activation_exact(x)
+    q, s = quantize_rotated(x_rot)
+    return q, s, x_rot
+
+
+def act_quant_had128_matmul(x: torch.Tensor):
+    x_rot = rotate_activation_matmul(x)
+    q, s = quantize_rotated(x_rot)
+    return q, s, x_rot
+
+
+def act_quant_plain(x: torch.Tensor):
+    """W8A8 without rotation (int8_linear.py:87-88), used when K % 128 != 0."""
+    q, s = quantize_rotated(x)
+    return q, s
+
+
+# ---------------------------------------------------------------------------
+# weight prep (hadamard.py:47-75, int8_linear.py:67-73, :256-281)
+# ---------------------------------------------------------------------------
+
+def rotate_weight_exact(w: torch.Tensor) -> torch.Tensor:
+    """W_rot = W @ H^T per 128-group, in fp64 with the fp32 constant 1/sqrt(128), rounded to fp32."""
+    N, K = w.shape
+    s = fwht_f64(w.float().numpy().reshape(N, K // GROUP, GROUP)) * np.float64(H_FP32)
+    return torch.from_numpy(s.reshape(N, K).astype(np.float32))
+
+
+def quantize_weight_per_channel(w32: torch.Tensor):
+    """int8_linear.py:67-73 (fp32 in, int8 + fp32 scale out)."""
+    scale = w32.abs().amax(dim=1).clamp(min=1e-5) / 127.0
+    wq = (w32 / scale.unsqueeze(1)).round().clamp(-128, 127).to(torch.int8)
+    return wq, scale
+
+
+def weight_prep(w: torch.Tensor, hadamard: bool = True):
+    """Returns (w_int8 [N,K], w_scale bf16 [N], w_scale_fp32 [N])."""
+    w32 = rotate_weight_exact(w) if hadamard else w.float()
+    wq, s32 = quantize_weight_per_channel(w32)
+    return wq, s32.to(torch.bfloat16), s32
+
+
+# ---------------------------------------------------------------------------
+# GEMM + dequant epilogue (int8_linear.py:133-138)
+# ---------------------------------------------------------------------------
+
+def gemm_acc_i32(q: torch.Tensor, wq: torch.Tensor) -> torch.Tensor:
+    """int32 accumulators acc[m, n] = sum_k q[m,k] * wq[n,k] (torch._int_mm, int8_linear.py:133)."""
+    M = q.shape[0]
+    if M > 16 and M % 8 == 0 and q.shape[1] % 8 == 0 and wq.shape[0] % 8 == 0:
+        return torch._int_mm(q, wq.t())
+    return (q.to(torch.int64) @ wq.to(torch.int64).t()).to(torch.int32)
+
+
+def dequant_epilogue(acc: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor,
+                     bias: torch.Tensor | None) -> torch.Tensor:
+    """y = bf16(acc) * bf16(sx * sw) (+ bias), all bf16 (int8_linear.py:134-137)."""
+    y = acc.to(torch.bfloat16) * (sx.reshape(-1, 1) * sw.reshape(1, -1))
+    if bias is not None:
+        y = y + bias
+    return y
+
+
+def w8a8_linear(x: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                bias: torch.Tensor | None = None, hadamard: bool = True) -> torch.Tensor:
+    """_make_w8a8_hadamard_forward._forward (int8_linear.py:114-138) on a 2-D bf16 input."""
+    if hadamard:
+        q, sx, _ = act_quant_had128(x)
+    else:
+        q, sx = act_quant_plain(x)
+    return dequant_epilogue(gemm_acc_i32(q, wq), sx, sw, bias)
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm family (rms_norm.py:47-57, fused_norm_residual.py:58-73)
+# ---------------------------------------------------------------------------
+
+def rstd_rows(x: torch.Tensor, eps: float) -> torch.Tensor:
+    """rsqrt(mean(x^2) + eps) per row in fp32 (exactly-rounded sum, IEEE ops)."""
+    n = x.shape[-1]
+    ss = (x.double() ** 2).sum(-1, keepdim=True).float()
+    ms = ss / np.float32(n)
+    return 1.0 / torch.sqrt(ms + np.float32(eps))
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """Y = bf16( bf16(x * rstd) * w )  (rms_norm.py:47-57).
+
+    The weight product is formed in fp32 and rounded once to bf16, which equals
+    the Triton kernel's result both for bf16 weights (exact fp32 product) and
+    for fp32 weights (fp32 product, rounded at the bf16 store).
+    """
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1])
+    xn = (x2.float() * rstd_rows(x2, eps)).to(torch.bfloat16)
+    return (xn.float() * w.float()).to(x.dtype).reshape(shape)
+
+
+def modulate(n: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor | None = None) -> torch.Tensor:
+    """n * (1 + scale) per batch row (patching_comfyui.py:378, :401); optional shift (zero = reference).
+
+    n [B, S, D] bf16, scale/shift [B, D] bf16.
+    """
+    y = n * (1 + scale.unsqueeze(1))
+    if shift is not None:
+        y = y + shift.unsqueeze(1)
+    return y
+
+
+def norm_gate_residual(x, residual, gate, w, eps: float = 1e-5):
+    """Y = R + G * bf16(bf16(X * rstd) * W)   (fused_norm_residual.py:58-73).
+
+    x, residual [B, S, D]; gate broadcastable [B, 1, D] or [B, D].
+    """
+    shape = x.shape
+    D = shape[-1]
+    xs = rms_norm(x, w, eps)
+    g = gate.reshape(gate.shape[0], 1, D) if gate.dim() == 2 else gate
+    return residual + (g.expand(shape) * xs)
+
+
+# ---------------------------------------------------------------------------
+# SwiGLU (swiglu.py:51-58)
+# ---------------------------------------------------------------------------
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """out = bf16( silu_fp32(gate) ) * up."""
+    g = gate.float()
+    silu = g * torch.sigmoid(g)
+    return silu.to(up.dtype) * up
+
+
+# ---------------------------------------------------------------------------
+# RoPE (rope_3d.py:56-89, fused_qknorm_rope.py:85-151)
+# ---------------------------------------------------------------------------
+
+def rope_pairs(xn: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Interleaved-pair rotation in fp32, no FMA contraction; xn [..., d] bf16; cos/sin [..., d/2] fp32."""
+    xe = xn[..., 0::2].float()
+    xo = xn[..., 1::2].float()
+    ne = xe * cos - xo * sin
+    no = xo * cos + xe * sin
+    return torch.stack([ne, no], dim=-1).flatten(-2).to(xn.dtype)
+
+
+def _cos_sin(freqs_cis: torch.Tensor, batch: int):
+    if freqs_cis.shape[0] != batch:
+        freqs_cis = freqs_cis.expand(batch, -1, -1)
+    return freqs_cis.real.float().unsqueeze(2), freqs_cis.imag.float().unsqueeze(2)
+
+
+def fused_qknorm_rope(x: torch.Tensor, w: torch.Tensor, freqs_cis: torch.Tensor, eps: float = 1e-5):
+    """x [B,S,H,d] bf16; w [d]; freqs_cis complex64 [B or 1, S, d/2] (fused_qknorm_rope.py:85-151)."""
+    B, S, H, d = x.shape
+    if d % 2:
+        raise ValueError(f"head_dim must be even, got {d}")
+    if freqs_cis.shape[-1] != d // 2:
+        raise ValueError(f"freqs_cis last dim {freqs_cis.shape[-1]} != head_dim//2 {d // 2}")
+    xn = rms_norm(x, w, eps)
+    c, s = _cos_sin(freqs_cis, B)
+    return rope_pairs(xn, c, s)
+
+
+def rope_3d(x: torch.Tensor, freqs_cis: torch.Tensor) -> torch.Tensor:
+    """RoPE only (rope_3d.py:56-89)."""
+    B, S, H, d = x.shape
+    if d % 2:
+        raise ValueError(f"head_dim must be even, got {d}")
+    if freqs_cis.shape[-1] != d // 2:
+        raise ValueError(f"freqs_cis last dim {freqs_cis.shape[-1]} != head_dim//2 {d // 2}")
+    c, s = _cos_sin(freqs_cis, B)
+    return rope_pairs(x, c, s)
+
+
+def convert_rope_matrix_to_complex(freqs_cis: torch.Tensor) -> torch.Tensor:
+    """2x2 rotation matrices [..., d/2, 2, 2] -> complex64 (patching_comfyui.py:115-134)."""
+    cos = freqs_cis[..., 0, 0]
+    sin = freqs_cis[..., 1, 0]
+    if cos.ndim == 4 and cos.shape[2] == 1:
+        cos = cos.squeeze(2)
+        sin = sin.squeeze(2)
+    return torch.complex(cos.float(), sin.float())
+
+
+def rope_angles(positions: torch.Tensor, axes_dims=(32, 48, 48), theta: float = 256.0) -> torch.Tensor:
+    """Angles [S, sum(d_i)/2] for multi-axis RoPE: pos_i * theta^(-2j/d_i), fp64 then fp32 trig.
+
+    positions: int [S, n_axes].  Per axis, frequencies are
+    theta ** -(2j / d_i) for j < d_i/2, concatenated in axis order.
+    """
+    parts = []
+    for a, d in enumerate(axes_dims):
+        j = torch.arange(0, d // 2, dtype=torch.float64)
+        omega = 1.0 / (theta ** (2.0 * j / d))
+        parts.append(positions[:, a].to(torch.float64)[:, None] * omega[None, :])
+    return torch.cat(parts, dim=-1)
+
+
+def rope_freqs_complex(positions: torch.Tensor, axes_dims=(32, 48, 48), theta: float = 256.0):
+    """complex64 [S, d/2] with cos/sin computed in fp64 and rounded to fp32."""
+    ang = rope_angles(positions, axes_dims, theta)
+    return torch.complex(torch.cos(ang).float(), torch.sin(ang).float())
+
+
+def rope_freqs_matrix(positions: torch.Tensor, axes_dims=(32, 48, 48), theta: float = 256.0):
+    """The same table in the 2x2-matrix form [S, d/2, 2, 2] fp32 ([[c, -s], [s, c]])."""
+    fc = rope_freqs_complex(positions, axes_dims, theta)
+    c, s = fc.real, fc.imag
+    return torch.stack([torch.stack([c, -s], -1), torch.stack([s, c], -1)], -2)
+
+
+def zimage_positions(grid_h: int = 64, grid_w: int = 64, n_text: int = 512) -> torch.Tensor:
+    """(frame, row, col) ids: image tokens on frame 1 over the grid, then text tokens on frames 0..n_text-1."""
+    r, c = torch.meshgrid(torch.arange(grid_h), torch.arange(grid_w), indexing="ij")
+    img = torch.stack([torch.ones(grid_h * grid_w, dtype=torch.long), r.flatten(), c.flatten()], -1)
+    txt = torch.stack([torch.arange(n_text), torch.zeros(n_text, dtype=torch.long),
+                       torch.zeros(n_text, dtype=torch.long)], -1)
+    return torch.cat([img, txt], 0)
+
+
+# ---------------------------------------------------------------------------
+# adaLN modulation (patching_comfyui.py:368-372; adaln_modulation.py:68-81)
+# ---------------------------------------------------------------------------
+
+def adaln_chunks(raw: torch.Tensor, dim: int):
+    """Eager default: chunk(4) + tanh on the gates, scales raw (patching_comfyui.py:368-372)."""
+    s_msa, g_msa, s_mlp, g_mlp = raw.reshape(raw.shape[0], 4 * dim).chunk(4, dim=1)
+    return s_msa, g_msa.tanh(), s_mlp, g_mlp.tanh()
+
+
+def adaln_modulation(raw: torch.Tensor, dim: int):
+    """Triton variant: (1+scale_msa, tanh(gate_msa), 1+scale_mlp, tanh(gate_mlp)) (adaln_modulation.py:68-81)."""
+    if raw.shape[-1] != 4 * dim:
+        raise ValueError(f"raw.shape[-1] must equal 4 * dim = {4 * dim}, got raw.shape={raw.shape}")
+    lead = raw.shape[:-1]
+    r = raw.reshape(-1, 4 * dim)
+    sm, gm, sp, gp = r[:, :dim], r[:, dim:2 * dim], r[:, 2 * dim:3 * dim], r[:, 3 * dim:]
+    out = (sm + 1.0, torch.tanh(gm.float()).to(raw.dtype), sp + 1.0, torch.tanh(gp.float()).to(raw.dtype))
+    return tuple(o.reshape(*lead, dim) for o in out)
+
+
+# ---------------------------------------------------------------------------
+# attention (SDPA stand-in for comfy's optimized_attention_masked)
+# ---------------------------------------------------------------------------
+
+def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """q,k,v [B,S,H,d] bf16 -> [B,S,H*d] bf16; fp32 softmax(QK^T/sqrt(d))V, non-causal."""
+    B, S, H, d = q.shape
+    o = torch.nn.functional.scaled_dot_product_attention(
+        q.float().transpose(1, 2), k.float().transpose(1, 2), v.float().transpose(1, 2))
+    return o.transpose(1, 2).reshape(B, S, H * d).to(q.dtype)
+
+
+__all__ = [n for n in dir() if not n.startswith("_")]

@@ -1,0 +1,260 @@
+"""sm_100a kernels vs the oracle, called through the C ABI (needs a B200)."""
+
+import pytest
+import torch
+
+from helpers import seeded_w, seeded_x
+from oracle import ops
+from zimage_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _act_quant(x, had=True, want_rot=True):
+    M, K = x.shape
+    xd = x.cuda().contiguous()
+    q = torch.empty(M, K, dtype=torch.int8, device="cuda")
+    sx = torch.empty(M, dtype=torch.bfloat16, device="cuda")
+    xr = torch.empty(M, K, dtype=torch.bfloat16, device="cuda") if want_rot else None
+    _lib.call("zib_act_quant", xd.data_ptr(), K, q.data_ptr(), K, sx.data_ptr(), _lib.ptr(xr), M, K,
+              1 if had else 0, _lib.stream_of(xd))
+    torch.cuda.synchronize()
+    return q.cpu(), sx.cpu(), None if xr is None else xr.cpu()
+
+
+@pytest.mark.parametrize("M,K", [(1, 128), (37, 3840), (256, 3840), (64, 10240), (5, 256)])
+def test_act_quant_hadamard_bitexact(cuda, M, K):
+    x = seeded_x(M, K, seed=M + K)
+    if M > 3:
+        x[2] = 0           # all-zero row: scale clamp path
+        x[3] *= 1e4        # huge row
+    q, sx, xr = _act_quant(x)
+    oq, osx, oxr = ops.act_quant_had128(x)
+    # the quantisation of the kernel's own rotation is exact reference arithmetic
+    rq, rs = ops.quantize_rotated(xr)
+    assert torch.equal(q, rq) and torch.equal(sx, rs.flatten())
+    # the rotation itself matches the exact oracle except for rare fp32-sum roundings
+    assert (xr != oxr).float().mean().item() <= 1e-5
+    assert torch.equal(sx, osx.flatten())
+    assert int((q != oq).sum()) == 0
+
+
+def test_act_quant_vs_reference_matmul_rotation(cuda):
+    """Against the reference's own bf16-matmul rotation (int8_linear.py:124-126)."""
+    x = seeded_x(1024, 3840, seed=0)
+    q, sx, _ = _act_quant(x, want_rot=False)
+    rq, rsx, _ = ops.act_quant_had128_matmul(x)
+    assert torch.equal(sx, rsx.flatten())
+    assert (q != rq).float().mean().item() <= 1e-5
+    assert int((q.int() - rq.int()).abs().max()) <= 1
+
+
+@pytest.mark.parametrize("M,K", [(3, 200), (64, 3840), (17, 8)])
+def test_act_quant_plain_bitexact(cuda, M, K):
+    x = seeded_x(M, K, seed=7)
+    q, sx, _ = _act_quant(x, had=False, want_rot=False)
+    oq, osx = ops.act_quant_plain(x)
+    assert torch.equal(q, oq) and torch.equal(sx, osx.flatten())
+
+
+def _rand_i8(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (7, 40, 32), (200, 300, 160), (257, 513, 384),
+                                   (128, 256, 3840), (300, 1024, 10240), (1024, 11520, 3840)])
+def test_gemm_int32_accumulators_bitexact(cuda, M, N, K):
+    q = _rand_i8((M, K), 1)
+    w = _rand_i8((N, K), 2)
+    acc = torch.empty(M, N + (-N) % 4, dtype=torch.int32, device="cuda")
+    qd, wd = q.cuda(), w.cuda()
+    _lib.call("zib_gemm_w8a8_acc_i32", qd.data_ptr(), K, wd.data_ptr(), K, acc.data_ptr(), acc.stride(0),
+              M, N, K, _lib.stream_of(qd))
+    torch.cuda.synchronize()
+    assert _lib.device_error_read_clear() == 0
+    want = ops.gemm_acc_i32(q, w)
+    assert torch.equal(acc[:, :N].cpu(), want)
+
+
+@pytest.mark.parametrize("M,N,K,bias", [(48, 256, 384, True), (129, 300, 256, False),
+                                        (512, 3840, 3840, False), (64, 20480, 3840, True)])
+def test_gemm_dequant_epilogue_bitexact(cuda, M, N, K, bias):
+    x = seeded_x(M, K, seed=3)
+    w = seeded_w(N, K, seed=4)
+    wq, sw, _ = ops.weight_prep(w)
+    q, sx, _ = ops.act_quant_had128(x)
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(5)) * 0.5).to(torch.bfloat16) if bias else None
+    ldy = N + (-N) % 8
+    y = torch.empty(M, ldy, dtype=torch.bfloat16, device="cuda")
+    qd, wd, sxd, swd = q.cuda(), wq.cuda(), sx.flatten().cuda(), sw.cuda()
+    bd = b.cuda() if bias else None
+    _lib.call("zib_gemm_w8a8", qd.data_ptr(), K, wd.data_ptr(), K, sxd.data_ptr(), swd.data_ptr(),
+              _lib.ptr(bd), y.data_ptr(), ldy, M, N, K, _lib.stream_of(qd))
+    torch.cuda.synchronize()
+    want = ops.dequant_epilogue(ops.gemm_acc_i32(q, wq), sx, sw, b)
+    assert torch.equal(y[:, :N].cpu(), want)
+
+
+@pytest.mark.parametrize("N,K,had", [(256, 384, True), (64, 176, False), (1000, 3840, True), (40, 10240, True)])
+def test_weight_prep_bitexact(cuda, N, K, had):
+    w = seeded_w(N, K, seed=N)
+    wd = w.cuda()
+    wq = torch.empty(N, K, dtype=torch.int8, device="cuda")
+    sw = torch.empty(N, dtype=torch.bfloat16, device="cuda")
+    sw32 = torch.empty(N, dtype=torch.float32, device="cuda")
+    rot = torch.empty(N, K, dtype=torch.float32, device="cuda")
+    _lib.call("zib_weight_prep", wd.data_ptr(), K, wq.data_ptr(), K, sw.data_ptr(), sw32.data_ptr(),
+              rot.data_ptr(), K, N, K, 1 if had else 0, _lib.stream_of(wd))
+    torch.cuda.synchronize()
+    owq, osw, osw32 = ops.weight_prep(w, hadamard=had)
+    assert torch.equal(wq.cpu(), owq)
+    assert torch.equal(sw.cpu(), osw)
+    assert torch.equal(sw32.cpu(), osw32)
+    want_rot = ops.rotate_weight_exact(w) if had else w.float()
+    assert torch.equal(rot.cpu(), want_rot)
+
+
+# ---------------------------------------------------------------------------
+# row kernels
+# ---------------------------------------------------------------------------
+
+def _norm_w(n, seed=11):
+    return (1.0 + 0.1 * torch.randn(n, generator=torch.Generator().manual_seed(seed))).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("shape", [(2, 7, 3840), (1, 1, 128), (3, 5, 1000), (4, 130)])
+def test_rms_norm_bitexact(cuda, shape):
+    from zimage_b200 import triton_rms_norm
+
+    x = seeded_x(int(torch.tensor(shape[:-1]).prod()), shape[-1], seed=9).reshape(shape)
+    w = _norm_w(shape[-1])
+    y = triton_rms_norm(x.cuda(), w.cuda(), eps=1e-5).cpu()
+    assert torch.equal(y, ops.rms_norm(x, w, 1e-5))
+
+
+def test_rmsnorm_mod_and_quant_bitexact(cuda):
+    B, S, D = 2, 33, 3840
+    x = seeded_x(B * S, D, seed=12).reshape(B, S, D)
+    w = _norm_w(D)
+    raw = (torch.randn(B, 4 * D, generator=torch.Generator().manual_seed(13)) * 0.1).to(torch.bfloat16)
+    scale = raw[:, :D]
+    want = ops.modulate(ops.rms_norm(x, w, 1e-5), scale)
+    xd, wd, rawd = x.cuda().contiguous(), w.float().cuda(), raw.cuda()
+    y = torch.empty(B * S, D, dtype=torch.bfloat16, device="cuda")
+    st = _lib.stream_of(xd)
+    _lib.call("zib_rmsnorm_mod", xd.data_ptr(), D, wd.data_ptr(), rawd.data_ptr(), None, 4 * D, S,
+              y.data_ptr(), D, B * S, D, 1e-5, st)
+    q = torch.empty(B * S, D, dtype=torch.int8, device="cuda")
+    sx = torch.empty(B * S, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_rmsnorm_mod_quant", xd.data_ptr(), D, wd.data_ptr(), rawd.data_ptr(), None, 4 * D, S,
+              q.data_ptr(), D, sx.data_ptr(), B * S, D, 1e-5, 1, st)
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu().reshape(B, S, D), want)
+    oq, osx, _ = ops.act_quant_had128(want.reshape(B * S, D))
+    assert torch.equal(sx.cpu(), osx.flatten())
+    assert torch.equal(q.cpu(), oq)
+
+
+def test_norm_gate_residual_and_fused_quant_bitexact(cuda):
+    from zimage_b200 import triton_fused_norm_gate_residual
+
+    B, S, D = 2, 17, 3840
+    x = seeded_x(B * S, D, seed=21).reshape(B, S, D)
+    r = seeded_x(B * S, D, seed=22).reshape(B, S, D)
+    g = torch.tanh(torch.randn(B, 1, D, generator=torch.Generator().manual_seed(23))).to(torch.bfloat16)
+    w, w2 = _norm_w(D, 1), _norm_w(D, 2)
+    want = ops.norm_gate_residual(x, r, g, w, 1e-5)
+    y = triton_fused_norm_gate_residual(x.cuda(), r.cuda(), g.cuda(), w.cuda(), 1e-5).cpu()
+    assert torch.equal(y, want)
+    # fused with the next norm + modulation + quantisation
+    s = (torch.randn(B, D, generator=torch.Generator().manual_seed(24)) * 0.1).to(torch.bfloat16)
+    xd, rd, gd, sd = x.cuda().contiguous(), r.cuda().contiguous(), g.reshape(B, D).cuda().contiguous(), s.cuda()
+    wd, w2d = w.float().cuda(), w2.float().cuda()
+    y2 = torch.empty(B * S, D, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(B * S, D, dtype=torch.int8, device="cuda")
+    sx = torch.empty(B * S, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_norm_gate_residual_mod_quant", xd.data_ptr(), D, rd.data_ptr(), D, gd.data_ptr(), D, S,
+              wd.data_ptr(), y2.data_ptr(), D, w2d.data_ptr(), sd.data_ptr(), None, D,
+              q.data_ptr(), D, sx.data_ptr(), B * S, D, 1e-5, 1e-6, 1, _lib.stream_of(xd))
+    torch.cuda.synchronize()
+    assert torch.equal(y2.cpu().reshape(B, S, D), want)
+    nxt = ops.modulate(ops.rms_norm(want, w2, 1e-6), s)
+    oq, osx, _ = ops.act_quant_had128(nxt.reshape(B * S, D))
+    assert torch.equal(sx.cpu(), osx.flatten())
+    assert torch.equal(q.cpu(), oq)
+
+
+def test_swiglu_and_fused_quant(cuda):
+    from zimage_b200 import triton_swiglu_forward
+
+    M, F = 40, 10240
+    gate = seeded_x(M, F, seed=31, outlier_frac=0.0)
+    up = seeded_x(M, F, seed=32, outlier_frac=0.0)
+    out = triton_swiglu_forward(gate.cuda(), up.cuda()).cpu()
+    want = ops.swiglu(gate, up)
+    # sigmoid is an fp32 library function on both sides: rare 1-ulp bf16 differences
+    assert (out != want).float().mean().item() < 1e-3
+    assert (out.float() - want.float()).abs().max().item() <= 2 ** -6 * want.float().abs().max().item()
+    h = torch.cat([gate, up], dim=1).cuda()
+    q = torch.empty(M, F, dtype=torch.int8, device="cuda")
+    sx = torch.empty(M, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_swiglu_quant", h.data_ptr(), 2 * F, h.data_ptr() + 2 * F, 2 * F, q.data_ptr(), F,
+              sx.data_ptr(), M, F, 1, _lib.stream_of(h))
+    torch.cuda.synchronize()
+    oq, osx, _ = ops.act_quant_had128(out)  # quantisation of the kernel's own SwiGLU output
+    assert torch.equal(sx.cpu(), osx.flatten())
+    assert torch.equal(q.cpu(), oq)
+
+
+@pytest.mark.parametrize("B,S,H,fb", [(2, 48, 30, 1), (1, 5, 3, 1), (2, 9, 4, 2)])
+def test_qknorm_rope_bitexact(cuda, B, S, H, fb):
+    from zimage_b200 import triton_fused_qknorm_rope, triton_rope_3d
+
+    x = seeded_x(B * S * H, 128, seed=41).reshape(B, S, H, 128)
+    w = _norm_w(128, 42)
+    pos = ops.zimage_positions(4, 4, S)[:S]
+    fc = ops.rope_freqs_complex(pos).unsqueeze(0).expand(fb, -1, -1).contiguous()
+    want = ops.fused_qknorm_rope(x, w, fc, 1e-6)
+    got = triton_fused_qknorm_rope(x.cuda(), w.cuda(), fc.cuda(), eps=1e-6).cpu()
+    assert torch.equal(got, want)
+    want_r = ops.rope_3d(x, fc)
+    got_r = triton_rope_3d(x.cuda(), fc.cuda()).cpu()
+    assert torch.equal(got_r, want_r)
+
+
+def test_qknorm_rope_strided_in_place(cuda):
+    """In place on the Q slice of a fused QKV buffer (the block's use)."""
+    from zimage_b200.kernels.fused_qknorm_rope import qknorm_rope_into, rope_tables
+
+    B, S, H = 2, 16, 30
+    qkv = seeded_x(B * S, 3 * H * 128, seed=51).reshape(B, S, 3, H, 128)
+    w = _norm_w(128, 52)
+    fc = ops.rope_freqs_complex(ops.zimage_positions(4, 4, 0)).unsqueeze(0)
+    want = ops.fused_qknorm_rope(qkv[:, :, 1], w, fc, 1e-5)
+    d = qkv.cuda()
+    xk = d[:, :, 1]
+    cos, sin, cs_b = rope_tables(fc.cuda(), B)
+    qknorm_rope_into(xk, xk, w.float().cuda(), cos, sin, cs_b, 1e-5)
+    torch.cuda.synchronize()
+    got = d.cpu()
+    assert torch.equal(got[:, :, 1], want)
+    assert torch.equal(got[:, :, 0], qkv[:, :, 0]) and torch.equal(got[:, :, 2], qkv[:, :, 2])
+
+
+def test_adaln_kernels(cuda):
+    from zimage_b200 import triton_adaln_modulation
+
+    B, D = 2, 3840
+    raw = (torch.randn(B, 4 * D, generator=torch.Generator().manual_seed(61)) * 0.5).to(torch.bfloat16)
+    got = triton_adaln_modulation(raw.cuda(), D)
+    want = ops.adaln_modulation(raw, D)
+    for a, b in zip(got, want):
+        a = a.cpu()
+        assert (a != b).float().mean().item() < 1e-3
+        assert (a.float() - b.float()).abs().max().item() <= 2 ** -7
+    gates = torch.empty(B, 2, D, dtype=torch.bfloat16, device="cuda")
+    rd = raw.cuda()
+    _lib.call("zib_adaln_gates", rd.data_ptr(), 4 * D, gates.data_ptr(), B, D, _lib.stream_of(rd))
+    torch.cuda.synchronize()
+    assert torch.equal(gates[:, 0].cpu(), got[1].cpu()) and torch.equal(gates[:, 1].cpu(), got[3].cpu())
