@@ -267,8 +267,7 @@ __global__ void __launch_bounds__(1024) norm_gate_residual_kernel(
 // K4: SwiGLU  out = bf16(bf16(silu(g)) * u)   (swiglu.py:51-58)  (+ quant)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float silu_bf16(float g) {
-  float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-  return bf16_round(__fmul_rn(g, sig));
+  return bf16_round(__fmul_rn(g, zib_sigmoidf(g)));
 }
 
 template <int CPT, bool VEC, bool QUANT, bool HAD>
@@ -357,9 +356,9 @@ __global__ void adaln_modulation_kernel(const uint16_t* __restrict__ raw, int64_
   const int64_t r = i / dim, c = i % dim;
   const uint16_t* rr = raw + r * ldr;
   sm[i] = float_to_bf16_bits(__fadd_rn(bf16_bits_to_float(rr[c]), 1.0f));
-  gm[i] = float_to_bf16_bits(tanhf(bf16_bits_to_float(rr[dim + c])));
+  gm[i] = float_to_bf16_bits(zib_tanhf(bf16_bits_to_float(rr[dim + c])));
   sp[i] = float_to_bf16_bits(__fadd_rn(bf16_bits_to_float(rr[2 * dim + c]), 1.0f));
-  gp[i] = float_to_bf16_bits(tanhf(bf16_bits_to_float(rr[3 * dim + c])));
+  gp[i] = float_to_bf16_bits(zib_tanhf(bf16_bits_to_float(rr[3 * dim + c])));
 }
 
 __global__ void adaln_gates_kernel(const uint16_t* __restrict__ raw, int64_t ldr,
@@ -368,7 +367,7 @@ __global__ void adaln_gates_kernel(const uint16_t* __restrict__ raw, int64_t ldr
   if (i >= rows * 2 * dim) return;
   const int64_t r = i / (2 * dim), k = (i / dim) % 2, c = i % dim;
   const uint16_t* rr = raw + r * ldr;
-  gates[i] = float_to_bf16_bits(tanhf(bf16_bits_to_float(rr[(2 * k + 1) * dim + c])));
+  gates[i] = float_to_bf16_bits(zib_tanhf(bf16_bits_to_float(rr[(2 * k + 1) * dim + c])));
 }
 
 // ---------------------------------------------------------------------------

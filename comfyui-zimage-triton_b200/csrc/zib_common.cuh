@@ -79,6 +79,61 @@ __device__ __forceinline__ float act_scale(float amax_bf16) {
   return bf16_round(__fdiv_rn(a, 127.0f));
 }
 
+// --- bit-reproducible fp32 exp / sigmoid / tanh ---------------------------
+// exp(x) by Cody & Waite two-constant range reduction, x = k*ln2 + r with
+// |r| <= ln2/2, and the degree-7 Taylor polynomial of e^r evaluated by Horner,
+// then an exact scaling by 2^k.  Only separately rounded IEEE multiplies and
+// adds are used (no FMA contraction), so the oracle replays it exactly with
+// numpy float32 arithmetic.  Accuracy: within 2 ulp of exp on [-87, 88].
+constexpr float kInvLn2 = 1.44269502f;
+constexpr float kLn2Hi = 0.693145751953125f;   // 16 significant bits: k*kLn2Hi is exact
+constexpr float kLn2Lo = 1.42860677e-06f;
+constexpr float kExpC7 = 1.98412701e-04f;      // 1/7!
+constexpr float kExpC6 = 1.38888892e-03f;      // 1/6!
+constexpr float kExpC5 = 8.33333377e-03f;      // 1/5!
+constexpr float kExpC4 = 4.16666679e-02f;      // 1/4!
+constexpr float kExpC3 = 1.66666672e-01f;      // 1/3!
+
+__device__ __forceinline__ float zib_expf(float x) {
+  x = fminf(fmaxf(x, -87.0f), 88.0f);
+  const float k = rintf(__fmul_rn(x, kInvLn2));
+  float r = __fsub_rn(x, __fmul_rn(k, kLn2Hi));
+  r = __fsub_rn(r, __fmul_rn(k, kLn2Lo));
+  float p = kExpC7;
+  p = __fadd_rn(__fmul_rn(p, r), kExpC6);
+  p = __fadd_rn(__fmul_rn(p, r), kExpC5);
+  p = __fadd_rn(__fmul_rn(p, r), kExpC4);
+  p = __fadd_rn(__fmul_rn(p, r), kExpC3);
+  p = __fadd_rn(__fmul_rn(p, r), 0.5f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  return ldexpf(p, (int)k);
+}
+
+// sigmoid(g) = 1 / (1 + exp(-g))
+__device__ __forceinline__ float zib_sigmoidf(float g) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, zib_expf(-g)));
+}
+
+// tanh: odd Taylor polynomial (to x^11) for |x| < 0.25, else (1 - e^-2|x|) / (1 + e^-2|x|)
+__device__ __forceinline__ float zib_tanhf(float x) {
+  const float a = fabsf(x);
+  float t;
+  if (a < 0.25f) {
+    const float x2 = __fmul_rn(a, a);
+    float p = -8.86323552e-03f;                  // -1382/155925
+    p = __fadd_rn(__fmul_rn(p, x2), 2.18694880e-02f);   // 62/2835
+    p = __fadd_rn(__fmul_rn(p, x2), -5.39682545e-02f);  // -17/315
+    p = __fadd_rn(__fmul_rn(p, x2), 1.33333340e-01f);   // 2/15
+    p = __fadd_rn(__fmul_rn(p, x2), -3.33333343e-01f);  // -1/3
+    t = __fadd_rn(a, __fmul_rn(__fmul_rn(p, x2), a));
+  } else {
+    const float e = zib_expf(__fmul_rn(-2.0f, a));
+    t = __fdiv_rn(__fsub_rn(1.0f, e), __fadd_rn(1.0f, e));
+  }
+  return copysignf(t, x);
+}
+
 // rstd = 1 / sqrt(RN32(sum)/n + eps), IEEE fp32 ops
 __device__ __forceinline__ float rstd_from_sum(double ss, int n, float eps) {
   float ms = __fdiv_rn((float)ss, (float)n);

@@ -1,0 +1,247 @@
+"""Per-kernel microbenchmark of the sm_100a kernels at the Z-Image shapes.
+
+    python -m zimage_b200.kernel_bench [--only a,b] [--iters 20] [--out file.jsonl]
+
+Each kernel runs at the shape it has in the 1024x1024 CFG-pair step (B*S = 9216
+token rows, D = 3840, F = 10240, 30 heads x 128) unless noted.  Every timed
+iteration is preceded by a 256 MB memset that evicts L2, and is timed alone
+with CUDA events on the launch stream; the median is reported.  Bandwidth
+kernels report algorithmic bytes / time against the measured HBM copy
+bandwidth; GEMMs report 2*M*N*K / time against the dense INT8 datasheet peak.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+from pathlib import Path
+
+import torch
+
+from . import _lib
+
+HBM_FALLBACK_GBS = 6650.0
+INT8_DATASHEET_TOPS = 4500.0
+M_TOK, D, F, H, HD, S, B = 9216, 3840, 10240, 30, 128, 4608, 2
+
+
+def _hbm_peak() -> tuple[float, str]:
+    for p in (Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json",):
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json)"
+        except Exception:
+            pass
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+def _bf16(*shape, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return torch.randn(*shape, generator=g, device="cuda").to(torch.bfloat16)
+
+
+def _i8(*shape, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return torch.randint(-127, 128, shape, generator=g, device="cuda", dtype=torch.int8)
+
+
+def _empty(*shape, dtype=torch.bfloat16):
+    return torch.empty(*shape, dtype=dtype, device="cuda")
+
+
+def case_act_quant(M=M_TOK, K=D):
+    x, q, sx = _bf16(M, K), _empty(M, K, dtype=torch.int8), _empty(M)
+    st = _lib.stream_of(x)
+
+    def run():
+        _lib.call("zib_act_quant", x.data_ptr(), K, q.data_ptr(), K, sx.data_ptr(), None, M, K, 1, st)
+
+    return run, M * K * 2 + M * K + M * 2, f"[{M},{K}] bf16 -> int8"
+
+
+def case_rmsnorm_mod_quant(M=M_TOK, Dm=D):
+    x, w, raw = _bf16(M, Dm), torch.ones(Dm, device="cuda"), _bf16(B, 4 * Dm, seed=1) * 0.1
+    q, sx = _empty(M, Dm, dtype=torch.int8), _empty(M)
+    st = _lib.stream_of(x)
+
+    def run():
+        _lib.call("zib_rmsnorm_mod_quant", x.data_ptr(), Dm, w.data_ptr(), raw.data_ptr(), None, 4 * Dm, M // B,
+                  q.data_ptr(), Dm, sx.data_ptr(), M, Dm, 1e-5, 1, st)
+
+    return run, M * Dm * 2 + M * Dm + M * 2 + Dm * 4 + B * Dm * 2, f"[{M},{Dm}] norm*mod -> int8"
+
+
+def case_norm_gate_residual_mod_quant(M=M_TOK, Dm=D):
+    x, r = _bf16(M, Dm), _bf16(M, Dm, seed=1)
+    gates, raw = _bf16(B, 2, Dm, seed=2) * 0.3, _bf16(B, 4 * Dm, seed=3) * 0.1
+    w = torch.ones(Dm, device="cuda")
+    y, q, sx = _empty(M, Dm), _empty(M, Dm, dtype=torch.int8), _empty(M)
+    st = _lib.stream_of(x)
+
+    def run():
+        _lib.call("zib_norm_gate_residual_mod_quant", x.data_ptr(), Dm, r.data_ptr(), Dm, gates.data_ptr(), 2 * Dm,
+                  M // B, w.data_ptr(), y.data_ptr(), Dm, w.data_ptr(), raw.data_ptr(), None, 4 * Dm, q.data_ptr(),
+                  Dm, sx.data_ptr(), M, Dm, 1e-5, 1e-5, 1, st)
+
+    return run, 3 * M * Dm * 2 + M * Dm + M * 2 + 2 * Dm * 4 + 2 * B * Dm * 2, f"[{M},{Dm}] x,r -> y + int8"
+
+
+def case_norm_gate_residual(M=M_TOK, Dm=D):
+    x, r, gates = _bf16(M, Dm), _bf16(M, Dm, seed=1), _bf16(B, 2, Dm, seed=2) * 0.3
+    w = torch.ones(Dm, device="cuda")
+    y = _empty(M, Dm)
+    st = _lib.stream_of(x)
+
+    def run():
+        _lib.call("zib_norm_gate_residual", x.data_ptr(), Dm, r.data_ptr(), Dm, gates.data_ptr(), 2 * Dm, M // B,
+                  w.data_ptr(), y.data_ptr(), Dm, M, Dm, 1e-5, st)
+
+    return run, 3 * M * Dm * 2 + Dm * 4 + B * Dm * 2, f"[{M},{Dm}] x,r -> y"
+
+
+def case_swiglu_quant(M=M_TOK, Fm=F):
+    h, q, sx = _bf16(M, 2 * Fm), _empty(M, Fm, dtype=torch.int8), _empty(M)
+    st = _lib.stream_of(h)
+
+    def run():
+        _lib.call("zib_swiglu_quant", h.data_ptr(), 2 * Fm, h.data_ptr() + 2 * Fm, 2 * Fm, q.data_ptr(), Fm,
+                  sx.data_ptr(), M, Fm, 1, st)
+
+    return run, M * 2 * Fm * 2 + M * Fm + M * 2, f"[{M},2x{Fm}] -> int8"
+
+
+def case_swiglu(M=S, Fm=F):
+    g, u, o = _bf16(M, Fm), _bf16(M, Fm, seed=1), _empty(M, Fm)
+    st = _lib.stream_of(g)
+
+    def run():
+        _lib.call("zib_swiglu", g.data_ptr(), Fm, u.data_ptr(), Fm, o.data_ptr(), Fm, M, Fm, st)
+
+    return run, 3 * M * Fm * 2, f"[{M},{Fm}] x2 -> bf16"
+
+
+def case_qknorm_rope():
+    qkv = _bf16(B, S, 3, H, HD)
+    cos = torch.rand(S, HD // 2, device="cuda")
+    sin = torch.rand(S, HD // 2, device="cuda")
+    w = torch.ones(HD, device="cuda")
+    st = _lib.stream_of(qkv)
+    sb, ss, sh = qkv.stride(0), qkv.stride(1), qkv.stride(3)
+
+    def run():
+        for part in (0, 1):
+            p = qkv.data_ptr() + part * H * HD * 2
+            _lib.call("zib_qknorm_rope", p, sb, ss, sh, p, sb, ss, sh, cos.data_ptr(), sin.data_ptr(), 0,
+                      w.data_ptr(), B, S, H, HD, 1e-6, st)
+
+    return run, 2 * 2 * B * S * H * HD * 2 + 2 * S * HD * 4, f"Q,K [{B},{S},{H},{HD}] in place (2 launches)"
+
+
+def case_gemm(M, N, K):
+    q, w = _i8(M, K), _i8(N, K, seed=1)
+    sx, sw = _bf16(M).abs() * 1e-2, _bf16(N, seed=2).abs() * 1e-3
+    y = _empty(M, N)
+    st = _lib.stream_of(q)
+
+    def run():
+        _lib.call("zib_gemm_w8a8", q.data_ptr(), K, w.data_ptr(), K, sx.data_ptr(), sw.data_ptr(), None,
+                  y.data_ptr(), N, M, N, K, st)
+
+    return run, 2 * M * N * K, f"{M}x{N}x{K} int8 -> bf16"
+
+
+def case_weight_prep(N=3 * D, K=D):
+    w, wq, sw = _bf16(N, K) * 0.02, _empty(N, K, dtype=torch.int8), _empty(N)
+    st = _lib.stream_of(w)
+
+    def run():
+        _lib.call("zib_weight_prep", w.data_ptr(), K, wq.data_ptr(), K, sw.data_ptr(), None, None, 0, N, K, 1, st)
+
+    return run, N * K * 2 + N * K + N * 2, f"[{N},{K}] bf16 -> int8 (offline)"
+
+
+def case_sdpa():
+    """torch SDPA (library) at the block's shape, for the step's time budget."""
+    q = _bf16(B, S, 3, H, HD)
+    xq, xk, xv = (q[:, :, i].transpose(1, 2) for i in range(3))
+
+    def run():
+        torch.nn.functional.scaled_dot_product_attention(xq, xk, xv)
+
+    return run, 4 * B * H * S * S * HD, f"[{B},{H},{S},{HD}] bf16 (torch SDPA, library)"
+
+
+CASES = {
+    "act_quant": (lambda: case_act_quant(), "hbm"),
+    "act_quant_m1024": (lambda: case_act_quant(1024, D), "hbm"),
+    "act_quant_k10240": (lambda: case_act_quant(M_TOK, F), "hbm"),
+    "rmsnorm_mod_quant": (lambda: case_rmsnorm_mod_quant(), "hbm"),
+    "norm_gate_residual_mod_quant": (lambda: case_norm_gate_residual_mod_quant(), "hbm"),
+    "norm_gate_residual": (lambda: case_norm_gate_residual(), "hbm"),
+    "swiglu_quant": (lambda: case_swiglu_quant(), "hbm"),
+    "swiglu": (lambda: case_swiglu(), "hbm"),
+    "qknorm_rope": (lambda: case_qknorm_rope(), "hbm"),
+    "weight_prep": (lambda: case_weight_prep(), "hbm"),
+    "gemm_cfg1_qkv_m1024": (lambda: case_gemm(1024, 3 * D, D), "int8"),
+    "gemm_qkv": (lambda: case_gemm(M_TOK, 3 * D, D), "int8"),
+    "gemm_out": (lambda: case_gemm(M_TOK, D, D), "int8"),
+    "gemm_w13": (lambda: case_gemm(M_TOK, 2 * F, D), "int8"),
+    "gemm_w2": (lambda: case_gemm(M_TOK, D, F), "int8"),
+    "sdpa_torch": (lambda: case_sdpa(), "bf16"),
+}
+
+
+def run_case(name: str, iters: int, flush: torch.Tensor) -> dict:
+    run, work, shape = CASES[name][0]()
+    kind = CASES[name][1]
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(iters):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    ts = [a.elapsed_time(b) for a, b in evs]
+    med = statistics.median(ts)
+    rec = {"kernel": name, "shape": shape, "ms_median": round(med, 4), "ms_min": round(min(ts), 4)}
+    if kind == "hbm":
+        peak, src = _hbm_peak()
+        gbs = work / (med * 1e-3) / 1e9
+        rec.update(bytes=work, gbs=round(gbs, 1), peak_gbs=peak, frac=round(gbs / peak, 4), peak_source=src)
+    elif kind == "int8":
+        tops = work / (med * 1e-3) / 1e12
+        rec.update(ops=work, tops=round(tops, 1), peak_tops=INT8_DATASHEET_TOPS,
+                   frac=round(tops / INT8_DATASHEET_TOPS, 4), peak_source="datasheet dense INT8")
+    else:
+        tf = work / (med * 1e-3) / 1e12
+        rec.update(flops=work, tflops=round(tf, 1))
+    return rec
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--out", default="")
+    a = ap.parse_args()
+    names = [n for n in a.only.split(",") if n] or list(CASES)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    lines = []
+    for n in names:
+        rec = run_case(n, a.iters, flush)
+        lines.append(json.dumps(rec))
+        print(lines[-1], flush=True)
+    err = _lib.device_error_read_clear()
+    if err:
+        raise RuntimeError(f"device error word set: {err}")
+    if a.out:
+        Path(a.out).write_text("\n".join(lines) + "\n")
+
+
+if __name__ == "__main__":
+    main()

@@ -73,10 +73,12 @@ def linear(p: dict, key: str, x2: torch.Tensor, bias=None) -> torch.Tensor:
 
 def block_forward(p: dict, x: torch.Tensor, freqs_cis: torch.Tensor, adaln_input: torch.Tensor,
                   eps: float = 1e-5, qk_eps: float = 1e-5, n_heads=N_HEADS, head_dim=HEAD_DIM,
-                  trace: dict | None = None) -> torch.Tensor:
+                  trace: dict | None = None, attn=ops.sdpa) -> torch.Tensor:
     """One patched block forward (patching_comfyui.py:340-415).
 
     x [B,S,D] bf16; freqs_cis complex64 [B or 1, S, d/2]; adaln_input [B, 256] bf16.
+    ``attn(q, k, v) -> [B, S, H*d]`` is the attention (fp32 SDPA by default; tests
+    may replay the attention library's recorded outputs instead).
     """
     B, S, D = x.shape
     raw = linear(p, "adaln_w", adaln_input, p["adaln_b"])                    # :368
@@ -89,7 +91,7 @@ def block_forward(p: dict, x: torch.Tensor, freqs_cis: torch.Tensor, adaln_input
     xv = qkv[..., 2 * hd:].reshape(B, S, n_heads, head_dim)
     xq = ops.fused_qknorm_rope(xq, p["q_norm"], freqs_cis, qk_eps)          # :189
     xk = ops.fused_qknorm_rope(xk, p["k_norm"], freqs_cis, qk_eps)          # :190
-    o = ops.sdpa(xq, xk, xv)                                                 # :197-205
+    o = attn(xq, xk, xv)                                                     # :197-205
     attn_out = linear(p, "out", o.reshape(B * S, hd)).reshape(B, S, D)       # :207
     x = ops.norm_gate_residual(attn_out, x, g_msa, p["attention_norm2"], eps)  # :386-393
     ffn_in = ops.modulate(ops.rms_norm(x, p["ffn_norm1"], eps), s_mlp)      # :401

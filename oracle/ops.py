@@ -262,13 +262,68 @@ def norm_gate_residual(x, residual, gate, w, eps: float = 1e-5):
 
 
 # ---------------------------------------------------------------------------
+# fp32 exp / sigmoid / tanh with a fixed operation order
+# ---------------------------------------------------------------------------
+# exp by Cody & Waite two-constant range reduction (x = k ln2 + r, |r| <= ln2/2)
+# and the degree-7 Taylor polynomial of e^r in Horner form, then an exact
+# scaling by 2^k; every step is one IEEE fp32 operation, so this restatement
+# and the CUDA kernels produce identical bits.  The reference computes these
+# functions with Triton's / torch's own fp32 implementations (swiglu.py:55,
+# adaln_modulation.py:73-74, patching_comfyui.py:371-372); all agree to a few ulp.
+
+_F = np.float32
+EXP_C = [_F(1.98412701e-04), _F(1.38888892e-03), _F(8.33333377e-03), _F(4.16666679e-02),
+         _F(1.66666672e-01), _F(0.5), _F(1.0), _F(1.0)]
+INV_LN2, LN2_HI, LN2_LO = _F(1.44269502), _F(0.693145751953125), _F(1.42860677e-06)
+TANH_C = [_F(-8.86323552e-03), _F(2.18694880e-02), _F(-5.39682545e-02), _F(1.33333340e-01),
+          _F(-3.33333343e-01)]
+
+
+def exp_f32(x: np.ndarray) -> np.ndarray:
+    x = np.minimum(np.maximum(np.asarray(x, dtype=_F), _F(-87.0)), _F(88.0))
+    k = np.rint(x * INV_LN2).astype(_F)
+    r = (x - k * LN2_HI).astype(_F)
+    r = (r - k * LN2_LO).astype(_F)
+    p = np.full_like(r, EXP_C[0])
+    for c in EXP_C[1:]:
+        p = (p * r).astype(_F) + c
+    return np.ldexp(p.astype(_F), k.astype(np.int32)).astype(_F)
+
+
+def sigmoid_f32(g: np.ndarray) -> np.ndarray:
+    return (_F(1.0) / (_F(1.0) + exp_f32(-np.asarray(g, dtype=_F)))).astype(_F)
+
+
+def tanh_f32(x: np.ndarray) -> np.ndarray:
+    x = np.asarray(x, dtype=_F)
+    a = np.abs(x)
+    x2 = (a * a).astype(_F)
+    p = np.full_like(a, TANH_C[0])
+    for c in TANH_C[1:]:
+        p = (p * x2).astype(_F) + c
+    small = (a + ((p * x2).astype(_F) * a).astype(_F)).astype(_F)
+    e = exp_f32((_F(-2.0) * a).astype(_F))
+    big = ((_F(1.0) - e) / (_F(1.0) + e)).astype(_F)
+    return np.copysign(np.where(a < _F(0.25), small, big), x).astype(_F)
+
+
+def _np32(t: torch.Tensor) -> np.ndarray:
+    return t.float().numpy()
+
+
+def tanh_bf16(t: torch.Tensor) -> torch.Tensor:
+    """tanh of a bf16 tensor in fp32, rounded once to bf16."""
+    return torch.from_numpy(tanh_f32(_np32(t))).to(t.dtype)
+
+
+# ---------------------------------------------------------------------------
 # SwiGLU (swiglu.py:51-58)
 # ---------------------------------------------------------------------------
 
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
-    """out = bf16( silu_fp32(gate) ) * up."""
-    g = gate.float()
-    silu = g * torch.sigmoid(g)
+    """out = bf16( silu_fp32(gate) ) * up, silu = g * sigmoid(g) in fp32."""
+    g = _np32(gate)
+    silu = torch.from_numpy((g * sigmoid_f32(g)).astype(_F))
     return silu.to(up.dtype) * up
 
 
@@ -367,7 +422,7 @@ def zimage_positions(grid_h: int = 64, grid_w: int = 64, n_text: int = 512) -> t
 def adaln_chunks(raw: torch.Tensor, dim: int):
     """Eager default: chunk(4) + tanh on the gates, scales raw (patching_comfyui.py:368-372)."""
     s_msa, g_msa, s_mlp, g_mlp = raw.reshape(raw.shape[0], 4 * dim).chunk(4, dim=1)
-    return s_msa, g_msa.tanh(), s_mlp, g_mlp.tanh()
+    return s_msa, tanh_bf16(g_msa), s_mlp, tanh_bf16(g_mlp)
 
 
 def adaln_modulation(raw: torch.Tensor, dim: int):
@@ -377,7 +432,7 @@ def adaln_modulation(raw: torch.Tensor, dim: int):
     lead = raw.shape[:-1]
     r = raw.reshape(-1, 4 * dim)
     sm, gm, sp, gp = r[:, :dim], r[:, dim:2 * dim], r[:, 2 * dim:3 * dim], r[:, 3 * dim:]
-    out = (sm + 1.0, torch.tanh(gm.float()).to(raw.dtype), sp + 1.0, torch.tanh(gp.float()).to(raw.dtype))
+    out = (sm + 1.0, tanh_bf16(gm), sp + 1.0, tanh_bf16(gp))
     return tuple(o.reshape(*lead, dim) for o in out)
 
 

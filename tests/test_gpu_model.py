@@ -113,24 +113,103 @@ def test_block_fused_equals_composed_and_matches_oracle(cuda):
             pc.ENABLE_FUSED_BLOCK = True
     assert "_zib_cache" in m.layers[0].__dict__
     assert torch.equal(y_fused, y_comp)
+    # oracle with its own weight prep and fp32 attention: within the attention-numerics band
     p = omodel.prep_layer(params[0], quant_adaln=True)
     want = omodel.block_forward(p, x, fc, t, n_heads=heads)
-    y = y_fused.cpu()
-    assert rel_l2(y, want) <= 5e-3
-    assert max_abs(y, want) <= 2e-2 * max(1.0, want.abs().max().item())
+    assert rel_l2(y_fused.cpu(), want) <= 1.5e-2
 
 
-def test_step_matches_oracle(cuda):
+def _record_attention():
+    """Wrap the attention call of the patched path; returns (records, restore)."""
+    from zimage_b200.patching import patching_comfyui as pc
+
+    rec = []
+    orig = pc._attention_bshd
+
+    def wrapped(xq, xk, xv, mask):
+        o = orig(xq, xk, xv, mask)
+        rec.append(tuple(t.detach().cpu() for t in (xq, xk, xv, o)))
+        return o
+
+    pc._attention_bshd = wrapped
+
+    def restore():
+        pc._attention_bshd = orig
+
+    return rec, restore
+
+
+def _replay(rec):
+    """Oracle attention that returns the recorded library outputs after checking its inputs."""
+    it = iter(rec)
+
+    def attn(q, k, v):
+        gq, gk, gv, go = next(it)
+        assert torch.equal(q, gq) and torch.equal(k, gk) and torch.equal(v, gv)
+        B, S, H, d = q.shape
+        return go.reshape(B, S, H * d)
+
+    return attn
+
+
+def _gpu_weights_into(params, m):
+    """Oracle params using the GPU-prepped int8 weights (weight prep is checked bit-exact separately)."""
+    out = []
+    for blk, p in zip(m.layers, params):
+        q = dict(p)
+        lins = {"qkv": blk.attention.qkv, "out": blk.attention.out, "w1": blk.feed_forward.w1,
+                "w2": blk.feed_forward.w2, "w3": blk.feed_forward.w3, "adaln_w": blk.adaLN_modulation[0]}
+        for k, lin in lins.items():
+            q[k + "_q"] = lin._w_int8.cpu()
+            q[k + "_s"] = lin._w_scale.cpu()
+        out.append(q)
+    return out
+
+
+def test_step_bitexact_given_attention_library_outputs(cuda):
+    """Full width (dim 3840, 30 heads x 128, FFN 10240), 2 layers, CFG pair: every op of the
+    step is bit-exact with the oracle when the oracle is handed the attention library's own
+    outputs (and checks it feeds that library bit-identical Q, K, V)."""
+    dim, heads, ffn, L = 3840, 30, 10240, 2
+    m, params = _small_model(L, dim, heads, ffn, seed=3)
+    _patch(m)
+    x, t, fm, fc = _inputs(2, 8, 8, 16, dim, seed=8)
+    rec, restore = _record_attention()
+    try:
+        with torch.no_grad():
+            y = m(x.cuda(), t.cuda(), fm.cuda()).cpu()
+    finally:
+        restore()
+    assert len(rec) == L
+    owq, osw, _ = ops.weight_prep(params[0]["out"])
+    assert torch.equal(m.layers[0].attention.out._w_int8.cpu(), owq)
+    want = omodel.step_forward(_gpu_weights_into(params, m), x, fc, t, n_heads=heads, attn=_replay(rec))
+    assert torch.equal(y, want)
+    # the attention library itself, per call, against fp32 attention of the same inputs
+    for q, k, v, o in rec:
+        ref = ops.sdpa(q, k, v).reshape(o.shape)
+        assert rel_l2(o, ref) <= 5e-3
+        assert max_abs(o, ref) <= 2e-2
+
+
+def test_step_vs_fp32_attention_oracle(cuda):
+    """Against an oracle with fp32 attention the only difference is the attention library's
+    bf16 numerics, which the W8A8 re-quantisation of its output amplifies.  Measured:
+    rel-L2 ~6e-3 per block, ~1.4e-2 after 3 blocks at this size."""
     dim, heads, ffn, L = 1024, 8, 2816, 3
     m, params = _small_model(L, dim, heads, ffn, seed=1)
     _patch(m)
     x, t, fm, fc = _inputs(2, 8, 8, 16, dim, seed=6)
-    with torch.no_grad():
-        y = m(x.cuda(), t.cuda(), fm.cuda()).cpu()
-    want = omodel.step_forward([omodel.prep_layer(p, quant_adaln=True) for p in params], x, fc, t,
-                               n_heads=heads)
-    assert rel_l2(y, want) <= 5e-3
-    assert max_abs(y, want) <= 2e-2 * max(1.0, want.abs().max().item())
+    rec, restore = _record_attention()
+    try:
+        with torch.no_grad():
+            y = m(x.cuda(), t.cuda(), fm.cuda()).cpu()
+    finally:
+        restore()
+    layers = _gpu_weights_into(params, m)
+    assert torch.equal(y, omodel.step_forward(layers, x, fc, t, n_heads=heads, attn=_replay(rec)))
+    want = omodel.step_forward(layers, x, fc, t, n_heads=heads)
+    assert rel_l2(y, want) <= 3e-2
 
 
 def test_reference_policy_mixed_bf16_and_int8_layers(cuda):

@@ -117,3 +117,25 @@ def test_rope_table_layout():
     m = ops.rope_freqs_matrix(pos)
     back = ops.convert_rope_matrix_to_complex(m.unsqueeze(0))
     assert torch.equal(back[0], fc)
+
+
+def test_exp_tanh_constants_match_kernel_source_and_accuracy():
+    src = (ROOT / "comfyui-zimage-triton_b200" / "csrc" / "zib_common.cuh").read_text()
+
+    def c(name):
+        return np.float32(float(re.search(rf"{name} = ([-0-9.e]+)f;", src).group(1)))
+
+    assert [c(f"kExpC{i}") for i in (7, 6, 5, 4, 3)] == list(ops.EXP_C[:5])
+    assert (c("kInvLn2"), c("kLn2Hi"), c("kLn2Lo")) == (ops.INV_LN2, ops.LN2_HI, ops.LN2_LO)
+    x = np.linspace(-87, 88, 200001, dtype=np.float32)
+    ref = np.exp(x.astype(np.float64))
+    assert (np.abs(ops.exp_f32(x) - ref) / np.spacing(ref.astype(np.float32))).max() < 1.5
+    g = np.linspace(-12, 12, 100001, dtype=np.float32)
+    tr = np.tanh(g.astype(np.float64))
+    assert (np.abs(ops.tanh_f32(g) - tr) / np.spacing(np.abs(tr).astype(np.float32) + 1e-45)).max() < 2.5
+    # rounded to bf16, the restated silu / tanh agree with torch's on a large sample
+    t = torch.randn(200000, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+    assert torch.equal(ops.tanh_bf16(t), t.float().tanh().to(torch.bfloat16))
+    u = torch.randn(200000, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    g32 = t.float()
+    assert torch.equal(ops.swiglu(t, u), (g32 * torch.sigmoid(g32)).to(torch.bfloat16) * u)
