@@ -10,18 +10,19 @@
 //               128-byte swizzle, 4-stage shared-memory ring.
 //   warp 1      owns TMEM (512 columns = two 128x256 int32 accumulators) and
 //               issues tcgen05.mma (M=128, N=256, K=32) from one thread.
-//   warps 2..5  epilogue: tcgen05.ld 32x32b of the finished accumulator,
+//   warps 2..9  epilogue (two warps per TMEM lane quarter, 128 columns each):
+//               tcgen05.ld 32x32b of the finished accumulator,
 //               dequant + bias + bf16 rounding in registers, global stores;
 //               overlaps the next tile's MMAs (double-buffered TMEM).
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records
 // ZIB_ERR_TIMEOUT in a device error word, drains its in-flight TMA loads and
 // MMAs, frees TMEM and exits.  No TMA multicast is used anywhere.
-#include "zib_common.cuh"
+#include "zib_async.cuh"
 
 #include <cuda.h>
 #include <mutex>
 
-__device__ int g_zib_device_error = 0;
+ZIB_DEFINE_ERROR_READER(zib_err_read_clear_gemm)
 
 namespace zib {
 namespace gemm {
@@ -35,72 +36,13 @@ constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 512;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;  // warp 0 TMA, warp 1 MMA/TMEM, warps 2..9 epilogue
+constexpr int EPI_WARPS = 8;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
-constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 // instruction descriptor: D=s32, A=B=s8, both K-major, N=256, M=128
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                             ((uint32_t)(BM >> 4) << 24);
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: returns false (and raises the CTA abort flag) after kTimeoutNs,
-// or as soon as another role has raised the abort flag.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > kTimeoutNs) {
-      *abort_flag = 1;
-      atomicExch(&g_zib_device_error, (int)ZIB_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
-// Wait used while draining after an abort: bounded, never raises the flag.
-__device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity) {
-  const unsigned long long t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kTimeoutNs) return;
-  }
-}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
@@ -169,6 +111,77 @@ struct Params {
   int64_t ldacc;
 };
 
+// Dequant epilogue of one thread's accumulator row (128-row x 256-column tile
+// in TMEM, this thread = one row): tcgen05.ld 32 columns at a time, then
+// y = bf16(bf16(acc) * bf16(sx*sw)) (+ bias), or the raw int32 accumulators.
+// bf16 round-to-nearest-even on the ALU pipe (finite inputs); keeps the
+// conversion (XU) pipe for the int32 -> fp32 conversions.
+__device__ __forceinline__ float bf16_rne_alu(float v) {
+  uint32_t b = __float_as_uint(v);
+  b += 0x7FFFu + ((b >> 16) & 1u);
+  return __uint_as_float(b & 0xFFFF0000u);
+}
+
+template <bool ACC_OUT>
+__device__ __forceinline__ void epilogue_rows(const Params& p, uint32_t t_row, int row, int nb, int ch_begin,
+                                              int ch_end) {
+  const bool row_ok = row < p.M;
+  float sxf = 0.0f;
+  if (!ACC_OUT && row_ok) sxf = bf16_bits_to_float(p.sx[row]);
+#pragma unroll 1
+  for (int ch = ch_begin; ch < ch_end; ++ch) {
+    uint32_t r[32];
+    __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it converged
+    tmem_ld32(t_row + (uint32_t)(ch * 32), r);
+    tmem_wait_ld();
+    const int n0 = nb * BN + ch * 32;
+    if (!row_ok || n0 >= p.N) continue;
+    const bool full = n0 + 32 <= p.N;
+    if (ACC_OUT) {
+      int32_t* dst = p.acc + (int64_t)row * p.ldacc + n0;
+      if (full && (p.ldacc % 4) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<int4*>(dst + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
+      } else {
+        for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (int)r[j];
+      }
+    } else {
+      float out[32];
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        float swv[8], bv[8];
+        if (full) {
+          load_bf16x8_nc(p.sw + n0 + j, swv);
+          if (p.bias) load_bf16x8_nc(p.bias + n0 + j, bv);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const int n = n0 + j + t;
+            swv[t] = n < p.N ? bf16_bits_to_float(p.sw[n]) : 0.0f;
+            bv[t] = (p.bias && n < p.N) ? bf16_bits_to_float(p.bias[n]) : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float s = bf16_rne_alu(__fmul_rn(sxf, swv[t]));
+          const float a = bf16_rne_alu(__int2float_rn((int)r[j + t]));
+          float v = bf16_rne_alu(__fmul_rn(a, s));
+          if (p.bias) v = bf16_rne_alu(__fadd_rn(v, bv[t]));
+          out[j + t] = v;
+        }
+      }
+      uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, out + j);
+      } else {
+        for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (uint16_t)(__float_as_uint(out[j]) >> 16);
+      }
+    }
+  }
+}
+
 template <bool ACC_OUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -196,7 +209,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);
+      mbar_init(&tempty_bar[a], EPI_WARPS);
     }
     mbar_init(mma_done_bar, 1);
     *abort_flag = 0;
@@ -225,7 +238,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         const int mb = tile % p.num_mb, nb = tile / p.num_mb;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
           tma_load_2d(smem_a + stage * A_BYTES, &tmap_a, &full_bar[stage], kb * BK, mb * BM);
           tma_load_2d(smem_b + stage * B_BYTES, &tmap_b, &full_bar[stage], kb * BK, nb * BN);
@@ -251,11 +264,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       const uint32_t a_base = smem_u32(smem_a), b_base = smem_u32(smem_b);
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(&tempty_bar[accb], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_bounded(&tempty_bar[accb], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(accb * BN);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = sdesc_sw128(a_base + stage * A_BYTES);
           const uint64_t bdesc = sdesc_sw128(b_base + stage * B_BYTES);
@@ -279,74 +292,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    // ---------------- epilogue (warps 2..9) ----------------
+    // warp w reads TMEM lanes [32*(w%4), +32); warps w and w+4 split the 256 columns
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     int accb = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&tfull_bar[accb], acc_phase, abort_flag) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait_bounded(&tfull_bar[accb], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
       tc_fence_after();
       const int mb = tile % p.num_mb, nb = tile / p.num_mb;
-      const int row = mb * BM + quarter * 32 + lane;
-      const bool row_ok = row < p.M;
-      float sxf = 0.0f;
-      if (!ACC_OUT && row_ok) sxf = bf16_bits_to_float(p.sx[row]);
-      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN);
-#pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it converged
-        tmem_ld32(t_row + (uint32_t)(ch * 32), r);
-        tmem_wait_ld();
-        const int n0 = nb * BN + ch * 32;
-        if (!row_ok || n0 >= p.N) continue;
-        const bool full = n0 + 32 <= p.N;
-        if (ACC_OUT) {
-          int32_t* dst = p.acc + (int64_t)row * p.ldacc + n0;
-          if (full && (p.ldacc % 4) == 0) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<int4*>(dst + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
-          } else {
-            for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (int)r[j];
-          }
-        } else {
-          float out[32];
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            float swv[8], bv[8];
-            if (full) {
-              load_bf16x8_nc(p.sw + n0 + j, swv);
-              if (p.bias) load_bf16x8_nc(p.bias + n0 + j, bv);
-            } else {
-#pragma unroll
-              for (int t = 0; t < 8; ++t) {
-                const int n = n0 + j + t;
-                swv[t] = n < p.N ? bf16_bits_to_float(p.sw[n]) : 0.0f;
-                bv[t] = (p.bias && n < p.N) ? bf16_bits_to_float(p.bias[n]) : 0.0f;
-              }
-            }
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              const float s = bf16_round(__fmul_rn(sxf, swv[t]));
-              const float a = bf16_round(__int2float_rn((int)r[j + t]));
-              float v = bf16_round(__fmul_rn(a, s));
-              if (p.bias) v = bf16_round(__fadd_rn(v, bv[t]));
-              out[j + t] = v;
-            }
-          }
-          uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
-          if (full) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, out + j);
-          } else {
-            for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (uint16_t)(__float_as_uint(out[j]) >> 16);
-          }
-        }
-      }
+      epilogue_rows<ACC_OUT>(p, tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN),
+                             mb * BM + quarter * 32 + lane, nb, half * 4, half * 4 + 4);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[accb]);
@@ -360,6 +320,232 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 2-CTA variant (cta_group::2).  A cluster of two CTAs on two SMs computes a
+// 256x256 output tile: each CTA stages its own 128 rows of A and 128 of the
+// tile's 256 B rows (32 KB per 128-deep k-block, 6 stages), both CTAs' TMA
+// loads complete on the leader's full barrier, the leader CTA issues
+// M=256 x N=256 x K=32 MMAs that read both CTAs' shared memory, and each CTA's
+// TMEM receives its 128 accumulator rows.  Per SM this halves the B traffic
+// through shared memory relative to the 1-CTA 128x256 tile.  TMA loads carry
+// .cta_group::2 only; no load uses cluster multicast.  The leader's MMA
+// commits are multicast to both CTAs' barriers (tcgen05.commit), and both
+// CTAs' epilogue warps release an accumulator on the leader's barrier.
+// ---------------------------------------------------------------------------
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK;
+constexpr int P_B_BYTES = 128 * BK;
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+// D=s32, A=B=s8, K-major, N=256, M=256
+constexpr uint32_t kIdescPair = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                                ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrive (when all prior MMAs of this thread retire) on `bar` in every CTA of `mask`.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+template <bool ACC_OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + P_STAGES * P_A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t* full_bar = bars;                          // [P_STAGES]  (leader's is used)
+  uint64_t* empty_bar = bars + P_STAGES;              // [P_STAGES]  (both)
+  uint64_t* tfull_bar = bars + 2 * P_STAGES;          // [2]         (both)
+  uint64_t* tempty_bar = bars + 2 * P_STAGES + 2;     // [2]         (leader's is used)
+  uint64_t* mma_done_bar = bars + 2 * P_STAGES + 4;   // [1]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 2 * EPI_WARPS);  // epilogue warps of both CTAs
+    }
+    mbar_init(mma_done_bar, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  bool aborted = false;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t pend_mask = 0, pend_parity = 0;
+      bool ok = true;
+      for (int tile = cluster_id; tile < p.num_tiles && ok; tile += nclusters) {
+        const int mb = tile % p.num_mb, nb = tile / p.num_mb;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * P_STAGE_BYTES);
+          const uint32_t fb_leader = leader ? fb : mapa_rank(fb, 0);
+          tma_load_2d_pair(smem_a + stage * P_A_BYTES, &tmap_a, fb_leader, kb * BK, mb * 256 + (int)rank * 128);
+          tma_load_2d_pair(smem_b + stage * P_B_BYTES, &tmap_b, fb_leader, kb * BK, nb * 256 + (int)rank * 128);
+          pend_mask |= 1u << stage;
+          pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        aborted = true;
+        if (leader) {
+          for (int s = 0; s < P_STAGES; ++s)
+            if (pend_mask & (1u << s)) mbar_drain_wait(&full_bar[s], (pend_parity >> s) & 1u);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only) ----------------
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int accb = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      const uint32_t a_base = smem_u32(smem_a), b_base = smem_u32(smem_b);
+      for (int tile = cluster_id; tile < p.num_tiles && ok; tile += nclusters) {
+        if (!mbar_wait_bounded(&tempty_bar[accb], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(accb * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_sw128(a_base + stage * P_A_BYTES);
+          const uint64_t bdesc = sdesc_sw128(b_base + stage * P_B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            umma_i8_pair(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4),
+                         kIdescPair, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty_bar[stage], (uint16_t)3);  // frees the stage in both CTAs
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull_bar[accb], (uint16_t)3);
+        accb ^= 1;
+        if (accb == 0) acc_phase ^= 1u;
+      }
+      if (!ok) aborted = true;
+      umma_commit_pair(mma_done_bar, (uint16_t)1);
+      mbar_drain_wait(mma_done_bar, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    int accb = 0;
+    uint32_t acc_phase = 0;
+    const uint32_t tempty_leader0 = mapa_rank(smem_u32(&tempty_bar[0]), 0);
+    for (int tile = cluster_id; tile < p.num_tiles; tile += nclusters) {
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_bounded(&tfull_bar[accb], acc_phase, abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) { aborted = true; break; }
+      tc_fence_after();
+      const int mb = tile % p.num_mb, nb = tile / p.num_mb;
+      epilogue_rows<ACC_OUT>(p, tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN),
+                             mb * 256 + (int)rank * 128 + quarter * 32 + lane, nb, half * 4, half * 4 + 4);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + (uint32_t)(accb * 8));
+      accb ^= 1;
+      if (accb == 0) acc_phase ^= 1u;
+    }
+  }
+
+  // An aborted CTA gives copies still in flight (the peer's loads complete on
+  // the leader's barrier) a bounded grace period before the CTAs leave.
+  if (__syncthreads_or(aborted ? 1 : 0)) {
+    const unsigned long long t0 = globaltimer();
+    while (globaltimer() - t0 < 2000000ull) {
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs are done with TMEM and with each other's barriers
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                  : "memory");
   }
 }
@@ -404,6 +590,9 @@ static int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t o
   }
   return ZIB_OK;
 }
+
+// 0 = automatic (2-CTA pairs when M > 128), 1 = 1-CTA tiles, 2 = 2-CTA pairs
+static int g_gemm_variant = 0;
 
 static int num_sms_for_current_device() {
   int dev = 0;
@@ -462,21 +651,37 @@ static int launch(const void* q, int64_t ldq, const void* wq, int64_t ldw, const
   p.acc = (int32_t*)acc;
   p.ldacc = ldacc;
 
-  static bool attr_set[2][64] = {{false}};
+  const int variant = g_gemm_variant;
+  const bool pair = variant == 2 || (variant == 0 && M > 128);
+  static bool attr_set[2][2][64] = {{{false}}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[ACC_OUT][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_w8a8_kernel<ACC_OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_BYTES);
+  if (dev >= 0 && dev < 64 && !attr_set[pair][ACC_OUT][dev]) {
+    cudaError_t e = pair ? cudaFuncSetAttribute(gemm_w8a8_pair_kernel<ACC_OUT>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES)
+                         : cudaFuncSetAttribute(gemm_w8a8_kernel<ACC_OUT>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) {
       zib_set_error("gemm_w8a8: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
       return ZIB_ERR_LAUNCH;
     }
-    attr_set[ACC_OUT][dev] = true;
+    attr_set[pair][ACC_OUT][dev] = true;
   }
-  int grid = num_sms_for_current_device();
-  if (grid > p.num_tiles) grid = p.num_tiles;
-  gemm_w8a8_kernel<ACC_OUT><<<grid, NUM_THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, p);
+  const int sms = num_sms_for_current_device();
+  if (pair) {
+    // B tiles are re-described with 128-row boxes (each CTA stages half of the 256-row tile)
+    st = make_map(&tb, wq, K, N, ldw, BK, 128);
+    if (st) return st;
+    p.num_mb = (int)((M + 255) / 256);
+    p.num_tiles = p.num_mb * p.num_nb;
+    int clusters = sms / 2;
+    if (clusters > p.num_tiles) clusters = p.num_tiles;
+    gemm_w8a8_pair_kernel<ACC_OUT><<<2 * clusters, NUM_THREADS, P_SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, p);
+  } else {
+    int grid = sms;
+    if (grid > p.num_tiles) grid = p.num_tiles;
+    gemm_w8a8_kernel<ACC_OUT><<<grid, NUM_THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, p);
+  }
   return zib_check_launch(ACC_OUT ? "gemm_w8a8_acc_i32" : "gemm_w8a8");
 }
 
@@ -495,10 +700,11 @@ extern "C" int zib_gemm_w8a8_acc_i32(const void* q, int64_t ldq, const void* wq,
                                  stream);
 }
 
-extern "C" int zib_device_error_read_clear(void) {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_zib_device_error, sizeof(int)) != cudaSuccess) return ZIB_ERR_LAUNCH;
-  int zero = 0;
-  cudaMemcpyToSymbol(g_zib_device_error, &zero, sizeof(int));
-  return v;
+extern "C" int zib_gemm_set_variant(int variant) {
+  if (variant < 0 || variant > 2) {
+    zib_set_error("gemm_set_variant: variant must be 0, 1 or 2");
+    return ZIB_ERR_INVALID_ARG;
+  }
+  zib::gemm::g_gemm_variant = variant;
+  return ZIB_OK;
 }

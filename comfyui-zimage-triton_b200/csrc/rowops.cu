@@ -5,9 +5,11 @@
 // held by 16 consecutive lanes (8 values each) and rotated with 3 in-thread
 // butterfly stages plus 4 xor-shuffle stages.  Every kernel keeps the
 // reference's bf16 rounding points; see zib_common.cuh.
-#include "zib_common.cuh"
+#include "zib_async.cuh"
 
 #include <stdio.h>
+
+ZIB_DEFINE_ERROR_READER(zib_err_read_clear_rows)
 
 namespace zib {
 
@@ -301,47 +303,66 @@ __global__ void __launch_bounds__(1024) swiglu_kernel(
 // K3: per-head RMSNorm + interleaved RoPE, d = 128 (fused_qknorm_rope.py:85-151)
 // 16 lanes per (token, head) row, 8 values (4 pairs) per lane.
 // ---------------------------------------------------------------------------
-template <bool NORM>
-__global__ void __launch_bounds__(256) qknorm_rope_kernel(
+template <bool NORM, int R>
+__global__ void __launch_bounds__(256, 3) qknorm_rope_kernel(
     const uint16_t* __restrict__ x, int64_t x_sb, int64_t x_ss, int64_t x_sh,
     uint16_t* __restrict__ out, int64_t o_sb, int64_t o_ss, int64_t o_sh,
     const float* __restrict__ cosp, const float* __restrict__ sinp, int64_t cs_b,
     const float* __restrict__ w, int64_t S, int64_t H, int64_t total_rows, float eps) {
+  // 16 lanes per (token, head) row, 8 values (4 pairs) per lane; each half-warp
+  // handles R rows spaced 16 apart so the block's loads stay contiguous and
+  // every thread has R independent loads in flight.
   const int lane = threadIdx.x & 31;
   const int sub = lane & 15;
-  const int64_t rowg = (int64_t)blockIdx.x * (blockDim.x / 16) + (threadIdx.x >> 4);
-  const bool valid = rowg < total_rows;
-  const int64_t rr = valid ? rowg : 0;
-  const int64_t h = rr % H;
-  const int64_t t = rr / H;
-  const int64_t s = t % S;
-  const int64_t b = t / S;
-  float v[8];
-  load_bf16x8(x + b * x_sb + s * x_ss + h * x_sh + sub * 8, v);
+  const int hw = threadIdx.x >> 4;
+  const int64_t base = (int64_t)blockIdx.x * (16 * R);
+  float v[R][8];
+  float4 c4[R], s4[R];
+  int64_t oo[R];
+  bool ok[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int64_t rowg = base + r * 16 + hw;
+    ok[r] = rowg < total_rows;
+    const int64_t rr = ok[r] ? rowg : 0;
+    const int64_t h = rr % H;
+    const int64_t t = rr / H;
+    const int64_t s = t % S;
+    const int64_t b = t / S;
+    load_bf16x8(x + b * x_sb + s * x_ss + h * x_sh + sub * 8, v[r]);
+    c4[r] = __ldg(reinterpret_cast<const float4*>(cosp + b * cs_b + s * 64 + sub * 4));
+    s4[r] = __ldg(reinterpret_cast<const float4*>(sinp + b * cs_b + s * 64 + sub * 4));
+    oo[r] = b * o_sb + s * o_ss + h * o_sh + sub * 8;
+  }
+  float wv[8];
   if (NORM) {
-    double ss = 0.0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss += (double)(v[j] * v[j]);
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-    const float rstd = rstd_from_sum(ss, 128, eps);
-    float4 wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
-    float4 wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
-    const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = bf16_round(__fmul_rn(bf16_round(__fmul_rn(v[j], rstd)), wv[j]));
+    const float4 wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
+    const float4 wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
+    wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
+    wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
   }
-  const float4 c4 = __ldg(reinterpret_cast<const float4*>(cosp + b * cs_b + s * 64 + sub * 4));
-  const float4 s4 = __ldg(reinterpret_cast<const float4*>(sinp + b * cs_b + s * 64 + sub * 4));
-  const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
-  const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float a = v[2 * k], bb = v[2 * k + 1];
-    v[2 * k] = bf16_round(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(bb, sv[k])));
-    v[2 * k + 1] = bf16_round(__fadd_rn(__fmul_rn(bb, cv[k]), __fmul_rn(a, sv[k])));
+  for (int r = 0; r < R; ++r) {
+    if (NORM) {
+      double ss = 0.0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += (double)(v[r][j] * v[r][j]);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+      const float rstd = rstd_from_sum(ss, 128, eps);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[r][j] = bf16_round(__fmul_rn(bf16_round(__fmul_rn(v[r][j], rstd)), wv[j]));
+    }
+    const float cv[4] = {c4[r].x, c4[r].y, c4[r].z, c4[r].w};
+    const float sv[4] = {s4[r].x, s4[r].y, s4[r].z, s4[r].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float a = v[r][2 * k], bb = v[r][2 * k + 1];
+      v[r][2 * k] = bf16_round(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(bb, sv[k])));
+      v[r][2 * k + 1] = bf16_round(__fadd_rn(__fmul_rn(bb, cv[k]), __fmul_rn(a, sv[k])));
+    }
+    if (ok[r]) store_bf16x8(out + oo[r], v[r]);
   }
-  if (valid) store_bf16x8(out + b * o_sb + s * o_ss + h * o_sh + sub * 8, v);
 }
 
 // ---------------------------------------------------------------------------
@@ -484,6 +505,582 @@ static inline bool row_launch(int64_t nchunks, RowLaunch* l) {
 
 static inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
+// ===========================================================================
+// v3: persistent row pipeline, few warps per row
+//
+// A CTA of 32*W threads (W = 1, 2 or 4 warps) owns one row at a time and
+// streams its rows (blockIdx.x, blockIdx.x + gridDim.x, ...) through a 2-3
+// stage shared-memory ring filled by 1-D bulk async copies (thread 0 keeps the
+// next rows in flight).  Each thread walks many 8-element chunks of the row
+// (chunk c = tid + k*32W, so a 128-element Hadamard group always sits in 16
+// consecutive lanes); intermediate results that must wait for a row statistic
+// (RMS, absmax) are written back into the ring slot as bf16 and re-read in
+// the next pass, so registers stay small while per-row costs (reductions,
+// rstd/scale divisions, index math) are spread over 30-160 elements per thread.
+// Same arithmetic as the v1 kernels.
+// ===========================================================================
+namespace pipe {
+
+constexpr int kMaxStages = 3;
+
+struct Ring {
+  uint64_t* full;
+  uint8_t* buf;
+  uint32_t row_bytes;
+  uint32_t stage_bytes;
+  int stages;
+};
+
+__device__ __forceinline__ void ring_issue(const Ring& r, int slot, int64_t row, const uint16_t* in0, int64_t ld0,
+                                           const uint16_t* in1, int64_t ld1) {
+  uint64_t* bar = &r.full[slot];
+  mbar_arrive_expect_tx(bar, r.stage_bytes);
+  uint8_t* dst = r.buf + (size_t)slot * r.stage_bytes;
+  bulk_g2s(dst, in0 + row * ld0, r.row_bytes, bar);
+  if (in1) bulk_g2s(dst + r.row_bytes, in1 + row * ld1, r.row_bytes, bar);
+}
+
+struct Driver {
+  Ring ring;
+  int64_t first, stride, my_rows;
+  const uint16_t *in0, *in1;
+  int64_t ld0, ld1;
+  int* abort_s;
+
+  __device__ __forceinline__ int64_t row_of(int64_t i) const { return first + i * stride; }
+
+  __device__ __forceinline__ void prologue() {
+    if (threadIdx.x == 0)
+      for (int j = 0; j < ring.stages - 1 && j < my_rows; ++j) ring_issue(ring, j, row_of(j), in0, ld0, in1, ld1);
+  }
+
+  // Issue row i+S-1 into the slot row i-1 used (every thread finished with it
+  // before the trailing barrier of iteration i-1), then wait for row i.
+  __device__ __forceinline__ bool wait(int64_t i) {
+    const int S = ring.stages;
+    const int slot = (int)(i % S);
+    const uint32_t par = (uint32_t)((i / S) & 1);
+    if (threadIdx.x == 0) {
+      if (i + S - 1 < my_rows) ring_issue(ring, (int)((i + S - 1) % S), row_of(i + S - 1), in0, ld0, in1, ld1);
+      if (!mbar_wait_bounded(&ring.full[slot], par, abort_s)) *abort_s = 1;
+    }
+    __syncthreads();
+    if (*(volatile int*)abort_s) return false;
+    mbar_try_wait(&ring.full[slot], par);  // completed: acquires the bulk-copy writes for this thread
+    return true;
+  }
+
+  __device__ __forceinline__ void drain(int64_t i) {
+    if (threadIdx.x != 0) return;
+    const int S = ring.stages;
+    for (int64_t k = i; k < my_rows && k < i + S; ++k)
+      mbar_drain_wait(&ring.full[k % S], (uint32_t)((k / S) & 1));
+  }
+
+  __device__ __forceinline__ uint16_t* slot_ptr(int64_t i, int which) const {
+    return reinterpret_cast<uint16_t*>(ring.buf + (size_t)(i % ring.stages) * ring.stage_bytes +
+                                       which * ring.row_bytes);
+  }
+};
+
+__device__ __forceinline__ Driver make_driver(uint8_t* smem, uint64_t* full, int* abort_s, int stages, int64_t n,
+                                              int nin, int64_t rows, const uint16_t* in0, int64_t ld0,
+                                              const uint16_t* in1, int64_t ld1) {
+  Driver d;
+  d.ring.full = full;
+  d.ring.buf = smem;
+  d.ring.row_bytes = (uint32_t)(n * 2);
+  d.ring.stage_bytes = (uint32_t)(n * 2 * nin);
+  d.ring.stages = stages;
+  d.first = blockIdx.x;
+  d.stride = gridDim.x;
+  d.my_rows = d.first < rows ? (rows - d.first + d.stride - 1) / d.stride : 0;
+  d.in0 = in0;
+  d.in1 = in1;
+  d.ld0 = ld0;
+  d.ld1 = ld1;
+  d.abort_s = abort_s;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    *abort_s = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  return d;
+}
+
+// --- reductions over the CTA (W warps) -----------------------------------------
+
+template <int W>
+__device__ __forceinline__ float cta_max(float v, float* red) {
+  v = warp_max(v);
+  if (W == 1) return v;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int k = 1; k < W; ++k) r = fmaxf(r, red[k]);
+  __syncthreads();
+  return r;
+}
+
+template <int W>
+__device__ __forceinline__ double cta_sum(double v, double* red) {
+  v = warp_sum_f64(v);
+  if (W == 1) return v;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  double r = red[0];
+#pragma unroll
+  for (int k = 1; k < W; ++k) r += red[k];
+  __syncthreads();
+  return r;
+}
+
+// --- cheap exact roundings ------------------------------------------------------
+
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  uint32_t w = *reinterpret_cast<uint32_t*>(&h);
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xFFFF0000u);
+}
+
+__device__ __forceinline__ void had_round8(float v[8]) {
+  float p[8];
+  bool tie = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    p[j] = __fmul_rn(v[j], kHBf16);
+    tie |= (__float_as_uint(p[j]) & 0xFFFFu) == 0x8000u;
+  }
+  if (__any_sync(0xFFFFFFFFu, tie)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = mul_round_bf16(v[j], kHBf16);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) bf16_round2(p[j], p[j + 1]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = p[j];
+}
+
+__device__ __forceinline__ void quant8(const float v[8], float s, float rcp, int q[8]) {
+  float t[8];
+  bool near = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    t[j] = __fmul_rn(v[j], rcp);
+    near |= ((__float_as_uint(t[j]) & 0xFFFFu) - 0x7FFAu) <= 12u;
+  }
+  if (__any_sync(0xFFFFFFFFu, near)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = quant_i8(v[j], s, rcp);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) bf16_round2(t[j], t[j + 1]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    int i = __float_as_int(__fadd_rn(t[j], 12582912.0f)) - 0x4B400000;  // rint via 1.5*2^23
+    q[j] = max(min(i, 127), -128);
+  }
+}
+
+__device__ __forceinline__ void store_i8x8_prmt(void* p, const int q[8]) {
+  uint32_t a = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+  uint32_t b = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+  *reinterpret_cast<uint2*>(p) = make_uint2(a, b);
+}
+
+__device__ __forceinline__ void fwht128(float v[8], int lane) {
+  fwht8(v);
+#pragma unroll
+  for (int m = 1; m < 16; m <<= 1) {
+    const float sg = (lane & m) ? -1.0f : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float o = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
+      v[i] = __fmaf_rn(sg, v[i], o);
+    }
+  }
+}
+
+// Rotate (optional) the bf16 chunk in place in shared memory and fold its absmax.
+// Every lane of the warp must call this (shuffles), valid or not.
+template <bool HAD>
+__device__ __forceinline__ void rot_chunk_inplace(float v[8], bool valid, uint16_t* sp, float& amax, int lane) {
+  if (HAD) {
+    fwht128(v, lane);
+    had_round8(v);
+    if (valid) store_bf16x8(sp, v);
+  }
+  if (valid) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+  }
+}
+
+// Final pass: quantise the bf16 row held in shared memory.
+template <int W>
+__device__ __forceinline__ void quant_pass(const uint16_t* srow, int64_t nchunks, float amax, int64_t row,
+                                           int8_t* __restrict__ q, int64_t ldq, uint16_t* __restrict__ sx,
+                                           float* red) {
+  amax = cta_max<W>(amax, red);
+  const float s = act_scale(amax);
+  const float rcp = __fdiv_rn(1.0f, s);
+#pragma unroll 2
+  for (int64_t c0 = 0; c0 < nchunks; c0 += 32 * W) {
+    const int64_t c = c0 + threadIdx.x;
+    const bool valid = c < nchunks;
+    float v[8];
+    if (valid) load_bf16x8(srow + c * 8, v);
+    else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+    }
+    int qq[8];
+    quant8(v, s, rcp, qq);
+    if (valid) store_i8x8_prmt(q + row * ldq + c * 8, qq);
+  }
+  if (threadIdx.x == 0) sx[row] = float_to_bf16_bits(s);
+}
+
+// --- kernels -------------------------------------------------------------------
+
+template <int W, bool HAD>
+__global__ void __launch_bounds__(128) act_quant_pipe(const uint16_t* __restrict__ x, int64_t ldx,
+                                                      int8_t* __restrict__ q, int64_t ldq,
+                                                      uint16_t* __restrict__ sx, int64_t n, int64_t rows,
+                                                      int stages) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full[kMaxStages];
+  __shared__ float red[4];
+  __shared__ int abort_s;
+  Driver d = make_driver(smem, full, &abort_s, stages, n, 1, rows, x, ldx, nullptr, 0);
+  const int64_t nchunks = n / 8;
+  const int lane = threadIdx.x & 31;
+  d.prologue();
+  for (int64_t i = 0; i < d.my_rows; ++i) {
+    if (!d.wait(i)) { d.drain(i); return; }
+    uint16_t* sr = d.slot_ptr(i, 0);
+    float amax = 0.0f;
+#pragma unroll 2
+    for (int64_t c0 = 0; c0 < nchunks; c0 += 32 * W) {
+      const int64_t c = c0 + threadIdx.x;
+      const bool valid = c < nchunks;
+      float v[8];
+      if (valid) load_bf16x8(sr + c * 8, v);
+      else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+      }
+      rot_chunk_inplace<HAD>(v, valid, sr + c * 8, amax, lane);
+    }
+    quant_pass<W>(sr, nchunks, amax, d.row_of(i), q, ldq, sx, red);
+    __syncthreads();
+  }
+}
+
+// MODE 0: rmsnorm -> bf16; 1: rmsnorm*(1+s)(+shift) -> bf16; 2: MODE 1 -> rotate/quant
+template <int W, int MODE, bool HAD>
+__global__ void __launch_bounds__(128) rmsnorm_pipe(const uint16_t* __restrict__ x, int64_t ldx,
+                                                    const float* __restrict__ w, const uint16_t* __restrict__ scale,
+                                                    const uint16_t* __restrict__ shift, int64_t ld_mod,
+                                                    int64_t rows_per_batch, uint16_t* __restrict__ y, int64_t ldy,
+                                                    int8_t* __restrict__ q, int64_t ldq, uint16_t* __restrict__ sx,
+                                                    int64_t n, float eps, int64_t rows, int stages) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full[kMaxStages];
+  __shared__ double redd[4];
+  __shared__ float red[4];
+  __shared__ int abort_s;
+  Driver d = make_driver(smem, full, &abort_s, stages, n, 1, rows, x, ldx, nullptr, 0);
+  const int64_t nchunks = n / 8;
+  const int lane = threadIdx.x & 31;
+  d.prologue();
+  for (int64_t i = 0; i < d.my_rows; ++i) {
+    if (!d.wait(i)) { d.drain(i); return; }
+    const int64_t row = d.row_of(i);
+    uint16_t* sr = d.slot_ptr(i, 0);
+    double ss = 0.0;
+#pragma unroll 2
+    for (int64_t c = threadIdx.x; c < nchunks; c += 32 * W) {
+      float v[8];
+      load_bf16x8(sr + c * 8, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += (double)(v[j] * v[j]);
+    }
+    ss = cta_sum<W>(ss, redd);
+    const float rstd = rstd_from_sum(ss, (int)n, eps);
+    const int64_t b = row / rows_per_batch;
+    float amax = 0.0f;
+#pragma unroll 2
+    for (int64_t c0 = 0; c0 < nchunks; c0 += 32 * W) {
+      const int64_t c = c0 + threadIdx.x;
+      const bool valid = c < nchunks;
+      float v[8];
+      if (valid) {
+        float wv[8];
+        load_bf16x8(sr + c * 8, v);
+        ld_w<true>(w, c, n, wv);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          float a0 = __fmul_rn(v[j], rstd), a1 = __fmul_rn(v[j + 1], rstd);
+          bf16_round2(a0, a1);
+          a0 = __fmul_rn(a0, wv[j]);
+          a1 = __fmul_rn(a1, wv[j + 1]);
+          bf16_round2(a0, a1);
+          v[j] = a0;
+          v[j + 1] = a1;
+        }
+        if (MODE >= 1) {
+          float sv[8];
+          load_bf16x8_nc(scale + b * ld_mod + c * 8, sv);
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            float m0 = __fadd_rn(1.0f, sv[j]), m1 = __fadd_rn(1.0f, sv[j + 1]);
+            bf16_round2(m0, m1);
+            float a0 = __fmul_rn(v[j], m0), a1 = __fmul_rn(v[j + 1], m1);
+            bf16_round2(a0, a1);
+            v[j] = a0;
+            v[j + 1] = a1;
+          }
+          if (shift) {
+            load_bf16x8_nc(shift + b * ld_mod + c * 8, sv);
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              float a0 = __fadd_rn(v[j], sv[j]), a1 = __fadd_rn(v[j + 1], sv[j + 1]);
+              bf16_round2(a0, a1);
+              v[j] = a0;
+              v[j + 1] = a1;
+            }
+          }
+        }
+        if (MODE <= 1) store_bf16x8(y + row * ldy + c * 8, v);
+        else if (!HAD) store_bf16x8(sr + c * 8, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+      }
+      if (MODE == 2) rot_chunk_inplace<HAD>(v, valid, sr + c * 8, amax, lane);
+    }
+    if (MODE == 2) quant_pass<W>(sr, nchunks, amax, row, q, ldq, sx, red);
+    __syncthreads();
+  }
+}
+
+// y = r + g*rmsnorm(x); FUSE: then rmsnorm(y;w2)*(1+s)(+shift) -> rotate/quant
+template <int W, bool FUSE, bool HAD>
+__global__ void __launch_bounds__(128) ngr_pipe(
+    const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ r, int64_t ldr,
+    const uint16_t* __restrict__ gate, int64_t ld_gate, int64_t rows_per_batch, const float* __restrict__ w,
+    uint16_t* __restrict__ y, int64_t ldy, const float* __restrict__ w2, const uint16_t* __restrict__ scale,
+    const uint16_t* __restrict__ shift, int64_t ld_mod, int8_t* __restrict__ q, int64_t ldq,
+    uint16_t* __restrict__ sx, int64_t n, float eps, float eps2, int64_t rows, int stages) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full[kMaxStages];
+  __shared__ double redd[4];
+  __shared__ float red[4];
+  __shared__ int abort_s;
+  Driver d = make_driver(smem, full, &abort_s, stages, n, 1, rows, x, ldx, nullptr, 0);
+  const int64_t nchunks = n / 8;
+  const int lane = threadIdx.x & 31;
+  d.prologue();
+  for (int64_t i = 0; i < d.my_rows; ++i) {
+    if (!d.wait(i)) { d.drain(i); return; }
+    const int64_t row = d.row_of(i);
+    uint16_t* sxr = d.slot_ptr(i, 0);  // x, later overwritten with y
+    const uint16_t* rr = r + row * ldr;  // read once: straight from global
+    const int64_t b = row / rows_per_batch;
+    double ss = 0.0;
+#pragma unroll 2
+    for (int64_t c = threadIdx.x; c < nchunks; c += 32 * W) {
+      float v[8];
+      load_bf16x8(sxr + c * 8, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += (double)(v[j] * v[j]);
+    }
+    ss = cta_sum<W>(ss, redd);
+    const float rstd = rstd_from_sum(ss, (int)n, eps);
+    double ss2 = 0.0;
+#pragma unroll 2
+    for (int64_t c = threadIdx.x; c < nchunks; c += 32 * W) {
+      float v[8], wv[8], gv[8], rv[8];
+      load_bf16x8(sxr + c * 8, v);
+      load_bf16x8_nc(rr + c * 8, rv);
+      ld_w<true>(w, c, n, wv);
+      load_bf16x8_nc(gate + b * ld_gate + c * 8, gv);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        float a0 = __fmul_rn(v[j], rstd), a1 = __fmul_rn(v[j + 1], rstd);
+        bf16_round2(a0, a1);
+        a0 = __fmul_rn(a0, wv[j]);
+        a1 = __fmul_rn(a1, wv[j + 1]);
+        bf16_round2(a0, a1);
+        a0 = __fmul_rn(gv[j], a0);
+        a1 = __fmul_rn(gv[j + 1], a1);
+        bf16_round2(a0, a1);
+        a0 = __fadd_rn(rv[j], a0);
+        a1 = __fadd_rn(rv[j + 1], a1);
+        bf16_round2(a0, a1);
+        v[j] = a0;
+        v[j + 1] = a1;
+        if (FUSE) ss2 += (double)(a0 * a0) + (double)(a1 * a1);
+      }
+      store_bf16x8(y + row * ldy + c * 8, v);
+      if (FUSE) store_bf16x8(sxr + c * 8, v);
+    }
+    if (FUSE) {
+      ss2 = cta_sum<W>(ss2, redd);
+      const float rstd2 = rstd_from_sum(ss2, (int)n, eps2);
+      float amax = 0.0f;
+  #pragma unroll 2
+    for (int64_t c0 = 0; c0 < nchunks; c0 += 32 * W) {
+        const int64_t c = c0 + threadIdx.x;
+        const bool valid = c < nchunks;
+        float v[8];
+        if (valid) {
+          float wv[8], sv[8];
+          load_bf16x8(sxr + c * 8, v);
+          ld_w<true>(w2, c, n, wv);
+          load_bf16x8_nc(scale + b * ld_mod + c * 8, sv);
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            float a0 = __fmul_rn(v[j], rstd2), a1 = __fmul_rn(v[j + 1], rstd2);
+            bf16_round2(a0, a1);
+            a0 = __fmul_rn(a0, wv[j]);
+            a1 = __fmul_rn(a1, wv[j + 1]);
+            bf16_round2(a0, a1);
+            float m0 = __fadd_rn(1.0f, sv[j]), m1 = __fadd_rn(1.0f, sv[j + 1]);
+            bf16_round2(m0, m1);
+            a0 = __fmul_rn(a0, m0);
+            a1 = __fmul_rn(a1, m1);
+            bf16_round2(a0, a1);
+            v[j] = a0;
+            v[j + 1] = a1;
+          }
+          if (shift) {
+            load_bf16x8_nc(shift + b * ld_mod + c * 8, sv);
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              float a0 = __fadd_rn(v[j], sv[j]), a1 = __fadd_rn(v[j + 1], sv[j + 1]);
+              bf16_round2(a0, a1);
+              v[j] = a0;
+              v[j + 1] = a1;
+            }
+          }
+          if (!HAD) store_bf16x8(sxr + c * 8, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+        }
+        rot_chunk_inplace<HAD>(v, valid, sxr + c * 8, amax, lane);
+      }
+      quant_pass<W>(sxr, nchunks, amax, row, q, ldq, sx, red);
+    }
+    __syncthreads();
+  }
+}
+
+// out = bf16(bf16(silu(g)) * u); QUANT: rotate/quant instead of storing out
+template <int W, bool QUANT, bool HAD>
+__global__ void __launch_bounds__(128) swiglu_pipe(const uint16_t* __restrict__ g, int64_t ldg,
+                                                   const uint16_t* __restrict__ u, int64_t ldu,
+                                                   uint16_t* __restrict__ out, int64_t ldo, int8_t* __restrict__ q,
+                                                   int64_t ldq, uint16_t* __restrict__ sx, int64_t n, int64_t rows,
+                                                   int stages) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full[kMaxStages];
+  __shared__ float red[4];
+  __shared__ int abort_s;
+  Driver d = make_driver(smem, full, &abort_s, stages, n, 1, rows, g, ldg, nullptr, 0);
+  const int64_t nchunks = n / 8;
+  const int lane = threadIdx.x & 31;
+  d.prologue();
+  for (int64_t i = 0; i < d.my_rows; ++i) {
+    if (!d.wait(i)) { d.drain(i); return; }
+    const int64_t row = d.row_of(i);
+    uint16_t* sg = d.slot_ptr(i, 0);
+    const uint16_t* su = u + row * ldu;  // read once: straight from global
+    float amax = 0.0f;
+#pragma unroll 2
+    for (int64_t c0 = 0; c0 < nchunks; c0 += 32 * W) {
+      const int64_t c = c0 + threadIdx.x;
+      const bool valid = c < nchunks;
+      float v[8];
+      if (valid) {
+        float gv[8], uv[8];
+        load_bf16x8(sg + c * 8, gv);
+        load_bf16x8_nc(su + c * 8, uv);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          float a0 = __fmul_rn(gv[j], zib_sigmoidf(gv[j])), a1 = __fmul_rn(gv[j + 1], zib_sigmoidf(gv[j + 1]));
+          bf16_round2(a0, a1);
+          a0 = __fmul_rn(a0, uv[j]);
+          a1 = __fmul_rn(a1, uv[j + 1]);
+          bf16_round2(a0, a1);
+          v[j] = a0;
+          v[j + 1] = a1;
+        }
+        if (!QUANT) store_bf16x8(out + row * ldo + c * 8, v);
+        else if (!HAD) store_bf16x8(sg + c * 8, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+      }
+      if (QUANT) rot_chunk_inplace<HAD>(v, valid, sg + c * 8, amax, lane);
+    }
+    if (QUANT) quant_pass<W>(sg, nchunks, amax, row, q, ldq, sx, red);
+    __syncthreads();
+  }
+}
+
+// --- host launch helpers ---------------------------------------------------------
+
+struct PipeCfg {
+  int threads, warps, stages, grid;
+  size_t smem;
+};
+
+static int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// Warps per row (CTA size 32*W): 4 keeps ~40 warps per SM at the Z-Image row lengths.
+static inline int pipe_warps(int64_t) { return 4; }
+
+template <class K>
+static bool pipe_cfg(K kernel, int64_t n, int nin, int64_t rows, int warps, PipeCfg* c) {
+  c->warps = warps;
+  c->threads = 32 * warps;
+  const size_t stage = (size_t)n * 2 * nin;
+  c->stages = stage <= 16 * 1024 ? 3 : 2;
+  c->smem = stage * c->stages;
+  if (c->smem > 160 * 1024) return false;
+  if (c->smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->smem) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, c->threads, c->smem) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    return false;
+  }
+  int64_t g = (int64_t)per_sm * num_sms();
+  c->grid = (int)(g < rows ? g : rows);
+  return true;
+}
+
+}  // namespace pipe
+
 }  // namespace zib
 
 using namespace zib;
@@ -495,6 +1092,23 @@ using namespace zib;
     case 4: { constexpr int CPT = 4; __VA_ARGS__; } break; \
     default: { constexpr int CPT = 8; __VA_ARGS__; } break; \
   }
+
+
+#define ZIB_DISPATCH_W(warps, ...)                                  \
+  switch (warps) {                                                 \
+    case 1: { constexpr int W = 1; __VA_ARGS__; } break;            \
+    case 2: { constexpr int W = 2; __VA_ARGS__; } break;            \
+    default: { constexpr int W = 4; __VA_ARGS__; } break;           \
+  }
+
+#define ZIB_PIPE_TRY(KERNEL, NIN, ROWS, N, ...)                                                 \
+  do {                                                                                         \
+    pipe::PipeCfg pc_;                                                                         \
+    if (pipe::pipe_cfg(KERNEL, (N), (NIN), (ROWS), W, &pc_)) {                                  \
+      KERNEL<<<pc_.grid, pc_.threads, pc_.smem, st>>>(__VA_ARGS__, (ROWS), pc_.stages);        \
+      launched = true;                                                                         \
+    }                                                                                          \
+  } while (0)
 
 #define ZIB_DISPATCH_BOOL(flag, NAME, ...)      \
   if (flag) { constexpr bool NAME = true; __VA_ARGS__; } \
@@ -514,9 +1128,20 @@ extern "C" int zib_act_quant(const void* x, int64_t ldx, void* q, int64_t ldq, v
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(K / 8, &l), ZIB_ERR_TOO_LARGE, "act_quant: K=%lld exceeds 65536", (long long)K);
   cudaStream_t st = (cudaStream_t)stream;
-  ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
-      act_quant_kernel<CPT, HAD><<<(unsigned)M, l.threads, 0, st>>>(
-          (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, K)));
+  if (x_rot) {  // debug output of the rotation: the direct-load kernel writes it
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
+        act_quant_kernel<CPT, HAD><<<(unsigned)M, l.threads, 0, st>>>(
+            (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, K)));
+  } else {
+    bool launched = false;
+    ZIB_DISPATCH_W(pipe::pipe_warps(K), ZIB_DISPATCH_BOOL(hadamard, HAD,
+        ZIB_PIPE_TRY((pipe::act_quant_pipe<W, HAD>), 1, M, K,
+                     (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, K)));
+    if (!launched)
+      ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
+          act_quant_kernel<CPT, HAD><<<(unsigned)M, l.threads, 0, st>>>(
+              (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, nullptr, K)));
+  }
   return zib_check_launch("act_quant");
 }
 
@@ -530,9 +1155,14 @@ extern "C" int zib_rms_norm(const void* x, int64_t ldx, const float* w, void* y,
                  "Cannot launch kernel since n = %lld exceeds the maximum fused size 65536.", (long long)n);
   const bool vec = n % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(y) && aligned16(w);
   cudaStream_t st = (cudaStream_t)stream;
-  ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(vec, VEC,
-      rmsnorm_kernel<CPT, VEC, 0, false><<<(unsigned)rows, l.threads, 0, st>>>(
-          (const uint16_t*)x, ldx, w, nullptr, nullptr, 0, 1, (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps)));
+  bool launched = false;
+  if (vec)
+    ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_PIPE_TRY((pipe::rmsnorm_pipe<W, 0, false>), 1, rows, n,
+        (const uint16_t*)x, ldx, w, nullptr, nullptr, 0, 1, (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps));
+  if (!launched)
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(vec, VEC,
+        rmsnorm_kernel<CPT, VEC, 0, false><<<(unsigned)rows, l.threads, 0, st>>>(
+            (const uint16_t*)x, ldx, w, nullptr, nullptr, 0, 1, (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps)));
   return zib_check_launch("rms_norm");
 }
 
@@ -548,10 +1178,16 @@ extern "C" int zib_rmsnorm_mod(const void* x, int64_t ldx, const float* w, const
   const bool vec = n % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0 && ld_mod % 8 == 0 && aligned16(x) &&
                    aligned16(y) && aligned16(w) && aligned16(scale) && (!shift || aligned16(shift));
   cudaStream_t st = (cudaStream_t)stream;
-  ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(vec, VEC,
-      rmsnorm_kernel<CPT, VEC, 1, false><<<(unsigned)rows, l.threads, 0, st>>>(
-          (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
-          (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps)));
+  bool launched = false;
+  if (vec)
+    ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_PIPE_TRY((pipe::rmsnorm_pipe<W, 1, false>), 1, rows, n,
+        (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
+        (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps));
+  if (!launched)
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(vec, VEC,
+        rmsnorm_kernel<CPT, VEC, 1, false><<<(unsigned)rows, l.threads, 0, st>>>(
+            (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
+            (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps)));
   return zib_check_launch("rmsnorm_mod");
 }
 
@@ -569,10 +1205,16 @@ extern "C" int zib_rmsnorm_mod_quant(const void* x, int64_t ldx, const float* w,
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "rmsnorm_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
-      rmsnorm_kernel<CPT, true, 2, HAD><<<(unsigned)rows, l.threads, 0, st>>>(
+  bool launched = false;
+  ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_DISPATCH_BOOL(hadamard, HAD,
+      ZIB_PIPE_TRY((pipe::rmsnorm_pipe<W, 2, HAD>), 1, rows, n,
           (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
           nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, n, eps)));
+  if (!launched)
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
+        rmsnorm_kernel<CPT, true, 2, HAD><<<(unsigned)rows, l.threads, 0, st>>>(
+            (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
+            nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, n, eps)));
   return zib_check_launch("rmsnorm_mod_quant");
 }
 
@@ -589,10 +1231,16 @@ extern "C" int zib_norm_gate_residual(const void* x, int64_t ldx, const void* r,
   const bool vec = n % 8 == 0 && ldx % 8 == 0 && ldr % 8 == 0 && ldy % 8 == 0 && ld_gate % 8 == 0 &&
                    aligned16(x) && aligned16(r) && aligned16(y) && aligned16(gate) && aligned16(w);
   cudaStream_t st = (cudaStream_t)stream;
-  ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(vec, VEC,
-      norm_gate_residual_kernel<CPT, VEC, false, false><<<(unsigned)rows, l.threads, 0, st>>>(
-          (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch,
-          w, (uint16_t*)y, ldy, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, n, eps, eps)));
+  bool launched = false;
+  if (vec)
+    ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_PIPE_TRY((pipe::ngr_pipe<W, false, false>), 1, rows, n,
+        (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch,
+        w, (uint16_t*)y, ldy, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, n, eps, eps));
+  if (!launched)
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(vec, VEC,
+        norm_gate_residual_kernel<CPT, VEC, false, false><<<(unsigned)rows, l.threads, 0, st>>>(
+            (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch,
+            w, (uint16_t*)y, ldy, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, n, eps, eps)));
   return zib_check_launch("norm_gate_residual");
 }
 
@@ -615,11 +1263,18 @@ extern "C" int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, cons
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "norm_gate_residual_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
-      norm_gate_residual_kernel<CPT, true, true, HAD><<<(unsigned)rows, l.threads, 0, st>>>(
+  bool launched = false;
+  ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_DISPATCH_BOOL(hadamard, HAD,
+      ZIB_PIPE_TRY((pipe::ngr_pipe<W, true, HAD>), 1, rows, n,
           (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch,
           w, (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
           (uint16_t*)sx, n, eps, eps2)));
+  if (!launched)
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
+        norm_gate_residual_kernel<CPT, true, true, HAD><<<(unsigned)rows, l.threads, 0, st>>>(
+            (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch,
+            w, (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
+            (uint16_t*)sx, n, eps, eps2)));
   return zib_check_launch("norm_gate_residual_mod_quant");
 }
 
@@ -634,9 +1289,14 @@ extern "C" int zib_swiglu(const void* gate, int64_t ldg, const void* up, int64_t
   const bool vec = n % 8 == 0 && ldg % 8 == 0 && ldu % 8 == 0 && ldo % 8 == 0 && aligned16(gate) &&
                    aligned16(up) && aligned16(out);
   cudaStream_t st = (cudaStream_t)stream;
-  ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(vec, VEC,
-      swiglu_kernel<CPT, VEC, false, false><<<(unsigned)rows, l.threads, 0, st>>>(
-          (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, (uint16_t*)out, ldo, nullptr, 0, nullptr, n)));
+  bool launched = false;
+  if (vec)
+    ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_PIPE_TRY((pipe::swiglu_pipe<W, false, false>), 1, rows, n,
+        (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, (uint16_t*)out, ldo, nullptr, 0, nullptr, n));
+  if (!launched)
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(vec, VEC,
+        swiglu_kernel<CPT, VEC, false, false><<<(unsigned)rows, l.threads, 0, st>>>(
+            (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, (uint16_t*)out, ldo, nullptr, 0, nullptr, n)));
   return zib_check_launch("swiglu");
 }
 
@@ -652,9 +1312,14 @@ extern "C" int zib_swiglu_quant(const void* gate, int64_t ldg, const void* up, i
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "swiglu_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
-      swiglu_kernel<CPT, true, true, HAD><<<(unsigned)rows, l.threads, 0, st>>>(
+  bool launched = false;
+  ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_DISPATCH_BOOL(hadamard, HAD,
+      ZIB_PIPE_TRY((pipe::swiglu_pipe<W, true, HAD>), 1, rows, n,
           (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, n)));
+  if (!launched)
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
+        swiglu_kernel<CPT, true, true, HAD><<<(unsigned)rows, l.threads, 0, st>>>(
+            (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, n)));
   return zib_check_launch("swiglu_quant");
 }
 
@@ -672,15 +1337,16 @@ extern "C" int zib_qknorm_rope(const void* x, int64_t x_sb, int64_t x_ss, int64_
                  ZIB_ERR_ALIGNMENT, "qknorm_rope: operands must be 16-byte aligned");
   const int64_t rows = B * S * H;
   if (rows == 0) return ZIB_OK;
-  const int rows_per_block = 16;  // 256 threads
+  constexpr int R = 4;
+  const int rows_per_block = 16 * R;  // 256 threads, 4 rows per half-warp
   const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
   ZIB_HOST_CHECK(blocks < (1ll << 31), ZIB_ERR_TOO_LARGE, "qknorm_rope: too many rows");
   cudaStream_t st = (cudaStream_t)stream;
   if (w) {
-    qknorm_rope_kernel<true><<<(unsigned)blocks, 256, 0, st>>>(
+    qknorm_rope_kernel<true, R><<<(unsigned)blocks, 256, 0, st>>>(
         (const uint16_t*)x, x_sb, x_ss, x_sh, (uint16_t*)out, o_sb, o_ss, o_sh, cosp, sinp, cs_b, w, S, H, rows, eps);
   } else {
-    qknorm_rope_kernel<false><<<(unsigned)blocks, 256, 0, st>>>(
+    qknorm_rope_kernel<false, R><<<(unsigned)blocks, 256, 0, st>>>(
         (const uint16_t*)x, x_sb, x_ss, x_sh, (uint16_t*)out, o_sb, o_ss, o_sh, cosp, sinp, cs_b, w, S, H, rows, eps);
   }
   return zib_check_launch("qknorm_rope");

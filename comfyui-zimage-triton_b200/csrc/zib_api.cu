@@ -40,6 +40,16 @@ extern "C" const char* zib_status_string(int status) {
 
 extern "C" const char* zib_last_error(void) { return g_last_error; }
 
+// per-translation-unit device error words (see zib_async.cuh)
+int zib_err_read_clear_gemm();
+int zib_err_read_clear_rows();
+
+extern "C" int zib_device_error_read_clear(void) {
+  int a = zib_err_read_clear_gemm();
+  int b = zib_err_read_clear_rows();
+  return a ? a : b;
+}
+
 extern "C" int zib_device_check(int dev) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {

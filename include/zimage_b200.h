@@ -86,6 +86,12 @@ ZIB_API int zib_gemm_w8a8_acc_i32(const void* q, int64_t ldq, const void* wq, in
                           void* acc, int64_t ldacc, int64_t M, int64_t N, int64_t K,
                           void* stream);
 
+/* Selects the GEMM tiling for subsequent zib_gemm_w8a8* calls on this process:
+ * 0 = automatic (2-CTA 256x256 tiles with cta_group::2 when M > 128, else
+ * 1-CTA 128x256 tiles), 1 = always 1-CTA, 2 = always 2-CTA.  Results are
+ * bit-identical across variants.  No reference counterpart (tuning knob). */
+ZIB_API int zib_gemm_set_variant(int variant);
+
 /* Offline weight prep: rotate_weight (hadamard.py:47-75) in exact arithmetic
  * rounded to fp32, then _quantize_weight_per_channel (int8_linear.py:67-73).
  * w: bf16 [N,K] stride ldw -> wq int8 [N,K] stride ldq, sw bf16 [N]

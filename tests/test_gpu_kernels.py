@@ -62,9 +62,18 @@ def _rand_i8(shape, seed):
     return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
 
 
+@pytest.fixture(params=[1, 2], ids=["cta1", "cta2"])
+def gemm_variant(request):
+    """Runs a GEMM test with the 1-CTA (128x256) and the 2-CTA cta_group::2 (256x256) tiling."""
+    lib = _lib.load()
+    assert lib.zib_gemm_set_variant(request.param) == 0
+    yield request.param
+    lib.zib_gemm_set_variant(0)
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 256, 128), (7, 40, 32), (200, 300, 160), (257, 513, 384),
                                    (128, 256, 3840), (300, 1024, 10240), (1024, 11520, 3840)])
-def test_gemm_int32_accumulators_bitexact(cuda, M, N, K):
+def test_gemm_int32_accumulators_bitexact(cuda, gemm_variant, M, N, K):
     q = _rand_i8((M, K), 1)
     w = _rand_i8((N, K), 2)
     acc = torch.empty(M, N + (-N) % 4, dtype=torch.int32, device="cuda")
@@ -78,8 +87,9 @@ def test_gemm_int32_accumulators_bitexact(cuda, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K,bias", [(48, 256, 384, True), (129, 300, 256, False),
-                                        (512, 3840, 3840, False), (64, 20480, 3840, True)])
-def test_gemm_dequant_epilogue_bitexact(cuda, M, N, K, bias):
+                                        (512, 3840, 3840, False), (64, 20480, 3840, True),
+                                        (600, 1000, 512, True)])
+def test_gemm_dequant_epilogue_bitexact(cuda, gemm_variant, M, N, K, bias):
     x = seeded_x(M, K, seed=3)
     w = seeded_w(N, K, seed=4)
     wq, sw, _ = ops.weight_prep(w)
