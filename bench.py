@@ -282,13 +282,12 @@ def run_ours(args) -> None:
         with torch.no_grad():
             return model(inp, t_emb, freqs)
 
+    from zimage_b200.shard import gather_images
+
     def gather(out):
-        lat = out[:, : GRID * GRID, :64].contiguous()
-        if world > 1:
-            bufs = [torch.empty_like(lat) for _ in range(world)]
-            dist.all_gather(bufs, lat)
-            return bufs
-        return [lat]
+        # this rank's image (its CFG pair) -> latent-sized slice; one NCCL all_gather of all images
+        lat = out[:, : GRID * GRID, :64].unsqueeze(0).contiguous()
+        return gather_images(lat, world)
 
     for _ in range(args.warmup):
         y = step(x)
