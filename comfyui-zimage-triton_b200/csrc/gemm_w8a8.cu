@@ -4,19 +4,38 @@
 // W8A8+Hadamard linear (src/zimage_triton/quantization/int8_linear.py:133-137):
 //   acc[m,n] = sum_k q[m,k] * wq[n,k]                         (int32, exact)
 //   y[m,n]   = bf16( bf16(acc) * bf16(sx[m] * sw[n]) ) (+ bias[n])
+// and, as fused epilogues, the op that consumes the GEMM output in the block:
+//   SWIGLU  x_rot = rot128( bf16( bf16(silu(g)) * u ) )   g = w1 output, u = w3 output
+//           (swiglu.py:51-58, then int8_linear.py:119-126 for the w2 input)
+//   QKROPE  per-head RMSNorm * w then interleaved RoPE on the Q and K heads of
+//           the QKV output (fused_qknorm_rope.py:85-151), V unchanged.
 //
-// Design (one CTA per SM, persistent over 128x256 output tiles):
-//   warp 0      TMA producer: 128x128 A tile + 256x128 B tile per k-block,
-//               128-byte swizzle, 4-stage shared-memory ring.
+// Design (persistent, warp-specialised, one CTA per SM):
+//   warp 0      TMA producer (128-byte swizzled K-major tiles).
 //   warp 1      owns TMEM (512 columns = two 128x256 int32 accumulators) and
-//               issues tcgen05.mma (M=128, N=256, K=32) from one thread.
-//   warps 2..9  epilogue (two warps per TMEM lane quarter, 128 columns each):
-//               tcgen05.ld 32x32b of the finished accumulator,
-//               dequant + bias + bf16 rounding in registers, global stores;
-//               overlaps the next tile's MMAs (double-buffered TMEM).
+//               issues tcgen05.mma from one thread.
+//   warps 2..9  epilogue: warps w and w+4 read the same 32 accumulator rows
+//               (TMEM lane quarter w%4) and split the 256 columns in halves;
+//               accumulator buffer b is drained while the MMA fills the other.
+//   1-CTA tiles are 128x256 (48 KB stages).  For M > 128 a cluster of two
+//   CTAs (cta_group::2) computes 256x256 tiles: each CTA stages its 128 A rows
+//   and 128 of the B rows (32 KB stages), both CTAs' TMA loads complete on
+//   the leader's barrier, the leader issues M=256 MMAs reading both CTAs'
+//   shared memory, and its commits are multicast to both CTAs.  No TMA load
+//   uses cluster multicast.
+//   The fused epilogues run in two phases.  Phase 1, one thread per
+//   accumulator row: TMEM -> dequant -> SwiGLU (or the row's sum of squares)
+//   -> bf16 into a swizzled shared-memory tile, after which the accumulator
+//   buffer is released to the MMA.  Phase 2, 16 lanes per row with 8 values
+//   each (the row kernels' layout): the 128-point Hadamard transform on
+//   shuffles (SWIGLU) or norm * w + RoPE with coalesced cos/sin (QKROPE), and
+//   coalesced 256-byte row stores.
+//   SWIGLU tiles interleave the two weights in 64-row blocks,
+//   [w1 f0..f0+63 | w3 f0..f0+63 | w1 f0+64..f0+127 | w3 f0+64..f0+127], so each
+//   column half holds gate and up for 64 features.
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records
 // ZIB_ERR_TIMEOUT in a device error word, drains its in-flight TMA loads and
-// MMAs, frees TMEM and exits.  No TMA multicast is used anywhere.
+// MMAs, frees TMEM and exits.
 #include "zib_async.cuh"
 
 #include <cuda.h>
@@ -27,22 +46,60 @@ ZIB_DEFINE_ERROR_READER(zib_err_read_clear_gemm)
 namespace zib {
 namespace gemm {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
+enum Epi : int { EPI_BF16 = 0, EPI_I32 = 1, EPI_SWIGLU = 2, EPI_QKROPE = 3 };
+
 constexpr int BK = 128;  // bytes == int8 elements == one 128-byte swizzle row
-constexpr int STAGES = 4;
+constexpr int BN = 256;  // accumulator columns per tile
 constexpr int UMMA_K = 32;
-constexpr int A_BYTES = BM * BK;
-constexpr int B_BYTES = BN * BK;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int HALF_BYTES = 128 * BK;  // one 128-row operand box
 constexpr int TMEM_COLS = 512;
 constexpr int NUM_THREADS = 320;  // warp 0 TMA, warp 1 MMA/TMEM, warps 2..9 epilogue
 constexpr int EPI_WARPS = 8;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int SW_BOX_BYTES = 64 * BK;          // SWIGLU B box: 64 weight rows
+constexpr int S_STAGE_BYTES = 3 * HALF_BYTES;  // 1-CTA: A 128x128 + B 256x128
+constexpr int P_STAGE_BYTES = 2 * HALF_BYTES;  // 2-CTA pair: A 128x128 + B 128x128 per CTA
+constexpr int MAX_SMEM = 232448;
 
-// instruction descriptor: D=s32, A=B=s8, both K-major, N=256, M=128
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+// Per-epilogue pipeline depth and shared-memory layout (from the 1024-aligned
+// base): [stages][256 B barriers][XBUF bytes of epilogue staging].
+template <int EPI>
+struct Cfg {
+  // SWIGLU: 128 rows x 128 features bf16.  QKROPE: 128 rows x 256 columns bf16 + rstd [128][2].
+  static constexpr int XBUF = EPI == EPI_SWIGLU ? 128 * 256 : (EPI == EPI_QKROPE ? 128 * 512 + 1024 : 0);
+  static constexpr int S_STAGES = EPI == EPI_QKROPE ? 3 : 4;
+  static constexpr int P_STAGES = EPI == EPI_QKROPE ? 4 : 6;
+  static constexpr int S_SMEM = S_STAGES * S_STAGE_BYTES + 1024 + 256 + XBUF;
+  static constexpr int P_SMEM = P_STAGES * P_STAGE_BYTES + 1024 + 256 + XBUF;
+  static_assert(S_SMEM <= MAX_SMEM && P_SMEM <= MAX_SMEM, "shared memory per CTA");
+};
+
+// instruction descriptors: D=s32, A=B=s8, both K-major, N=256, M=128 / 256
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+struct Params {
+  int M, N, K;  // N: output columns (SWIGLU: features)
+  int num_mb, num_nb, num_kb, num_tiles;
+  const uint16_t* sx;
+  const uint16_t* sw;   // per weight row (SWIGLU: w1 scales)
+  const uint16_t* sw2;  // SWIGLU: w3 scales
+  const uint16_t* bias;
+  uint16_t* y;
+  int64_t ldy;
+  int32_t* acc;
+  int64_t ldacc;
+  // QKROPE
+  const float* qn_w;
+  const float* kn_w;
+  float q_eps, k_eps;
+  const float* cosp;
+  const float* sinp;
+  int64_t cs_b;
+  int seq, heads;
+};
+
+// --- PTX wrappers ------------------------------------------------------------
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
@@ -52,19 +109,28 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// K-major operand tile in shared memory written by TMA with 128-byte swizzle:
-// rows of 128 bytes, 8-row core groups 1024 bytes apart (SBO), version 1.
+// K-major operand tile written by TMA with 128-byte swizzle: rows of 128 bytes,
+// 8-row core groups 1024 bytes apart (SBO), descriptor version 1.
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1u << 16;           // leading byte offset (unused with 128B swizzle)
-  d |= (uint64_t)(1024u >> 4) << 32; // stride byte offset
-  d |= (uint64_t)1u << 46;           // descriptor version for tcgen05
-  d |= (uint64_t)2u << 61;           // SWIZZLE_128B
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
   return d;
 }
 
@@ -77,9 +143,27 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b,
       : "memory");
 }
 
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// arrive (when this thread's prior MMAs retire) on `bar` in every CTA of `mask`
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -97,47 +181,134 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-struct Params {
-  int M, N, K;
-  int num_mb, num_nb, num_kb, num_tiles;
-  const uint16_t* sx;
-  const uint16_t* sw;
-  const uint16_t* bias;
-  uint16_t* y;
-  int64_t ldy;
-  int32_t* acc;
-  int64_t ldacc;
-};
+// whole warp, converged: load 32 accumulator columns of this thread's row
+__device__ __forceinline__ void tmem_row32(uint32_t taddr, uint32_t (&r)[32]) {
+  __syncwarp();
+  tmem_ld32(taddr, r);
+  tmem_wait_ld();
+}
 
-// Dequant epilogue of one thread's accumulator row (128-row x 256-column tile
-// in TMEM, this thread = one row): tcgen05.ld 32 columns at a time, then
-// y = bf16(bf16(acc) * bf16(sx*sw)) (+ bias), or the raw int32 accumulators.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// named barrier over the two warps of an epilogue pair (64 threads)
+__device__ __forceinline__ void pair_bar_sync(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+
+// same barrier, returning the AND of `ok` over the 64 threads
+__device__ __forceinline__ int pair_bar_and(int id, int ok) {
+  int out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, 64, q;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(out)
+      : "r"(ok), "r"(id)
+      : "memory");
+  return out;
+}
+
+// --- epilogues -----------------------------------------------------------------
+
 // bf16 round-to-nearest-even on the ALU pipe (finite inputs); keeps the
-// conversion (XU) pipe for the int32 -> fp32 conversions.
+// conversion pipe free for the int32 -> fp32 conversions.
 __device__ __forceinline__ float bf16_rne_alu(float v) {
   uint32_t b = __float_as_uint(v);
   b += 0x7FFFu + ((b >> 16) & 1u);
   return __uint_as_float(b & 0xFFFF0000u);
 }
 
-template <bool ACC_OUT>
-__device__ __forceinline__ void epilogue_rows(const Params& p, uint32_t t_row, int row, int nb, int ch_begin,
-                                              int ch_end) {
+// y = bf16( bf16(acc) * bf16(sx * sw) )   (int8_linear.py:134)
+__device__ __forceinline__ float dequant(uint32_t acc, float sxf, float swf) {
+  const float s = bf16_rne_alu(__fmul_rn(sxf, swf));
+  const float a = bf16_rne_alu(__int2float_rn((int)acc));
+  return bf16_rne_alu(__fmul_rn(a, s));
+}
+
+__device__ __forceinline__ void store_row_bf16(uint16_t* dst, const float* v, int n) {
+#pragma unroll
+  for (int j = 0; j < n; j += 8) store_bf16x8(dst + j, v + j);
+}
+
+// Staging-tile offsets: 16-byte chunk c of tile row r, XOR-swizzled so that
+// 8 consecutive rows writing the same chunk, and 8 consecutive chunks of one
+// row, fall on distinct bank groups.
+__device__ __forceinline__ uint32_t xoff_256(int r, int c) { return (uint32_t)(r * 256 + ((c ^ (r & 15)) << 4)); }
+__device__ __forceinline__ uint32_t xoff_512(int r, int c) { return (uint32_t)(r * 512 + ((c ^ (r & 7)) << 4)); }
+
+struct EpiCtx {
+  uint32_t t_row;  // TMEM address: this warp's lane quarter in the current accumulator buffer
+  int row_base;    // global row of tile row 0 in this CTA
+  int quarter;     // TMEM lane quarter (warp % 4)
+  int half;        // column half (warps 2..5 -> 0, 6..9 -> 1)
+  int lane;
+  int bar_id;      // named barrier of this warp pair
+  uint8_t* xbuf;   // epilogue staging tile
+};
+
+// releases the accumulator buffer: 1-CTA (local barrier) or pair (leader's barrier)
+struct ReleaseLocal {
+  uint64_t* bar;
+  __device__ __forceinline__ void operator()(int lane) const {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+  }
+};
+struct ReleaseLeader {
+  uint32_t bar_cluster;
+  __device__ __forceinline__ void operator()(int lane) const {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(bar_cluster);
+  }
+};
+
+// plain dequant (+bias) or raw int32: this thread's row, columns [128*half, 128*half+128)
+template <int EPI, class Rel>
+__device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
+  const int row = c.row_base + c.quarter * 32 + c.lane;
   const bool row_ok = row < p.M;
   float sxf = 0.0f;
-  if (!ACC_OUT && row_ok) sxf = bf16_bits_to_float(p.sx[row]);
+  if (EPI == EPI_BF16 && row_ok) sxf = bf16_bits_to_float(p.sx[row]);
 #pragma unroll 1
-  for (int ch = ch_begin; ch < ch_end; ++ch) {
+  for (int ch = c.half * 4; ch < c.half * 4 + 4; ++ch) {
     uint32_t r[32];
-    __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it converged
-    tmem_ld32(t_row + (uint32_t)(ch * 32), r);
-    tmem_wait_ld();
+    tmem_row32(c.t_row + (uint32_t)(ch * 32), r);
     const int n0 = nb * BN + ch * 32;
     if (!row_ok || n0 >= p.N) continue;
     const bool full = n0 + 32 <= p.N;
-    if (ACC_OUT) {
+    if (EPI == EPI_I32) {
       int32_t* dst = p.acc + (int64_t)row * p.ldacc + n0;
       if (full && (p.ldacc % 4) == 0) {
 #pragma unroll
@@ -164,41 +335,208 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, uint32_t t_row, i
         }
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-          const float s = bf16_rne_alu(__fmul_rn(sxf, swv[t]));
-          const float a = bf16_rne_alu(__int2float_rn((int)r[j + t]));
-          float v = bf16_rne_alu(__fmul_rn(a, s));
+          float v = dequant(r[j + t], sxf, swv[t]);
           if (p.bias) v = bf16_rne_alu(__fadd_rn(v, bv[t]));
           out[j + t] = v;
         }
       }
       uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
       if (full) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) store_bf16x8(dst + j, out + j);
+        store_row_bf16(dst, out, 32);
       } else {
         for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (uint16_t)(__float_as_uint(out[j]) >> 16);
       }
     }
   }
+  rel(c.lane);
 }
 
-template <bool ACC_OUT>
+// SWIGLU.  Phase 1 (thread = row): column half `half` holds gate (cols 0..63)
+// and up (64..127) of features 128*nb + 64*half + [0, 64); the bf16 SwiGLU
+// values go to the staging tile [128 rows][128 features].  Phase 2 (16 lanes
+// per row): Walsh-Hadamard over the 128 features of a row (index bits 0..2
+// in-thread, 3..6 by xor shuffles, the act_quant kernels' order), times
+// bf16(1/sqrt(128)) correctly rounded, stored to x_rot.
+template <class Rel>
+__device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
+  const int rt = c.quarter * 32 + c.lane;
+  const int row = c.row_base + rt;
+  const float sxf = row < p.M ? bf16_bits_to_float(p.sx[row]) : 0.0f;
+  const int fb = nb * 128 + c.half * 64;
+  const uint32_t tc = c.t_row + (uint32_t)(c.half * 128);
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) {
+    uint32_t rg[16], ru[16];
+    __syncwarp();
+    tmem_ld16(tc + (uint32_t)(g * 16), rg);
+    tmem_ld16(tc + (uint32_t)(64 + g * 16), ru);
+    tmem_wait_ld();
+    float s1[16], s3[16], v[16];
+    load_bf16x8_nc(p.sw + fb + g * 16, s1);
+    load_bf16x8_nc(p.sw + fb + g * 16 + 8, s1 + 8);
+    load_bf16x8_nc(p.sw2 + fb + g * 16, s3);
+    load_bf16x8_nc(p.sw2 + fb + g * 16 + 8, s3 + 8);
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const float gv = dequant(rg[t], sxf, s1[t]);
+      const float uv = dequant(ru[t], sxf, s3[t]);
+      const float sl = bf16_rne_alu(__fmul_rn(gv, zib_sigmoidf(gv)));
+      v[t] = bf16_rne_alu(__fmul_rn(sl, uv));
+    }
+    const int ch = c.half * 8 + g * 2;
+    store_bf16x8(c.xbuf + xoff_256(rt, ch), v);
+    store_bf16x8(c.xbuf + xoff_256(rt, ch + 1), v + 8);
+  }
+  rel(c.lane);  // accumulator read: the MMA may refill this buffer
+  pair_bar_sync(c.bar_id);
+  const int sub = c.lane & 15;
+#pragma unroll 2
+  for (int it = 0; it < 8; ++it) {
+    const int r2 = c.quarter * 32 + c.half * 16 + it * 2 + (c.lane >> 4);
+    float v[8];
+    load_bf16x8(c.xbuf + xoff_256(r2, sub), v);
+    fwht8(v);
+    fwht_cross16(v, c.lane);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = mul_round_bf16(v[j], kHBf16);
+    const int grow = c.row_base + r2;
+    if (grow < p.M) store_bf16x8(p.y + (int64_t)grow * p.ldy + nb * 128 + sub * 8, v);
+  }
+}
+
+// QKROPE: column half `half` is head hb = 2*nb + half of the [Q | K | V]
+// projection (the head count is even, so both halves have the same kind).
+// Phase 1 (thread = row): dequantised head -> staging tile, and the row's
+// rstd from the exact sum of squares.  Phase 2 (16 lanes per row, 8 values
+// each): bf16(bf16(x * rstd) * w), interleaved-pair RoPE, coalesced store.
+template <class Rel>
+__device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
+  const int rt = c.quarter * 32 + c.lane;
+  const int row = c.row_base + rt;
+  const bool row_ok = row < p.M;
+  const float sxf = row_ok ? bf16_bits_to_float(p.sx[row]) : 0.0f;
+  const int n0 = (nb * 2 + c.half) * 128;
+  const int kind = (nb * 2) / p.heads;  // 0 Q, 1 K, 2 V
+  const uint32_t tc = c.t_row + (uint32_t)(c.half * 128);
+  if (kind == 2) {
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t r[32];
+      tmem_row32(tc + (uint32_t)(cc * 32), r);
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        float swv[8];
+        load_bf16x8_nc(p.sw + n0 + cc * 32 + j, swv);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[j + t] = dequant(r[j + t], sxf, swv[t]);
+      }
+      if (row_ok) store_row_bf16(p.y + (int64_t)row * p.ldy + n0 + cc * 32, v, 32);
+    }
+    rel(c.lane);
+    return;
+  }
+  double ss0 = 0.0, ss1 = 0.0;
+#pragma unroll 1
+  for (int cc = 0; cc < 4; ++cc) {
+    uint32_t r[32];
+    tmem_row32(tc + (uint32_t)(cc * 32), r);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float swv[8];
+      load_bf16x8_nc(p.sw + n0 + cc * 32 + j, swv);
+#pragma unroll
+      for (int t = 0; t < 8; t += 2) {
+        v[j + t] = dequant(r[j + t], sxf, swv[t]);
+        v[j + t + 1] = dequant(r[j + t + 1], sxf, swv[t + 1]);
+        ss0 += (double)(v[j + t] * v[j + t]);  // bf16 squares are exact in fp32; the fp64 sum is exact
+        ss1 += (double)(v[j + t + 1] * v[j + t + 1]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) store_bf16x8(c.xbuf + xoff_512(rt, c.half * 16 + cc * 4 + k), v + 8 * k);
+  }
+  rel(c.lane);
+  float* rstd_buf = reinterpret_cast<float*>(c.xbuf + 128 * 512);
+  rstd_buf[rt * 2 + c.half] = rstd_from_sum(ss0 + ss1, 128, kind == 0 ? p.q_eps : p.k_eps);
+  pair_bar_sync(c.bar_id);
+  const int sub = c.lane & 15;
+  const float* w = kind == 0 ? p.qn_w : p.kn_w;
+  const float4 wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
+  const float4 wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
+  const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll 4
+  for (int it = 0; it < 16; ++it) {
+    const int r2 = c.quarter * 32 + it * 2 + (c.lane >> 4);
+    const int grow = c.row_base + r2;
+    const int gr = grow < p.M ? grow : 0;
+    const int64_t bi = gr / p.seq, si = gr % p.seq;
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cosp + bi * p.cs_b + si * 64 + sub * 4));
+    const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sinp + bi * p.cs_b + si * 64 + sub * 4));
+    float v[8];
+    load_bf16x8(c.xbuf + xoff_512(r2, c.half * 16 + sub), v);
+    const float rs = rstd_buf[r2 * 2 + c.half];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = bf16_rne_alu(__fmul_rn(bf16_rne_alu(__fmul_rn(v[j], rs)), wv[j]));
+    const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+    const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float a = v[2 * k], b = v[2 * k + 1];
+      v[2 * k] = bf16_rne_alu(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(b, sv[k])));
+      v[2 * k + 1] = bf16_rne_alu(__fadd_rn(__fmul_rn(b, cv[k]), __fmul_rn(a, sv[k])));
+    }
+    if (grow < p.M) store_bf16x8(p.y + (int64_t)grow * p.ldy + n0 + sub * 8, v);
+  }
+}
+
+template <int EPI, class Rel>
+__device__ __forceinline__ void epilogue_tile(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
+  if (EPI == EPI_SWIGLU) epi_swiglu(p, c, nb, rel);
+  else if (EPI == EPI_QKROPE) epi_qkrope(p, c, nb, rel);
+  else epi_plain<EPI>(p, c, nb, rel);
+}
+
+// Stage the B rows of tile nb for this CTA (`part` 0/1 = which 128 tile
+// columns; the 1-CTA kernel stages both).  Standard tiles: 128 consecutive
+// weight rows.  SWIGLU tiles: 64 rows of w1 then the same 64 rows of w3.
+template <int EPI>
+__device__ __forceinline__ void load_b_part(uint8_t* dst, const CUtensorMap* b0, const CUtensorMap* b1, int nb,
+                                            int part, int kx, uint64_t* bar, uint32_t pair_bar, bool pair) {
+  if (EPI == EPI_SWIGLU) {
+    const int f = nb * 128 + part * 64;
+    if (pair) {
+      tma_load_2d_pair(dst, b0, pair_bar, kx, f);
+      tma_load_2d_pair(dst + SW_BOX_BYTES, b1, pair_bar, kx, f);
+    } else {
+      tma_load_2d(dst, b0, bar, kx, f);
+      tma_load_2d(dst + SW_BOX_BYTES, b1, bar, kx, f);
+    }
+  } else {
+    if (pair) tma_load_2d_pair(dst, b0, pair_bar, kx, nb * 256 + part * 128);
+    else tma_load_2d(dst, b0, bar, kx, nb * 256 + part * 128);
+  }
+}
+
+// --- kernels -------------------------------------------------------------------
+
+template <int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     const Params p) {
+                     const __grid_constant__ CUtensorMap tmap_b2, const Params p) {
+  constexpr int STAGES = Cfg<EPI>::S_STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smem_a = smem;                          // STAGES x A_BYTES
-  uint8_t* smem_b = smem + STAGES * A_BYTES;       // STAGES x B_BYTES
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full_bar = bars;                       // [STAGES]
-  uint64_t* empty_bar = bars + STAGES;             // [STAGES]
-  uint64_t* tfull_bar = bars + 2 * STAGES;         // [2]
-  uint64_t* tempty_bar = bars + 2 * STAGES + 2;    // [2]
-  uint64_t* mma_done_bar = bars + 2 * STAGES + 4;  // [1]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S_STAGE_BYTES);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* tfull_bar = bars + 2 * STAGES;
+  uint64_t* tempty_bar = bars + 2 * STAGES + 2;
+  uint64_t* mma_done_bar = bars + 2 * STAGES + 4;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-
+  uint8_t* xbuf = smem + STAGES * S_STAGE_BYTES + 256;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -213,9 +551,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(mma_done_bar, 1);
     *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (EPI == EPI_SWIGLU) tma_prefetch_desc(&tmap_b2);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -229,40 +568,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
+    if (lane == 0) {  // ---- TMA producer
       int stage = 0;
-      uint32_t phase = 0;
-      uint32_t pend_mask = 0, pend_parity = 0;
+      uint32_t phase = 0, pend_mask = 0, pend_parity = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         const int mb = tile % p.num_mb, nb = tile / p.num_mb;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
-          tma_load_2d(smem_a + stage * A_BYTES, &tmap_a, &full_bar[stage], kb * BK, mb * BM);
-          tma_load_2d(smem_b + stage * B_BYTES, &tmap_b, &full_bar[stage], kb * BK, nb * BN);
+          uint8_t* st = smem + stage * S_STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], S_STAGE_BYTES);
+          tma_load_2d(st, &tmap_a, &full_bar[stage], kb * BK, mb * 128);
+          load_b_part<EPI>(st + HALF_BYTES, &tmap_b, &tmap_b2, nb, 0, kb * BK, &full_bar[stage], 0, false);
+          load_b_part<EPI>(st + 2 * HALF_BYTES, &tmap_b, &tmap_b2, nb, 1, kb * BK, &full_bar[stage], 0, false);
           pend_mask |= 1u << stage;
           pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
-      if (!ok) {
-        // drain: every stage has at most one load in flight; wait for it to land
+      if (!ok)
         for (int s = 0; s < STAGES; ++s)
           if (pend_mask & (1u << s)) mbar_drain_wait(&full_bar[s], (pend_parity >> s) & 1u);
-      }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int accb = 0;
-      uint32_t acc_phase = 0;
+    if (lane == 0) {  // ---- MMA issuer
+      int stage = 0, accb = 0;
+      uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      const uint32_t a_base = smem_u32(smem_a), b_base = smem_u32(smem_b);
+      const uint32_t base = smem_u32(smem);
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         if (!mbar_wait_bounded(&tempty_bar[accb], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
@@ -270,15 +604,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t adesc = sdesc_sw128(a_base + stage * A_BYTES);
-          const uint64_t bdesc = sdesc_sw128(b_base + stage * B_BYTES);
+          const uint64_t adesc = sdesc_sw128(base + stage * S_STAGE_BYTES);
+          const uint64_t bdesc = sdesc_sw128(base + stage * S_STAGE_BYTES + HALF_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            // advance the start address by k*32 bytes inside the swizzle atom
-            umma_i8(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4), kIdesc,
-                    (kb | k) != 0 ? 1u : 0u);
-          }
-          umma_commit(&empty_bar[stage]);  // frees the smem stage once these MMAs retire
+          for (int k = 0; k < BK / UMMA_K; ++k)
+            umma_i8(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4),
+                    idesc_i8(128, 256), (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
@@ -286,30 +618,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         accb ^= 1;
         if (accb == 0) acc_phase ^= 1u;
       }
-      // all MMAs issued by this thread retire before TMEM is released
       umma_commit(mma_done_bar);
       mbar_drain_wait(mma_done_bar, 0);
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..9) ----------------
-    // warp w reads TMEM lanes [32*(w%4), +32); warps w and w+4 split the 256 columns
-    const int quarter = warp & 3;
+    // ---- epilogue: warps w and w+4 share TMEM lane quarter w%4 and split the columns
     const int half = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int bar_id = 1 + ((warp - 2) & 3);
     int accb = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       int ok = 1;
       if (lane == 0) ok = mbar_wait_bounded(&tfull_bar[accb], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = pair_bar_and(bar_id, ok);  // the pair agrees
       if (!ok) break;
       tc_fence_after();
       const int mb = tile % p.num_mb, nb = tile / p.num_mb;
-      epilogue_rows<ACC_OUT>(p, tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN),
-                             mb * BM + quarter * 32 + lane, nb, half * 4, half * 4 + 4);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[accb]);
+      const EpiCtx c{tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN), mb * 128, quarter,
+                     half, lane, bar_id, xbuf};
+      epilogue_tile<EPI>(p, c, nb, ReleaseLocal{&tempty_bar[accb]});
       accb ^= 1;
       if (accb == 0) acc_phase ^= 1u;
     }
@@ -318,97 +648,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) {
+  if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                  : "memory");
-  }
 }
 
-// ---------------------------------------------------------------------------
-// 2-CTA variant (cta_group::2).  A cluster of two CTAs on two SMs computes a
-// 256x256 output tile: each CTA stages its own 128 rows of A and 128 of the
-// tile's 256 B rows (32 KB per 128-deep k-block, 6 stages), both CTAs' TMA
-// loads complete on the leader's full barrier, the leader CTA issues
-// M=256 x N=256 x K=32 MMAs that read both CTAs' shared memory, and each CTA's
-// TMEM receives its 128 accumulator rows.  Per SM this halves the B traffic
-// through shared memory relative to the 1-CTA 128x256 tile.  TMA loads carry
-// .cta_group::2 only; no load uses cluster multicast.  The leader's MMA
-// commits are multicast to both CTAs' barriers (tcgen05.commit), and both
-// CTAs' epilogue warps release an accumulator on the leader's barrier.
-// ---------------------------------------------------------------------------
-constexpr int P_STAGES = 6;
-constexpr int P_A_BYTES = 128 * BK;
-constexpr int P_B_BYTES = 128 * BK;
-constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
-// D=s32, A=B=s8, K-major, N=256, M=256
-constexpr uint32_t kIdescPair = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
-                                ((uint32_t)(256 >> 4) << 24);
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t mapa_rank(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int x,
-                                                 int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
-      "%4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar_cluster), "r"(x), "r"(y)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-// Arrive (when all prior MMAs of this thread retire) on `bar` in every CTA of `mask`.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(mask)
-      : "memory");
-}
-
-template <bool ACC_OUT>
+template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                          const Params p) {
+                          const __grid_constant__ CUtensorMap tmap_b2, const Params p) {
+  constexpr int STAGES = Cfg<EPI>::P_STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smem_a = smem;
-  uint8_t* smem_b = smem + P_STAGES * P_A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
-  uint64_t* full_bar = bars;                          // [P_STAGES]  (leader's is used)
-  uint64_t* empty_bar = bars + P_STAGES;              // [P_STAGES]  (both)
-  uint64_t* tfull_bar = bars + 2 * P_STAGES;          // [2]         (both)
-  uint64_t* tempty_bar = bars + 2 * P_STAGES + 2;     // [2]         (leader's is used)
-  uint64_t* mma_done_bar = bars + 2 * P_STAGES + 4;   // [1]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 5);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * P_STAGE_BYTES);
+  uint64_t* full_bar = bars;                     // leader's is used
+  uint64_t* empty_bar = bars + STAGES;           // both
+  uint64_t* tfull_bar = bars + 2 * STAGES;       // both
+  uint64_t* tempty_bar = bars + 2 * STAGES + 2;  // leader's is used
+  uint64_t* mma_done_bar = bars + 2 * STAGES + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-
+  uint8_t* xbuf = smem + STAGES * P_STAGE_BYTES + 256;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -417,7 +677,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const int nclusters = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
@@ -430,6 +690,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     mbar_fence_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (EPI == EPI_SWIGLU) tma_prefetch_desc(&tmap_b2);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -445,11 +706,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   bool aborted = false;
 
   if (warp == 0) {
-    // ---------------- TMA producer (both CTAs) ----------------
-    if (lane == 0) {
+    if (lane == 0) {  // ---- TMA producer (both CTAs)
       int stage = 0;
-      uint32_t phase = 0;
-      uint32_t pend_mask = 0, pend_parity = 0;
+      uint32_t phase = 0, pend_mask = 0, pend_parity = 0;
       bool ok = true;
       for (int tile = cluster_id; tile < p.num_tiles && ok; tile += nclusters) {
         const int mb = tile % p.num_mb, nb = tile / p.num_mb;
@@ -458,31 +717,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           const uint32_t fb = smem_u32(&full_bar[stage]);
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * P_STAGE_BYTES);
           const uint32_t fb_leader = leader ? fb : mapa_rank(fb, 0);
-          tma_load_2d_pair(smem_a + stage * P_A_BYTES, &tmap_a, fb_leader, kb * BK, mb * 256 + (int)rank * 128);
-          tma_load_2d_pair(smem_b + stage * P_B_BYTES, &tmap_b, fb_leader, kb * BK, nb * 256 + (int)rank * 128);
+          uint8_t* st = smem + stage * P_STAGE_BYTES;
+          tma_load_2d_pair(st, &tmap_a, fb_leader, kb * BK, mb * 256 + (int)rank * 128);
+          load_b_part<EPI>(st + HALF_BYTES, &tmap_b, &tmap_b2, nb, (int)rank, kb * BK, nullptr, fb_leader, true);
           pend_mask |= 1u << stage;
           pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
       if (!ok) {
         aborted = true;
-        if (leader) {
-          for (int s = 0; s < P_STAGES; ++s)
+        if (leader)
+          for (int s = 0; s < STAGES; ++s)
             if (pend_mask & (1u << s)) mbar_drain_wait(&full_bar[s], (pend_parity >> s) & 1u);
-        }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer (leader CTA only) ----------------
-    if (lane == 0 && leader) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int accb = 0;
-      uint32_t acc_phase = 0;
+    if (lane == 0 && leader) {  // ---- MMA issuer (leader CTA only)
+      int stage = 0, accb = 0;
+      uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      const uint32_t a_base = smem_u32(smem_a), b_base = smem_u32(smem_b);
+      const uint32_t base = smem_u32(smem);
       for (int tile = cluster_id; tile < p.num_tiles && ok; tile += nclusters) {
         if (!mbar_wait_bounded(&tempty_bar[accb], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
@@ -490,15 +746,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t adesc = sdesc_sw128(a_base + stage * P_A_BYTES);
-          const uint64_t bdesc = sdesc_sw128(b_base + stage * P_B_BYTES);
+          const uint64_t adesc = sdesc_sw128(base + stage * P_STAGE_BYTES);
+          const uint64_t bdesc = sdesc_sw128(base + stage * P_STAGE_BYTES + HALF_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
+          for (int k = 0; k < BK / UMMA_K; ++k)
             umma_i8_pair(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4),
-                         kIdescPair, (kb | k) != 0 ? 1u : 0u);
-          }
+                         idesc_i8(256, 256), (kb | k) != 0 ? 1u : 0u);
           umma_commit_pair(&empty_bar[stage], (uint16_t)3);  // frees the stage in both CTAs
-          if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
         umma_commit_pair(&tfull_bar[accb], (uint16_t)3);
@@ -511,24 +766,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
-    const int quarter = warp & 3;
+    // ---- epilogue (both CTAs): warps w and w+4 share lane quarter w%4, split the columns
     const int half = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int bar_id = 1 + ((warp - 2) & 3);
     int accb = 0;
     uint32_t acc_phase = 0;
-    const uint32_t tempty_leader0 = mapa_rank(smem_u32(&tempty_bar[0]), 0);
     for (int tile = cluster_id; tile < p.num_tiles; tile += nclusters) {
       int ok = 1;
       if (lane == 0) ok = mbar_wait_bounded(&tfull_bar[accb], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = pair_bar_and(bar_id, ok);  // the pair agrees
       if (!ok) { aborted = true; break; }
       tc_fence_after();
       const int mb = tile % p.num_mb, nb = tile / p.num_mb;
-      epilogue_rows<ACC_OUT>(p, tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN),
-                             mb * 256 + (int)rank * 128 + quarter * 32 + lane, nb, half * 4, half * 4 + 4);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + (uint32_t)(accb * 8));
+      const EpiCtx c{tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN),
+                     mb * 256 + (int)rank * 128, quarter, half, lane, bar_id, xbuf};
+      epilogue_tile<EPI>(p, c, nb, ReleaseLeader{mapa_rank(smem_u32(&tempty_bar[accb]), 0)});
       accb ^= 1;
       if (accb == 0) acc_phase ^= 1u;
     }
@@ -544,10 +798,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   tc_fence_before();
   cluster_sync_all();  // both CTAs are done with TMEM and with each other's barriers
   tc_fence_after();
-  if (warp == 1) {
+  if (warp == 1)
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                  : "memory");
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -570,8 +823,9 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+// int8 [outer, inner] row-major with row stride ld_bytes, boxes of 128 bytes x box_rows, 128B swizzle
 static int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld_bytes,
-                    int box_inner, int box_outer) {
+                    uint32_t box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) {
     zib_set_error("gemm_w8a8: cuTensorMapEncodeTiled unavailable");
@@ -579,7 +833,7 @@ static int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t o
   }
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
-  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -607,97 +861,157 @@ static int num_sms_for_current_device() {
   return cached[dev];
 }
 
-template <bool ACC_OUT>
-static int launch(const void* q, int64_t ldq, const void* wq, int64_t ldw, const void* sx, const void* sw,
-                  const void* bias, void* y, int64_t ldy, void* acc, int64_t ldacc, int64_t M, int64_t N, int64_t K,
-                  void* stream) {
-  ZIB_HOST_CHECK(q && wq, ZIB_ERR_INVALID_ARG, "gemm_w8a8: null operand");
-  ZIB_HOST_CHECK(M >= 0 && N > 0 && K > 0, ZIB_ERR_INVALID_ARG, "gemm_w8a8: bad shape M=%lld N=%lld K=%lld",
-                 (long long)M, (long long)N, (long long)K);
-  ZIB_HOST_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), ZIB_ERR_TOO_LARGE, "gemm_w8a8: too large");
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+// Common checks + tensor maps + launch.  w2 is the second B operand (SWIGLU: w3).
+template <int EPI>
+static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int64_t ldw, int64_t w_rows, Params p,
+                  void* stream, const char* what) {
+  const int64_t M = p.M, K = p.K;
+  ZIB_HOST_CHECK(q && w && (EPI != EPI_SWIGLU || w2), ZIB_ERR_INVALID_ARG, "%s: null operand", what);
+  ZIB_HOST_CHECK(M >= 0 && p.N > 0 && K > 0, ZIB_ERR_INVALID_ARG, "%s: bad shape M=%d N=%d K=%d", what, p.M, p.N,
+                 p.K);
   ZIB_HOST_CHECK(K % 16 == 0 && ldq >= K && ldw >= K && ldq % 16 == 0 && ldw % 16 == 0, ZIB_ERR_ALIGNMENT,
-                 "gemm_w8a8: K and row strides of q/wq must be multiples of 16 (K=%lld)", (long long)K);
-  ZIB_HOST_CHECK(((uintptr_t)q & 15) == 0 && ((uintptr_t)wq & 15) == 0, ZIB_ERR_ALIGNMENT,
-                 "gemm_w8a8: q/wq must be 16-byte aligned");
-  if (ACC_OUT) {
-    ZIB_HOST_CHECK(acc && ldacc >= N, ZIB_ERR_INVALID_ARG, "gemm_w8a8_acc_i32: bad output");
-    ZIB_HOST_CHECK(((uintptr_t)acc & 15) == 0, ZIB_ERR_ALIGNMENT, "gemm_w8a8_acc_i32: acc must be 16-byte aligned");
-  } else {
-    ZIB_HOST_CHECK(sx && sw && y && ldy >= N, ZIB_ERR_INVALID_ARG, "gemm_w8a8: bad epilogue operands");
-    ZIB_HOST_CHECK(ldy % 8 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)sw & 15) == 0 &&
-                       (!bias || ((uintptr_t)bias & 15) == 0),
-                   ZIB_ERR_ALIGNMENT, "gemm_w8a8: y/sw/bias must be 16-byte aligned and ldy %% 8 == 0");
-  }
+                 "%s: K and row strides of q/w must be multiples of 16 (K=%lld)", what, (long long)K);
+  ZIB_HOST_CHECK(aligned16(q) && aligned16(w) && (!w2 || aligned16(w2)), ZIB_ERR_ALIGNMENT,
+                 "%s: q/w must be 16-byte aligned", what);
   if (M == 0) return ZIB_OK;
-  CUtensorMap ta, tb;
-  int st = make_map(&ta, q, K, M, ldq, BK, BM);
+  CUtensorMap ta, tb, tb2;
+  const uint32_t b_box = EPI == EPI_SWIGLU ? 64u : 128u;
+  int st = make_map(&ta, q, K, M, ldq, 128u);
   if (st) return st;
-  st = make_map(&tb, wq, K, N, ldw, BK, BN);
+  st = make_map(&tb, w, K, w_rows, ldw, b_box);
+  if (st) return st;
+  st = make_map(&tb2, EPI == EPI_SWIGLU ? w2 : w, K, w_rows, ldw, b_box);
   if (st) return st;
 
-  Params p;
-  p.M = (int)M;
-  p.N = (int)N;
-  p.K = (int)K;
-  p.num_mb = (int)((M + BM - 1) / BM);
-  p.num_nb = (int)((N + BN - 1) / BN);
+  const int cols_per_tile = EPI == EPI_SWIGLU ? 128 : BN;  // output columns per tile
+  p.num_nb = (p.N + cols_per_tile - 1) / cols_per_tile;
   p.num_kb = (int)((K + BK - 1) / BK);
-  p.num_tiles = p.num_mb * p.num_nb;
-  p.sx = (const uint16_t*)sx;
-  p.sw = (const uint16_t*)sw;
-  p.bias = (const uint16_t*)bias;
-  p.y = (uint16_t*)y;
-  p.ldy = ldy;
-  p.acc = (int32_t*)acc;
-  p.ldacc = ldacc;
-
   const int variant = g_gemm_variant;
   const bool pair = variant == 2 || (variant == 0 && M > 128);
-  static bool attr_set[2][2][64] = {{{false}}};
+  const int smem_bytes = pair ? Cfg<EPI>::P_SMEM : Cfg<EPI>::S_SMEM;
+  static bool attr_set[2][4][64] = {{{false}}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[pair][ACC_OUT][dev]) {
-    cudaError_t e = pair ? cudaFuncSetAttribute(gemm_w8a8_pair_kernel<ACC_OUT>,
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES)
-                         : cudaFuncSetAttribute(gemm_w8a8_kernel<ACC_OUT>,
-                                                cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (dev >= 0 && dev < 64 && !attr_set[pair][EPI][dev]) {
+    cudaError_t e = pair ? cudaFuncSetAttribute(gemm_w8a8_pair_kernel<EPI>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes)
+                         : cudaFuncSetAttribute(gemm_w8a8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                smem_bytes);
     if (e != cudaSuccess) {
-      zib_set_error("gemm_w8a8: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+      zib_set_error("%s: cudaFuncSetAttribute failed: %s", what, cudaGetErrorString(e));
       return ZIB_ERR_LAUNCH;
     }
-    attr_set[pair][ACC_OUT][dev] = true;
+    attr_set[pair][EPI][dev] = true;
   }
   const int sms = num_sms_for_current_device();
   if (pair) {
-    // B tiles are re-described with 128-row boxes (each CTA stages half of the 256-row tile)
-    st = make_map(&tb, wq, K, N, ldw, BK, 128);
-    if (st) return st;
     p.num_mb = (int)((M + 255) / 256);
     p.num_tiles = p.num_mb * p.num_nb;
     int clusters = sms / 2;
     if (clusters > p.num_tiles) clusters = p.num_tiles;
-    gemm_w8a8_pair_kernel<ACC_OUT><<<2 * clusters, NUM_THREADS, P_SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, p);
+    gemm_w8a8_pair_kernel<EPI><<<2 * clusters, NUM_THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
   } else {
+    p.num_mb = (int)((M + 127) / 128);
+    p.num_tiles = p.num_mb * p.num_nb;
     int grid = sms;
     if (grid > p.num_tiles) grid = p.num_tiles;
-    gemm_w8a8_kernel<ACC_OUT><<<grid, NUM_THREADS, SMEM_BYTES, (cudaStream_t)stream>>>(ta, tb, p);
+    gemm_w8a8_kernel<EPI><<<grid, NUM_THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
   }
-  return zib_check_launch(ACC_OUT ? "gemm_w8a8_acc_i32" : "gemm_w8a8");
+  return zib_check_launch(what);
+}
+
+static Params base_params(int64_t M, int64_t N, int64_t K) {
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  return p;
 }
 
 }  // namespace gemm
 }  // namespace zib
 
+using zib::gemm::aligned16;
+
 extern "C" int zib_gemm_w8a8(const void* q, int64_t ldq, const void* wq, int64_t ldw, const void* sx,
                              const void* sw, const void* bias, void* y, int64_t ldy, int64_t M, int64_t N,
                              int64_t K, void* stream) {
-  return zib::gemm::launch<false>(q, ldq, wq, ldw, sx, sw, bias, y, ldy, nullptr, 0, M, N, K, stream);
+  ZIB_HOST_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), ZIB_ERR_TOO_LARGE, "gemm_w8a8: too large");
+  ZIB_HOST_CHECK(sx && sw && y && ldy >= N, ZIB_ERR_INVALID_ARG, "gemm_w8a8: bad epilogue operands");
+  ZIB_HOST_CHECK(ldy % 8 == 0 && aligned16(y) && aligned16(sw) && (!bias || aligned16(bias)), ZIB_ERR_ALIGNMENT,
+                 "gemm_w8a8: y/sw/bias must be 16-byte aligned and ldy %% 8 == 0");
+  zib::gemm::Params p = zib::gemm::base_params(M, N, K);
+  p.sx = (const uint16_t*)sx;
+  p.sw = (const uint16_t*)sw;
+  p.bias = (const uint16_t*)bias;
+  p.y = (uint16_t*)y;
+  p.ldy = ldy;
+  return zib::gemm::launch<zib::gemm::EPI_BF16>(q, ldq, wq, nullptr, ldw, N, p, stream, "gemm_w8a8");
 }
 
 extern "C" int zib_gemm_w8a8_acc_i32(const void* q, int64_t ldq, const void* wq, int64_t ldw, void* acc,
                                      int64_t ldacc, int64_t M, int64_t N, int64_t K, void* stream) {
-  return zib::gemm::launch<true>(q, ldq, wq, ldw, nullptr, nullptr, nullptr, nullptr, 0, acc, ldacc, M, N, K,
-                                 stream);
+  ZIB_HOST_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), ZIB_ERR_TOO_LARGE,
+                 "gemm_w8a8_acc_i32: too large");
+  ZIB_HOST_CHECK(acc && ldacc >= N, ZIB_ERR_INVALID_ARG, "gemm_w8a8_acc_i32: bad output");
+  ZIB_HOST_CHECK(aligned16(acc), ZIB_ERR_ALIGNMENT, "gemm_w8a8_acc_i32: acc must be 16-byte aligned");
+  zib::gemm::Params p = zib::gemm::base_params(M, N, K);
+  p.acc = (int32_t*)acc;
+  p.ldacc = ldacc;
+  return zib::gemm::launch<zib::gemm::EPI_I32>(q, ldq, wq, nullptr, ldw, N, p, stream, "gemm_w8a8_acc_i32");
+}
+
+extern "C" int zib_gemm_w8a8_swiglu_had(const void* q, int64_t ldq, const void* w1, const void* w3, int64_t ldw,
+                                        const void* sx, const void* sw1, const void* sw3, void* x_rot, int64_t ldo,
+                                        int64_t M, int64_t F, int64_t K, void* stream) {
+  ZIB_HOST_CHECK(M < (1ll << 31) && F < (1ll << 30) && K < (1ll << 31), ZIB_ERR_TOO_LARGE,
+                 "gemm_w8a8_swiglu_had: too large");
+  ZIB_HOST_CHECK(F > 0 && F % 128 == 0, ZIB_ERR_INVALID_ARG,
+                 "gemm_w8a8_swiglu_had: features %lld not divisible by group_size 128", (long long)F);
+  ZIB_HOST_CHECK(sx && sw1 && sw3 && x_rot && ldo >= F, ZIB_ERR_INVALID_ARG, "gemm_w8a8_swiglu_had: bad operands");
+  ZIB_HOST_CHECK(ldo % 8 == 0 && aligned16(x_rot) && aligned16(sw1) && aligned16(sw3), ZIB_ERR_ALIGNMENT,
+                 "gemm_w8a8_swiglu_had: outputs/scales must be 16-byte aligned");
+  zib::gemm::Params p = zib::gemm::base_params(M, F, K);
+  p.sx = (const uint16_t*)sx;
+  p.sw = (const uint16_t*)sw1;
+  p.sw2 = (const uint16_t*)sw3;
+  p.y = (uint16_t*)x_rot;
+  p.ldy = ldo;
+  return zib::gemm::launch<zib::gemm::EPI_SWIGLU>(q, ldq, w1, w3, ldw, F, p, stream, "gemm_w8a8_swiglu_had");
+}
+
+extern "C" int zib_gemm_w8a8_qk_norm_rope(const void* q, int64_t ldq, const void* wq, int64_t ldw, const void* sx,
+                                          const void* sw, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                                          const float* q_norm_w, const float* k_norm_w, float q_eps, float k_eps,
+                                          const float* cosp, const float* sinp, int64_t cs_b, int64_t seq,
+                                          int64_t heads, void* stream) {
+  ZIB_HOST_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), ZIB_ERR_TOO_LARGE,
+                 "gemm_w8a8_qk_norm_rope: too large");
+  ZIB_HOST_CHECK(heads > 0 && heads % 2 == 0 && N == 3 * heads * 128 && seq > 0 && M % seq == 0,
+                 ZIB_ERR_INVALID_ARG,
+                 "gemm_w8a8_qk_norm_rope: needs N = 3*heads*128 with an even head count and M a multiple of seq");
+  ZIB_HOST_CHECK(sx && sw && y && ldy >= N && q_norm_w && k_norm_w && cosp && sinp, ZIB_ERR_INVALID_ARG,
+                 "gemm_w8a8_qk_norm_rope: bad operands");
+  ZIB_HOST_CHECK(ldy % 8 == 0 && aligned16(y) && aligned16(sw) && aligned16(q_norm_w) && aligned16(k_norm_w) &&
+                     aligned16(cosp) && aligned16(sinp) && cs_b % 4 == 0,
+                 ZIB_ERR_ALIGNMENT, "gemm_w8a8_qk_norm_rope: operands must be 16-byte aligned");
+  zib::gemm::Params p = zib::gemm::base_params(M, N, K);
+  p.sx = (const uint16_t*)sx;
+  p.sw = (const uint16_t*)sw;
+  p.y = (uint16_t*)y;
+  p.ldy = ldy;
+  p.qn_w = q_norm_w;
+  p.kn_w = k_norm_w;
+  p.q_eps = q_eps;
+  p.k_eps = k_eps;
+  p.cosp = cosp;
+  p.sinp = sinp;
+  p.cs_b = cs_b;
+  p.seq = (int)seq;
+  p.heads = (int)heads;
+  return zib::gemm::launch<zib::gemm::EPI_QKROPE>(q, ldq, wq, nullptr, ldw, N, p, stream, "gemm_w8a8_qk_norm_rope");
 }
 
 extern "C" int zib_gemm_set_variant(int variant) {

@@ -96,7 +96,11 @@ constexpr float kExpC3 = 1.66666672e-01f;      // 1/3!
 
 __device__ __forceinline__ float zib_expf(float x) {
   x = fminf(fmaxf(x, -87.0f), 88.0f);
-  const float k = rintf(__fmul_rn(x, kInvLn2));
+  // k = rint(x / ln2) by the 1.5*2^23 shifter (round-half-even, |x / ln2| < 2^22);
+  // its integer value is read from the shifted sum's low mantissa bits
+  const float t = __fadd_rn(__fmul_rn(x, kInvLn2), 12582912.0f);
+  const int ki = (int)__float_as_uint(t) - 0x4B400000;
+  const float k = __fsub_rn(t, 12582912.0f);
   float r = __fsub_rn(x, __fmul_rn(k, kLn2Hi));
   r = __fsub_rn(r, __fmul_rn(k, kLn2Lo));
   float p = kExpC7;
@@ -107,12 +111,15 @@ __device__ __forceinline__ float zib_expf(float x) {
   p = __fadd_rn(__fmul_rn(p, r), 0.5f);
   p = __fadd_rn(__fmul_rn(p, r), 1.0f);
   p = __fadd_rn(__fmul_rn(p, r), 1.0f);
-  return ldexpf(p, (int)k);
+  // p * 2^k exactly: for x in [-87, 88], k is in [-126, 127] and p in [0.70, 1.42]
+  // (p >= 1 when k = -126, since x >= -87 > -126 ln2), so the result is a normal
+  // number and adding k to the exponent field equals ldexp
+  return __uint_as_float(__float_as_uint(p) + ((uint32_t)ki << 23));
 }
 
-// sigmoid(g) = 1 / (1 + exp(-g))
+// sigmoid(g) = 1 / (1 + exp(-g)), the correctly rounded reciprocal
 __device__ __forceinline__ float zib_sigmoidf(float g) {
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, zib_expf(-g)));
+  return __frcp_rn(__fadd_rn(1.0f, zib_expf(-g)));
 }
 
 // tanh: odd Taylor polynomial (to x^11) for |x| < 0.25, else (1 - e^-2|x|) / (1 + e^-2|x|)

@@ -150,6 +150,37 @@ def case_gemm(M, N, K):
     return run, 2 * M * N * K, f"{M}x{N}x{K} int8 -> bf16"
 
 
+def case_gemm_swiglu(M, F_, K):
+    q, w1, w3 = _i8(M, K), _i8(F_, K, seed=1), _i8(F_, K, seed=3)
+    sx, s1, s3 = _bf16(M).abs() * 1e-2, _bf16(F_, seed=2).abs() * 1e-3, _bf16(F_, seed=4).abs() * 1e-3
+    y = _empty(M, F_)
+    st = _lib.stream_of(q)
+
+    def run():
+        _lib.call("zib_gemm_w8a8_swiglu_had", q.data_ptr(), K, w1.data_ptr(), w3.data_ptr(), K, sx.data_ptr(),
+                  s1.data_ptr(), s3.data_ptr(), y.data_ptr(), F_, M, F_, K, st)
+
+    return run, 2 * M * 2 * F_ * K, f"{M}x(2x{F_})x{K} int8 -> SwiGLU -> rot128 bf16"
+
+
+def case_gemm_qk_rope(M, K):
+    N = 3 * H * HD
+    q, w = _i8(M, K), _i8(N, K, seed=1)
+    sx, sw = _bf16(M).abs() * 1e-2, _bf16(N, seed=2).abs() * 1e-3
+    qn, kn = torch.ones(HD, device="cuda"), torch.ones(HD, device="cuda")
+    ang = torch.rand(S, HD // 2, device="cuda")
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    y = _empty(M, N)
+    st = _lib.stream_of(q)
+
+    def run():
+        _lib.call("zib_gemm_w8a8_qk_norm_rope", q.data_ptr(), K, w.data_ptr(), K, sx.data_ptr(), sw.data_ptr(),
+                  y.data_ptr(), N, M, N, K, qn.data_ptr(), kn.data_ptr(), 1e-5, 1e-5, cos.data_ptr(),
+                  sin.data_ptr(), 0, S, H, st)
+
+    return run, 2 * M * N * K, f"{M}x{N}x{K} int8 -> QK-norm + RoPE bf16"
+
+
 def case_weight_prep(N=3 * D, K=D):
     w, wq, sw = _bf16(N, K) * 0.02, _empty(N, K, dtype=torch.int8), _empty(N)
     st = _lib.stream_of(w)
@@ -187,6 +218,8 @@ CASES = {
     "gemm_out": (lambda: case_gemm(M_TOK, D, D), "int8"),
     "gemm_w13": (lambda: case_gemm(M_TOK, 2 * F, D), "int8"),
     "gemm_w2": (lambda: case_gemm(M_TOK, D, F), "int8"),
+    "gemm_qkv_qk_rope": (lambda: case_gemm_qk_rope(M_TOK, D), "int8"),
+    "gemm_w13_swiglu_had": (lambda: case_gemm_swiglu(M_TOK, F, D), "int8"),
     "sdpa_torch": (lambda: case_sdpa(), "bf16"),
 }
 

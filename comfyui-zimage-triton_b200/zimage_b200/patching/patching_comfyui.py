@@ -236,14 +236,18 @@ def _f32(w: torch.Tensor) -> torch.Tensor:
 def _block_cache(block: nn.Module):
     """Per-block tensors of the fused path, or None when the block does not qualify.
 
-    w1/w3 int8 weights are concatenated once into one [2F, D] operand and the
-    modules' buffers are re-pointed at views of it (no extra memory).
+    The fused path needs W8A8+Hadamard int8 linears on every projection,
+    128-wide heads and an FFN width divisible by the 128-group of the w2
+    rotation.
     """
     attn, ff = block.attention, block.feed_forward
     lins = (attn.qkv, attn.out, ff.w1, ff.w2, ff.w3)
     if not all(_lin_ok(l) for l in lins):
         return None
     if attn.head_dim != 128 or attn.n_local_heads != attn.n_local_kv_heads:
+        return None
+    F_ = ff.w1._w_int8.shape[0]
+    if F_ % 128 or ff.w3._w_int8.shape[0] != F_:
         return None
     norms = (block.attention_norm1, block.attention_norm2, block.ffn_norm1, block.ffn_norm2,
              attn.q_norm, attn.k_norm)
@@ -254,17 +258,6 @@ def _block_cache(block: nn.Module):
     c = block.__dict__.get("_zib_cache")
     if c is not None and c["key"] == key:
         return c
-    w1, w3 = ff.w1, ff.w3
-    F_ = w1._w_int8.shape[0]
-    if w3._w_int8.data_ptr() == w1._w_int8.data_ptr() + w1._w_int8.numel() and \
-            w3._w_scale.data_ptr() == w1._w_scale.data_ptr() + 2 * F_:
-        w13 = torch.as_strided(w1._w_int8, (2 * F_, w1._w_int8.shape[1]), w1._w_int8.stride())
-        s13 = torch.as_strided(w1._w_scale, (2 * F_,), (1,))
-    else:
-        w13 = torch.cat([w1._w_int8, w3._w_int8], 0)
-        s13 = torch.cat([w1._w_scale, w3._w_scale], 0)
-        w1._buffers["_w_int8"], w3._buffers["_w_int8"] = w13[:F_], w13[F_:]
-        w1._buffers["_w_scale"], w3._buffers["_w_scale"] = s13[:F_], s13[F_:]
     c = {
         "an1": _f32(block.attention_norm1.weight), "an2": _f32(block.attention_norm2.weight),
         "fn1": _f32(block.ffn_norm1.weight), "fn2": _f32(block.ffn_norm2.weight),
@@ -272,10 +265,8 @@ def _block_cache(block: nn.Module):
         "eps_an1": _eps(block.attention_norm1), "eps_an2": _eps(block.attention_norm2),
         "eps_fn1": _eps(block.ffn_norm1), "eps_fn2": _eps(block.ffn_norm2),
         "eps_q": _eps(attn.q_norm), "eps_k": _eps(attn.k_norm),
-        "w13": w13, "s13": s13, "F": F_,
+        "F": F_, "key": key,
     }
-    c["key"] = tuple((n.weight.data_ptr(), n.weight._version) for n in norms) + tuple(
-        (l._w_int8.data_ptr(), l._w_scale.data_ptr()) for l in lins)
     block.__dict__["_zib_cache"] = c
     return c
 
@@ -285,16 +276,20 @@ def _block_cache(block: nn.Module):
 GEMM_EVENTS: list | None = None
 
 
-def _gemm(q8, sx, lin_w, lin_s, y, M, N, K, stream):
+def _timed_call(name: str, ops_count: int, *args) -> None:
     ev = GEMM_EVENTS
     if ev is not None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-    _lib.call("zib_gemm_w8a8", q8.data_ptr(), K, lin_w.data_ptr(), lin_w.stride(0), sx.data_ptr(),
-              lin_s.data_ptr(), None, y.data_ptr(), y.stride(0), M, N, K, stream)
+    _lib.call(name, *args)
     if ev is not None:
         e1.record()
-        ev.append((e0, e1, 2 * M * N * K))
+        ev.append((e0, e1, ops_count))
+
+
+def _gemm(q8, sx, lin_w, lin_s, y, M, N, K, stream):
+    _timed_call("zib_gemm_w8a8", 2 * M * N * K, q8.data_ptr(), K, lin_w.data_ptr(), lin_w.stride(0),
+                sx.data_ptr(), lin_s.data_ptr(), None, y.data_ptr(), y.stride(0), M, N, K, stream)
 
 
 def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freqs_cis: torch.Tensor,
@@ -325,15 +320,21 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
     sx = torch.empty(M, dtype=bf, device=dev)
     _lib.call("zib_rmsnorm_mod_quant", x.data_ptr(), D, c["an1"].data_ptr(), raw.data_ptr(), None, 4 * D, S,
               q8.data_ptr(), D, sx.data_ptr(), M, D, float(c["eps_an1"]), 1, stream)
-    # QKV projection (tcgen05 GEMM)                                       (:180)
+    # QKV projection with per-head Q/K RMSNorm + RoPE in the epilogue     (:180-190)
     nqkv = attn.qkv._w_int8.shape[0]
     qkv = torch.empty(M, nqkv, dtype=bf, device=dev)
-    _gemm(q8, sx, attn.qkv._w_int8, attn.qkv._w_scale, qkv, M, nqkv, D, stream)
     qkv5 = qkv.view(B, S, 3, H, 128)
     xq, xk, xv = qkv5[:, :, 0], qkv5[:, :, 1], qkv5[:, :, 2]
     cos, sin, cs_b = _cos_sin(freqs_cis, B)
-    qknorm_rope_into(xq, xq, c["qn"], cos, sin, cs_b, c["eps_q"])          # :189
-    qknorm_rope_into(xk, xk, c["kn"], cos, sin, cs_b, c["eps_k"])          # :190
+    if H % 2 == 0 and nqkv == 3 * hd:
+        _timed_call("zib_gemm_w8a8_qk_norm_rope", 2 * M * nqkv * D, q8.data_ptr(), D, attn.qkv._w_int8.data_ptr(),
+                    attn.qkv._w_int8.stride(0), sx.data_ptr(), attn.qkv._w_scale.data_ptr(), qkv.data_ptr(), nqkv,
+                    M, nqkv, D, c["qn"].data_ptr(), c["kn"].data_ptr(), float(c["eps_q"]), float(c["eps_k"]),
+                    cos.data_ptr(), sin.data_ptr(), cs_b, S, H, stream)
+    else:  # odd head count: a 256-column tile would straddle two heads
+        _gemm(q8, sx, attn.qkv._w_int8, attn.qkv._w_scale, qkv, M, nqkv, D, stream)
+        qknorm_rope_into(xq, xq, c["qn"], cos, sin, cs_b, c["eps_q"])
+        qknorm_rope_into(xk, xk, c["kn"], cos, sin, cs_b, c["eps_k"])
     o = _attention_bshd(xq, xk, xv, x_mask).reshape(M, hd)                  # :197-205
     # out projection: rotate + quantise + GEMM                            (:207)
     if o.stride(-1) != 1 or o.stride(0) % 8 != 0:
@@ -352,13 +353,14 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
               2 * D, S, c["an2"].data_ptr(), x1.data_ptr(), D, c["fn1"].data_ptr(),
               raw.data_ptr() + 2 * D * esz, None, 4 * D, q8f.data_ptr(), D, sxf.data_ptr(), M, D,
               float(c["eps_an2"]), float(c["eps_fn1"]), 1, stream)
-    # w1 || w3 in one GEMM, then SwiGLU -> rotate -> quantise, then w2
-    h = torch.empty(M, 2 * F_, dtype=bf, device=dev)
-    _gemm(q8f, sxf, c["w13"], c["s13"], h, M, 2 * F_, D, stream)
+    # w1 and w3 GEMMs + SwiGLU + w2-input rotation in one launch, then quantise   (swiglu.py:51-58)
+    x_rot = torch.empty(M, F_, dtype=bf, device=dev)
+    _timed_call("zib_gemm_w8a8_swiglu_had", 2 * M * 2 * F_ * D, q8f.data_ptr(), D, ff.w1._w_int8.data_ptr(),
+                ff.w3._w_int8.data_ptr(), D, sxf.data_ptr(), ff.w1._w_scale.data_ptr(), ff.w3._w_scale.data_ptr(),
+                x_rot.data_ptr(), F_, M, F_, D, stream)
     q8h = torch.empty(M, F_, dtype=i8, device=dev)
     sxh = torch.empty(M, dtype=bf, device=dev)
-    _lib.call("zib_swiglu_quant", h.data_ptr(), 2 * F_, h.data_ptr() + F_ * esz, 2 * F_, q8h.data_ptr(), F_,
-              sxh.data_ptr(), M, F_, 1, stream)
+    _lib.call("zib_act_quant", x_rot.data_ptr(), F_, q8h.data_ptr(), F_, sxh.data_ptr(), None, M, F_, 0, stream)
     ffn_out = torch.empty(M, D, dtype=bf, device=dev)
     _gemm(q8h, sxh, ff.w2._w_int8, ff.w2._w_scale, ffn_out, M, D, F_, stream)
     # x1 + g_mlp * ffn_norm2(ffn_out)                                     (:404-411)

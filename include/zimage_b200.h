@@ -86,6 +86,36 @@ ZIB_API int zib_gemm_w8a8_acc_i32(const void* q, int64_t ldq, const void* wq, in
                           void* acc, int64_t ldacc, int64_t M, int64_t N, int64_t K,
                           void* stream);
 
+/* FFN up-projection with the SwiGLU and the w2-input rotation fused into the
+ * GEMM epilogue.  Replaces, in one launch, the two int8 linears w1/w3
+ * (int8_linear.py:133-137), swiglu_fwd (kernels/swiglu.py:51-58: silu(g)
+ * rounded to bf16, times u, rounded to bf16) and the block-128 Hadamard
+ * rotation of the w2 input (int8_linear.py:119-126, hadamard.py:78-107):
+ *   g = dequant(q.w1^T), u = dequant(q.w3^T)                 (bf16 [M,F])
+ *   x_rot[m, 128j:128j+128] = bf16( H128 . bf16(bf16(silu(g)) * u) ) * bf16(1/sqrt(128))
+ * q: int8 [M,K] stride ldq; w1, w3: int8 [F,K] stride ldw; sx: bf16 [M];
+ * sw1, sw3: bf16 [F]; x_rot: bf16 [M,F] stride ldo.  F % 128 == 0.
+ * x_rot is what zib_act_quant(..., hadamard=0) quantises for w2. */
+ZIB_API int zib_gemm_w8a8_swiglu_had(const void* q, int64_t ldq, const void* w1, const void* w3,
+                             int64_t ldw, const void* sx, const void* sw1, const void* sw3,
+                             void* x_rot, int64_t ldo, int64_t M, int64_t F, int64_t K,
+                             void* stream);
+
+/* QKV projection with the per-head Q/K RMSNorm and the interleaved RoPE fused
+ * into the GEMM epilogue.  Replaces the int8 qkv linear (int8_linear.py:133-137)
+ * followed by fused_qknorm_rope on Q and K (kernels/fused_qknorm_rope.py:85-151).
+ * y: bf16 [M, 3*heads*128] stride ldy holding [Q | K | V] (head_dim 128, rows
+ * are (batch, token) with seq tokens per batch entry), Q and K normalised with
+ * q_norm_w/k_norm_w (fp32 [128], eps q_eps/k_eps) and rotated with the
+ * fp32 cos/sin tables [B][seq][64] (batch stride cs_b, 0 when shared); V is the
+ * plain dequantised projection.  heads even, M % seq == 0. */
+ZIB_API int zib_gemm_w8a8_qk_norm_rope(const void* q, int64_t ldq, const void* wq, int64_t ldw,
+                               const void* sx, const void* sw, void* y, int64_t ldy,
+                               int64_t M, int64_t N, int64_t K,
+                               const float* q_norm_w, const float* k_norm_w, float q_eps,
+                               float k_eps, const float* cos, const float* sin, int64_t cs_b,
+                               int64_t seq, int64_t heads, void* stream);
+
 /* Selects the GEMM tiling for subsequent zib_gemm_w8a8* calls on this process:
  * 0 = automatic (2-CTA 256x256 tiles with cta_group::2 when M > 128, else
  * 1-CTA 128x256 tiles), 1 = always 1-CTA, 2 = always 2-CTA.  Results are

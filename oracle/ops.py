@@ -11,9 +11,12 @@ Rounding conventions (the reference's, made explicit):
   sum (fp64 accumulation, then one rounding).  The reference's Triton
   ``tl.sum`` uses an implementation-defined tree order, so no order is
   canonical; the CUDA kernels use the same exactly-rounded convention.
-* ``rsqrt`` is restated as IEEE ``1 / sqrt(v)`` in fp32.  The reference's
-  libdevice ``rsqrt`` is an approximation; outputs are compared with
-  tolerances for that reason.
+* ``rsqrt`` is restated as IEEE ``1 / sqrt(v)`` in fp32: the correctly
+  rounded square root, then the correctly rounded reciprocal.  Both are
+  formed in fp64 and rounded once to fp32, which is exact for sqrt and
+  division (53 >= 2*24 + 2 bits); torch's own fp32 ``sqrt`` on CPU is not
+  correctly rounded on every input.  The reference's libdevice ``rsqrt`` is an
+  approximation; outputs are compared with tolerances for that reason.
 * The Hadamard rotation of activations is restated as the correctly rounded
   bf16 of the exact product ``h * sum(+-x)`` with ``h = bf16(1/sqrt(128))``.
   The reference computes it as a bf16 matmul (``int8_linear.py:124-126``),
@@ -221,8 +224,9 @@ def rstd_rows(x: torch.Tensor, eps: float) -> torch.Tensor:
     """rsqrt(mean(x^2) + eps) per row in fp32 (exactly-rounded sum, IEEE ops)."""
     n = x.shape[-1]
     ss = (x.double() ** 2).sum(-1, keepdim=True).float()
-    ms = ss / np.float32(n)
-    return 1.0 / torch.sqrt(ms + np.float32(eps))
+    ms = (ss.double() / n).float()
+    sq = torch.sqrt((ms + np.float32(eps)).double()).float()
+    return (1.0 / sq.double()).float()
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:

@@ -106,6 +106,109 @@ def test_gemm_dequant_epilogue_bitexact(cuda, gemm_variant, M, N, K, bias):
     assert torch.equal(y[:, :N].cpu(), want)
 
 
+@pytest.mark.parametrize("M,F,K", [(48, 128, 384), (129, 384, 256), (300, 1280, 3840), (1024, 10240, 3840)])
+def test_gemm_swiglu_hadamard_epilogue(cuda, gemm_variant, M, F, K):
+    """w1/w3 GEMMs + SwiGLU + w2-input rotation in one launch vs the oracle's composition."""
+    x = seeded_x(M, K, seed=13)
+    w1q, sw1, _ = ops.weight_prep(seeded_w(F, K, seed=14))
+    w3q, sw3, _ = ops.weight_prep(seeded_w(F, K, seed=15))
+    q, sx, _ = ops.act_quant_had128(x)
+    out = torch.empty(M, F, dtype=torch.bfloat16, device="cuda")
+    qd, w1d, w3d, sxd, s1d, s3d = (t.cuda() for t in (q, w1q, w3q, sx.flatten(), sw1, sw3))
+    _lib.call("zib_gemm_w8a8_swiglu_had", qd.data_ptr(), K, w1d.data_ptr(), w3d.data_ptr(), K, sxd.data_ptr(),
+              s1d.data_ptr(), s3d.data_ptr(), out.data_ptr(), F, M, F, K, _lib.stream_of(qd))
+    torch.cuda.synchronize()
+    assert _lib.device_error_read_clear() == 0
+    g = ops.dequant_epilogue(ops.gemm_acc_i32(q, w1q), sx, sw1, None)
+    u = ops.dequant_epilogue(ops.gemm_acc_i32(q, w3q), sx, sw3, None)
+    want = ops.rotate_activation_exact(ops.swiglu(g, u))
+    got = out.cpu()
+    # same fp32 Walsh-Hadamard adds as zib_act_quant: bit-exact but for rare inexact fp32 sums,
+    # whose error is a few fp32 ulps of the row's largest partial sum, then one bf16 rounding
+    assert (got != want).float().mean().item() <= 1e-5
+    rowmax = want.float().abs().amax(dim=1, keepdim=True)
+    err = (got.float() - want.float()).abs()
+    assert bool((err <= 2 ** -7 * want.float().abs() + 2 ** -16 * rowmax).all()), float(err.max())
+
+
+def test_gemm_swiglu_matches_composed_kernels(cuda):
+    """Fused epilogue == w1/w3 GEMMs, then the SwiGLU + rotation row kernel (bit-exact)."""
+    M, F, K = 700, 1024, 3840
+    q, sx, _ = ops.act_quant_had128(seeded_x(M, K, seed=21))
+    w1q, sw1, _ = ops.weight_prep(seeded_w(F, K, seed=22))
+    w3q, sw3, _ = ops.weight_prep(seeded_w(F, K, seed=23))
+    qd, sxd = q.cuda(), sx.flatten().cuda()
+    w13, s13 = torch.cat([w1q, w3q]).cuda(), torch.cat([sw1, sw3]).cuda()
+    st = _lib.stream_of(qd)
+    h = torch.empty(M, 2 * F, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_gemm_w8a8", qd.data_ptr(), K, w13.data_ptr(), K, sxd.data_ptr(), s13.data_ptr(), None,
+              h.data_ptr(), 2 * F, M, 2 * F, K, st)
+    q_ref = torch.empty(M, F, dtype=torch.int8, device="cuda")
+    s_ref = torch.empty(M, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_swiglu_quant", h.data_ptr(), 2 * F, h.data_ptr() + 2 * F, 2 * F, q_ref.data_ptr(), F,
+              s_ref.data_ptr(), M, F, 1, st)
+    x_rot = torch.empty(M, F, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_gemm_w8a8_swiglu_had", qd.data_ptr(), K, w13.data_ptr(), w13.data_ptr() + F * K, K,
+              sxd.data_ptr(), s13.data_ptr(), s13.data_ptr() + 2 * F, x_rot.data_ptr(), F, M, F, K, st)
+    q_f = torch.empty(M, F, dtype=torch.int8, device="cuda")
+    s_f = torch.empty(M, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_act_quant", x_rot.data_ptr(), F, q_f.data_ptr(), F, s_f.data_ptr(), None, M, F, 0, st)
+    torch.cuda.synchronize()
+    assert torch.equal(q_f, q_ref) and torch.equal(s_f, s_ref)
+
+
+def test_gemm_swiglu_rejects_ragged_features(cuda):
+    q = torch.zeros(8, 128, dtype=torch.int8, device="cuda")
+    w = torch.zeros(200, 128, dtype=torch.int8, device="cuda")
+    s = torch.ones(256, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(8, 200, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="group_size"):
+        _lib.call("zib_gemm_w8a8_swiglu_had", q.data_ptr(), 128, w.data_ptr(), w.data_ptr(), 128, s.data_ptr(),
+                  s.data_ptr(), s.data_ptr(), out.data_ptr(), 200, 8, 200, 128, _lib.stream_of(q))
+
+
+@pytest.mark.parametrize("B,S,H,fb", [(2, 48, 2, 1), (1, 200, 4, 1), (2, 130, 30, 2)])
+def test_gemm_qk_norm_rope_epilogue_bitexact(cuda, gemm_variant, B, S, H, fb):
+    """QKV GEMM + per-head RMSNorm + RoPE on Q and K in one launch vs GEMM then fused_qknorm_rope."""
+    from zimage_b200.kernels.fused_qknorm_rope import rope_tables
+
+    M, K, N = B * S, 384 if H < 30 else 3840, 3 * H * 128
+    x = seeded_x(M, K, seed=17)
+    wq, sw, _ = ops.weight_prep(seeded_w(N, K, seed=18))
+    q, sx, _ = ops.act_quant_had128(x)
+    qw, kw = _norm_w(128, 19), _norm_w(128, 20)
+    pos = ops.zimage_positions(8, 8, S)[:S]
+    fc = ops.rope_freqs_complex(pos).unsqueeze(0).expand(fb, -1, -1).contiguous()
+    if fb == 2:
+        fc[1] = fc[1].conj()  # a different table per batch entry
+    cos, sin, cs_b = rope_tables(fc.cuda(), B)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    qd, wd, sxd, swd = q.cuda(), wq.cuda(), sx.flatten().cuda(), sw.cuda()
+    qwd, kwd = qw.float().cuda(), kw.float().cuda()
+    _lib.call("zib_gemm_w8a8_qk_norm_rope", qd.data_ptr(), K, wd.data_ptr(), K, sxd.data_ptr(), swd.data_ptr(),
+              y.data_ptr(), N, M, N, K, qwd.data_ptr(), kwd.data_ptr(), 1e-5, 1e-6, cos.data_ptr(),
+              sin.data_ptr(), cs_b, S, H, _lib.stream_of(qd))
+    torch.cuda.synchronize()
+    assert _lib.device_error_read_clear() == 0
+    plain = ops.dequant_epilogue(ops.gemm_acc_i32(q, wq), sx, sw, None).reshape(B, S, 3, H, 128)
+    got = y.cpu().reshape(B, S, 3, H, 128)
+    assert torch.equal(got[:, :, 0], ops.fused_qknorm_rope(plain[:, :, 0], qw, fc, 1e-5))
+    assert torch.equal(got[:, :, 1], ops.fused_qknorm_rope(plain[:, :, 1], kw, fc, 1e-6))
+    assert torch.equal(got[:, :, 2], plain[:, :, 2])
+
+
+def test_gemm_qk_norm_rope_rejects_odd_heads(cuda):
+    q = torch.zeros(8, 128, dtype=torch.int8, device="cuda")
+    w = torch.zeros(3 * 3 * 128, 128, dtype=torch.int8, device="cuda")
+    s = torch.ones(3 * 3 * 128, dtype=torch.bfloat16, device="cuda")
+    f = torch.ones(8 * 64, dtype=torch.float32, device="cuda")
+    y = torch.empty(8, 3 * 3 * 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="even head count"):
+        _lib.call("zib_gemm_w8a8_qk_norm_rope", q.data_ptr(), 128, w.data_ptr(), 128, s.data_ptr(), s.data_ptr(),
+                  y.data_ptr(), 3 * 3 * 128, 8, 3 * 3 * 128, 128, f.data_ptr(), f.data_ptr(), 1e-5, 1e-5,
+                  f.data_ptr(), f.data_ptr(), 0, 8, 3, _lib.stream_of(q))
+
+
 @pytest.mark.parametrize("N,K,had", [(256, 384, True), (64, 176, False), (1000, 3840, True), (40, 10240, True)])
 def test_weight_prep_bitexact(cuda, N, K, had):
     w = seeded_w(N, K, seed=N)
