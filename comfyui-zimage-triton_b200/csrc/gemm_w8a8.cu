@@ -255,6 +255,31 @@ __device__ __forceinline__ float dequant(uint32_t acc, float sxf, float swf) {
   return bf16_rne_alu(__fmul_rn(a, s));
 }
 
+// Packed bf16x2 forms (low half = even column).  The product of two bf16
+// values is exact in fp32, so mul.rn.bf16x2 (one rounding of the exact
+// product) equals the reference's bf16 multiply (fp32 product, rounded).
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float lo_f32(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_f32(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// dequant of columns (2i, 2i+1): sx2 = {sx, sx}, sw2 = {sw[2i], sw[2i+1]}
+__device__ __forceinline__ uint32_t dequant2(uint32_t acc0, uint32_t acc1, uint32_t sx2, uint32_t sw2) {
+  const uint32_t s2 = mul_bf16x2(sx2, sw2);
+  const uint32_t a2 = cvt_bf16x2(__int2float_rn((int)acc0), __int2float_rn((int)acc1));
+  return mul_bf16x2(a2, s2);
+}
+
+__device__ __forceinline__ uint4 ldg_u4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
 __device__ __forceinline__ void store_row_bf16(uint16_t* dst, const float* v, int n) {
 #pragma unroll
   for (int j = 0; j < n; j += 8) store_bf16x8(dst + j, v + j);
@@ -299,8 +324,10 @@ template <int EPI, class Rel>
 __device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
   const int row = c.row_base + c.quarter * 32 + c.lane;
   const bool row_ok = row < p.M;
-  float sxf = 0.0f;
-  if (EPI == EPI_BF16 && row_ok) sxf = bf16_bits_to_float(p.sx[row]);
+  uint16_t sxb = 0;
+  if (EPI == EPI_BF16 && row_ok) sxb = p.sx[row];
+  const uint32_t sx2 = (uint32_t)sxb | ((uint32_t)sxb << 16);
+  const float sxf = __uint_as_float((uint32_t)sxb << 16);
 #pragma unroll 1
   for (int ch = c.half * 4; ch < c.half * 4 + 4; ++ch) {
     uint32_t r[32];
@@ -316,6 +343,18 @@ __device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int 
           *reinterpret_cast<int4*>(dst + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
       } else {
         for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (int)r[j];
+      }
+    } else if (full && !p.bias) {
+      uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        const uint4 w = ldg_u4(p.sw + n0 + j);
+        uint4 o;
+        o.x = dequant2(r[j], r[j + 1], sx2, w.x);
+        o.y = dequant2(r[j + 2], r[j + 3], sx2, w.y);
+        o.z = dequant2(r[j + 4], r[j + 5], sx2, w.z);
+        o.w = dequant2(r[j + 6], r[j + 7], sx2, w.w);
+        *reinterpret_cast<uint4*>(dst + j) = o;
       }
     } else {
       float out[32];
@@ -361,7 +400,8 @@ template <class Rel>
 __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
   const int rt = c.quarter * 32 + c.lane;
   const int row = c.row_base + rt;
-  const float sxf = row < p.M ? bf16_bits_to_float(p.sx[row]) : 0.0f;
+  const uint32_t sxb = row < p.M ? (uint32_t)p.sx[row] : 0u;
+  const uint32_t sx2 = sxb | (sxb << 16);
   const int fb = nb * 128 + c.half * 64;
   const uint32_t tc = c.t_row + (uint32_t)(c.half * 128);
 #pragma unroll 1
@@ -371,21 +411,23 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
     tmem_ld16(tc + (uint32_t)(g * 16), rg);
     tmem_ld16(tc + (uint32_t)(64 + g * 16), ru);
     tmem_wait_ld();
-    float s1[16], s3[16], v[16];
-    load_bf16x8_nc(p.sw + fb + g * 16, s1);
-    load_bf16x8_nc(p.sw + fb + g * 16 + 8, s1 + 8);
-    load_bf16x8_nc(p.sw2 + fb + g * 16, s3);
-    load_bf16x8_nc(p.sw2 + fb + g * 16 + 8, s3 + 8);
+    const uint4 s1a = ldg_u4(p.sw + fb + g * 16), s1b = ldg_u4(p.sw + fb + g * 16 + 8);
+    const uint4 s3a = ldg_u4(p.sw2 + fb + g * 16), s3b = ldg_u4(p.sw2 + fb + g * 16 + 8);
+    const uint32_t s1[8] = {s1a.x, s1a.y, s1a.z, s1a.w, s1b.x, s1b.y, s1b.z, s1b.w};
+    const uint32_t s3[8] = {s3a.x, s3a.y, s3a.z, s3a.w, s3b.x, s3b.y, s3b.z, s3b.w};
+    uint32_t v[8];
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const float gv = dequant(rg[t], sxf, s1[t]);
-      const float uv = dequant(ru[t], sxf, s3[t]);
-      const float sl = bf16_rne_alu(__fmul_rn(gv, zib_sigmoidf(gv)));
-      v[t] = bf16_rne_alu(__fmul_rn(sl, uv));
+    for (int t = 0; t < 8; ++t) {
+      const uint32_t g2 = dequant2(rg[2 * t], rg[2 * t + 1], sx2, s1[t]);
+      const uint32_t u2 = dequant2(ru[2 * t], ru[2 * t + 1], sx2, s3[t]);
+      const float g0 = lo_f32(g2), g1 = hi_f32(g2);
+      // silu in fp32, rounded to bf16; times up, rounded to bf16 (swiglu.py:51-58)
+      const uint32_t sl2 = cvt_bf16x2(__fmul_rn(g0, zib_sigmoidf(g0)), __fmul_rn(g1, zib_sigmoidf(g1)));
+      v[t] = mul_bf16x2(sl2, u2);
     }
     const int ch = c.half * 8 + g * 2;
-    store_bf16x8(c.xbuf + xoff_256(rt, ch), v);
-    store_bf16x8(c.xbuf + xoff_256(rt, ch + 1), v + 8);
+    *reinterpret_cast<uint4*>(c.xbuf + xoff_256(rt, ch)) = make_uint4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<uint4*>(c.xbuf + xoff_256(rt, ch + 1)) = make_uint4(v[4], v[5], v[6], v[7]);
   }
   rel(c.lane);  // accumulator read: the MMA may refill this buffer
   pair_bar_sync(c.bar_id);
@@ -414,7 +456,8 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
   const int rt = c.quarter * 32 + c.lane;
   const int row = c.row_base + rt;
   const bool row_ok = row < p.M;
-  const float sxf = row_ok ? bf16_bits_to_float(p.sx[row]) : 0.0f;
+  const uint32_t sxb = row_ok ? (uint32_t)p.sx[row] : 0u;
+  const uint32_t sx2 = sxb | (sxb << 16);
   const int n0 = (nb * 2 + c.half) * 128;
   const int kind = (nb * 2) / p.heads;  // 0 Q, 1 K, 2 V
   const uint32_t tc = c.t_row + (uint32_t)(c.half * 128);
@@ -423,15 +466,17 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
     for (int cc = 0; cc < 4; ++cc) {
       uint32_t r[32];
       tmem_row32(tc + (uint32_t)(cc * 32), r);
-      float v[32];
+      uint16_t* dst = p.y + (int64_t)row * p.ldy + n0 + cc * 32;
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
-        float swv[8];
-        load_bf16x8_nc(p.sw + n0 + cc * 32 + j, swv);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) v[j + t] = dequant(r[j + t], sxf, swv[t]);
+        const uint4 w = ldg_u4(p.sw + n0 + cc * 32 + j);
+        uint4 o;
+        o.x = dequant2(r[j], r[j + 1], sx2, w.x);
+        o.y = dequant2(r[j + 2], r[j + 3], sx2, w.y);
+        o.z = dequant2(r[j + 4], r[j + 5], sx2, w.z);
+        o.w = dequant2(r[j + 6], r[j + 7], sx2, w.w);
+        if (row_ok) *reinterpret_cast<uint4*>(dst + j) = o;
       }
-      if (row_ok) store_row_bf16(p.y + (int64_t)row * p.ldy + n0 + cc * 32, v, 32);
     }
     rel(c.lane);
     return;
@@ -441,21 +486,20 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
   for (int cc = 0; cc < 4; ++cc) {
     uint32_t r[32];
     tmem_row32(tc + (uint32_t)(cc * 32), r);
-    float v[32];
 #pragma unroll
     for (int j = 0; j < 32; j += 8) {
-      float swv[8];
-      load_bf16x8_nc(p.sw + n0 + cc * 32 + j, swv);
+      const uint4 w = ldg_u4(p.sw + n0 + cc * 32 + j);
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+      uint32_t o[4];
 #pragma unroll
-      for (int t = 0; t < 8; t += 2) {
-        v[j + t] = dequant(r[j + t], sxf, swv[t]);
-        v[j + t + 1] = dequant(r[j + t + 1], sxf, swv[t + 1]);
-        ss0 += (double)(v[j + t] * v[j + t]);  // bf16 squares are exact in fp32; the fp64 sum is exact
-        ss1 += (double)(v[j + t + 1] * v[j + t + 1]);
+      for (int t = 0; t < 4; ++t) {
+        o[t] = dequant2(r[j + 2 * t], r[j + 2 * t + 1], sx2, wv[t]);
+        const float a = lo_f32(o[t]), b = hi_f32(o[t]);
+        ss0 += (double)(a * a);  // bf16 squares are exact in fp32; the fp64 sum is exact
+        ss1 += (double)(b * b);
       }
+      *reinterpret_cast<uint4*>(c.xbuf + xoff_512(rt, c.half * 16 + cc * 4 + j / 8)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) store_bf16x8(c.xbuf + xoff_512(rt, c.half * 16 + cc * 4 + k), v + 8 * k);
   }
   rel(c.lane);
   float* rstd_buf = reinterpret_cast<float*>(c.xbuf + 128 * 512);
