@@ -14,9 +14,10 @@
 //   warp 0      TMA producer (128-byte swizzled K-major tiles).
 //   warp 1      owns TMEM (512 columns = two 128x256 int32 accumulators) and
 //               issues tcgen05.mma from one thread.
-//   warps 2..9  epilogue: warps w and w+4 read the same 32 accumulator rows
-//               (TMEM lane quarter w%4) and split the 256 columns in halves;
-//               accumulator buffer b is drained while the MMA fills the other.
+//   warps 2..    epilogue (8 warps, 16 for SWIGLU): the NQ warps w, w+4, ...
+//               read the same 32 accumulator rows (TMEM lane quarter w%4) and
+//               split the 256 columns in NQ parts; accumulator buffer b is
+//               drained while the MMA fills the other.
 //   1-CTA tiles are 128x256 (48 KB stages).  For M > 128 a cluster of two
 //   CTAs (cta_group::2) computes 256x256 tiles: each CTA stages its 128 A rows
 //   and 128 of the B rows (32 KB stages), both CTAs' TMA loads complete on
@@ -30,9 +31,9 @@
 //   each (the row kernels' layout): the 128-point Hadamard transform on
 //   shuffles (SWIGLU) or norm * w + RoPE with coalesced cos/sin (QKROPE), and
 //   coalesced 256-byte row stores.
-//   SWIGLU tiles interleave the two weights in 64-row blocks,
-//   [w1 f0..f0+63 | w3 f0..f0+63 | w1 f0+64..f0+127 | w3 f0+64..f0+127], so each
-//   column half holds gate and up for 64 features.
+//   SWIGLU tiles interleave the two weights in 32-row blocks,
+//   [w1 f0..f0+31 | w3 f0..f0+31 | w1 f0+32..f0+63 | w3 f0+32..f0+63 | ...], so
+//   each column quarter holds gate and up for 32 features.
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records
 // ZIB_ERR_TIMEOUT in a device error word, drains its in-flight TMA loads and
 // MMAs, frees TMEM and exits.
@@ -53,9 +54,8 @@ constexpr int BN = 256;  // accumulator columns per tile
 constexpr int UMMA_K = 32;
 constexpr int HALF_BYTES = 128 * BK;  // one 128-row operand box
 constexpr int TMEM_COLS = 512;
-constexpr int NUM_THREADS = 320;  // warp 0 TMA, warp 1 MMA/TMEM, warps 2..9 epilogue
-constexpr int EPI_WARPS = 8;
-constexpr int SW_BOX_BYTES = 64 * BK;          // SWIGLU B box: 64 weight rows
+constexpr int SW_BOX_ROWS = 32;                // SWIGLU B box: 32 weight rows
+constexpr int SW_BOX_BYTES = SW_BOX_ROWS * BK;
 constexpr int S_STAGE_BYTES = 3 * HALF_BYTES;  // 1-CTA: A 128x128 + B 256x128
 constexpr int P_STAGE_BYTES = 2 * HALF_BYTES;  // 2-CTA pair: A 128x128 + B 128x128 per CTA
 constexpr int MAX_SMEM = 232448;
@@ -64,8 +64,13 @@ constexpr int MAX_SMEM = 232448;
 // base): [stages][256 B barriers][XBUF bytes of epilogue staging].
 template <int EPI>
 struct Cfg {
-  // SWIGLU: 128 rows x 128 features bf16.  QKROPE: 128 rows x 256 columns bf16 + rstd [128][2].
-  static constexpr int XBUF = EPI == EPI_SWIGLU ? 128 * 256 : (EPI == EPI_QKROPE ? 128 * 512 + 1024 : 0);
+  // warp 0 TMA, warp 1 MMA/TMEM, then EPI_WARPS epilogue warps (NQ per TMEM lane quarter)
+  static constexpr int EPI_WARPS = EPI == EPI_SWIGLU ? 16 : 8;
+  static constexpr int NQ = EPI_WARPS / 4;
+  static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+  // SWIGLU: 128 rows x 128 features bf16.
+  // QKROPE: 128 rows x 256 columns bf16 + partial sums of squares fp64 [128][NQ].
+  static constexpr int XBUF = EPI == EPI_SWIGLU ? 128 * 256 : (EPI == EPI_QKROPE ? 128 * 512 + 128 * NQ * 8 : 0);
   static constexpr int S_STAGES = EPI == EPI_QKROPE ? 3 : 4;
   static constexpr int P_STAGES = EPI == EPI_QKROPE ? 4 : 6;
   static constexpr int S_SMEM = S_STAGES * S_STAGE_BYTES + 1024 + 256 + XBUF;
@@ -219,21 +224,21 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-// named barrier over the two warps of an epilogue pair (64 threads)
-__device__ __forceinline__ void pair_bar_sync(int id) {
-  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+// named barrier over the epilogue warps of one TMEM lane quarter (nthreads = 32 * NQ)
+__device__ __forceinline__ void group_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// same barrier, returning the AND of `ok` over the 64 threads
-__device__ __forceinline__ int pair_bar_and(int id, int ok) {
+// same barrier, returning the AND of `ok` over its threads
+__device__ __forceinline__ int group_bar_and(int id, int nthreads, int ok) {
   int out;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.b32 q, %1, 0;\n\t"
-      "bar.red.and.pred p, %2, 64, q;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(out)
-      : "r"(ok), "r"(id)
+      : "r"(ok), "r"(id), "r"(nthreads)
       : "memory");
   return out;
 }
@@ -295,9 +300,9 @@ struct EpiCtx {
   uint32_t t_row;  // TMEM address: this warp's lane quarter in the current accumulator buffer
   int row_base;    // global row of tile row 0 in this CTA
   int quarter;     // TMEM lane quarter (warp % 4)
-  int half;        // column half (warps 2..5 -> 0, 6..9 -> 1)
+  int cq;          // column part: 256/NQ accumulator columns (warps 2..5 -> 0, 6..9 -> 1, ...)
   int lane;
-  int bar_id;      // named barrier of this warp pair
+  int bar_id;      // named barrier of this lane quarter's four warps
   uint8_t* xbuf;   // epilogue staging tile
 };
 
@@ -319,7 +324,7 @@ struct ReleaseLeader {
   }
 };
 
-// plain dequant (+bias) or raw int32: this thread's row, columns [128*half, 128*half+128)
+// plain dequant (+bias) or raw int32: this thread's row, columns [256/NQ * cq, +256/NQ)
 template <int EPI, class Rel>
 __device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
   const int row = c.row_base + c.quarter * 32 + c.lane;
@@ -329,7 +334,8 @@ __device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int 
   const uint32_t sx2 = (uint32_t)sxb | ((uint32_t)sxb << 16);
   const float sxf = __uint_as_float((uint32_t)sxb << 16);
 #pragma unroll 1
-  for (int ch = c.half * 4; ch < c.half * 4 + 4; ++ch) {
+  constexpr int CH = 8 / Cfg<EPI>::NQ;  // 32-column chunks per warp
+  for (int ch = c.cq * CH; ch < c.cq * CH + CH; ++ch) {
     uint32_t r[32];
     tmem_row32(c.t_row + (uint32_t)(ch * 32), r);
     const int n0 = nb * BN + ch * 32;
@@ -390,26 +396,27 @@ __device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int 
   rel(c.lane);
 }
 
-// SWIGLU.  Phase 1 (thread = row): column half `half` holds gate (cols 0..63)
-// and up (64..127) of features 128*nb + 64*half + [0, 64); the bf16 SwiGLU
-// values go to the staging tile [128 rows][128 features].  Phase 2 (16 lanes
-// per row): Walsh-Hadamard over the 128 features of a row (index bits 0..2
-// in-thread, 3..6 by xor shuffles, the act_quant kernels' order), times
-// bf16(1/sqrt(128)) correctly rounded, stored to x_rot.
+// SWIGLU.  Phase 1 (thread = row): column quarter cq holds gate (cols
+// 64cq..64cq+31) and up (64cq+32..64cq+63) of features 128*nb + 32*cq + [0, 32);
+// the bf16 SwiGLU values go to the staging tile [128 rows][128 features].
+// Phase 2 (16 lanes per row): Walsh-Hadamard over the 128 features of a row
+// (index bits 0..2 in-thread, 3..6 by xor shuffles, the act_quant kernels'
+// order), times bf16(1/sqrt(128)) correctly rounded, stored to x_rot.
 template <class Rel>
 __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
+  static_assert(Cfg<EPI_SWIGLU>::NQ == 4, "SWIGLU column quarters");
   const int rt = c.quarter * 32 + c.lane;
   const int row = c.row_base + rt;
   const uint32_t sxb = row < p.M ? (uint32_t)p.sx[row] : 0u;
   const uint32_t sx2 = sxb | (sxb << 16);
-  const int fb = nb * 128 + c.half * 64;
-  const uint32_t tc = c.t_row + (uint32_t)(c.half * 128);
+  const int fb = nb * 128 + c.cq * 32;
+  const uint32_t tc = c.t_row + (uint32_t)(c.cq * 64);
 #pragma unroll 1
-  for (int g = 0; g < 4; ++g) {
+  for (int g = 0; g < 2; ++g) {
     uint32_t rg[16], ru[16];
     __syncwarp();
     tmem_ld16(tc + (uint32_t)(g * 16), rg);
-    tmem_ld16(tc + (uint32_t)(64 + g * 16), ru);
+    tmem_ld16(tc + (uint32_t)(32 + g * 16), ru);
     tmem_wait_ld();
     const uint4 s1a = ldg_u4(p.sw + fb + g * 16), s1b = ldg_u4(p.sw + fb + g * 16 + 8);
     const uint4 s3a = ldg_u4(p.sw2 + fb + g * 16), s3b = ldg_u4(p.sw2 + fb + g * 16 + 8);
@@ -425,16 +432,16 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
       const uint32_t sl2 = cvt_bf16x2(__fmul_rn(g0, zib_sigmoidf(g0)), __fmul_rn(g1, zib_sigmoidf(g1)));
       v[t] = mul_bf16x2(sl2, u2);
     }
-    const int ch = c.half * 8 + g * 2;
+    const int ch = c.cq * 4 + g * 2;
     *reinterpret_cast<uint4*>(c.xbuf + xoff_256(rt, ch)) = make_uint4(v[0], v[1], v[2], v[3]);
     *reinterpret_cast<uint4*>(c.xbuf + xoff_256(rt, ch + 1)) = make_uint4(v[4], v[5], v[6], v[7]);
   }
   rel(c.lane);  // accumulator read: the MMA may refill this buffer
-  pair_bar_sync(c.bar_id);
+  group_bar_sync(c.bar_id, 128);
   const int sub = c.lane & 15;
 #pragma unroll 2
-  for (int it = 0; it < 8; ++it) {
-    const int r2 = c.quarter * 32 + c.half * 16 + it * 2 + (c.lane >> 4);
+  for (int it = 0; it < 4; ++it) {
+    const int r2 = c.quarter * 32 + c.cq * 8 + it * 2 + (c.lane >> 4);
     float v[8];
     load_bf16x8(c.xbuf + xoff_256(r2, sub), v);
     fwht8(v);
@@ -446,24 +453,30 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
   }
 }
 
-// QKROPE: column half `half` is head hb = 2*nb + half of the [Q | K | V]
-// projection (the head count is even, so both halves have the same kind).
-// Phase 1 (thread = row): dequantised head -> staging tile, and the row's
-// rstd from the exact sum of squares.  Phase 2 (16 lanes per row, 8 values
-// each): bf16(bf16(x * rstd) * w), interleaved-pair RoPE, coalesced store.
+// QKROPE: the tile holds heads hb = 2*nb and 2*nb+1 of the [Q | K | V]
+// projection (the head count is even, so both have the same kind); column
+// part cq is tile columns [CW*cq, CW*cq + CW), CW = 256/NQ.
+// Phase 1 (thread = row): dequantised columns -> staging tile, and the exact
+// partial sum of squares.  Phase 2 (16 lanes per row, 8 values each): rstd
+// from the head's exact partial sums, bf16(bf16(x * rstd) * w),
+// interleaved-pair RoPE, coalesced store.
 template <class Rel>
 __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
+  constexpr int NQ = Cfg<EPI_QKROPE>::NQ;
+  constexpr int CW = 256 / NQ;        // columns per warp
+  constexpr int WPH = NQ / 2;         // warps per head
+  constexpr int RPW = 32 / WPH;       // phase-2 rows per warp
   const int rt = c.quarter * 32 + c.lane;
   const int row = c.row_base + rt;
   const bool row_ok = row < p.M;
   const uint32_t sxb = row_ok ? (uint32_t)p.sx[row] : 0u;
   const uint32_t sx2 = sxb | (sxb << 16);
-  const int n0 = (nb * 2 + c.half) * 128;
+  const int n0 = nb * 256 + c.cq * CW;  // first output column of this part
   const int kind = (nb * 2) / p.heads;  // 0 Q, 1 K, 2 V
-  const uint32_t tc = c.t_row + (uint32_t)(c.half * 128);
+  const uint32_t tc = c.t_row + (uint32_t)(c.cq * CW);
   if (kind == 2) {
 #pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
+    for (int cc = 0; cc < CW / 32; ++cc) {
       uint32_t r[32];
       tmem_row32(tc + (uint32_t)(cc * 32), r);
       uint16_t* dst = p.y + (int64_t)row * p.ldy + n0 + cc * 32;
@@ -483,7 +496,7 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
   }
   double ss0 = 0.0, ss1 = 0.0;
 #pragma unroll 1
-  for (int cc = 0; cc < 4; ++cc) {
+  for (int cc = 0; cc < CW / 32; ++cc) {
     uint32_t r[32];
     tmem_row32(tc + (uint32_t)(cc * 32), r);
 #pragma unroll
@@ -495,32 +508,38 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
       for (int t = 0; t < 4; ++t) {
         o[t] = dequant2(r[j + 2 * t], r[j + 2 * t + 1], sx2, wv[t]);
         const float a = lo_f32(o[t]), b = hi_f32(o[t]);
-        ss0 += (double)(a * a);  // bf16 squares are exact in fp32; the fp64 sum is exact
+        ss0 += (double)(a * a);  // bf16 squares are exact in fp32; the fp64 sums are exact
         ss1 += (double)(b * b);
       }
-      *reinterpret_cast<uint4*>(c.xbuf + xoff_512(rt, c.half * 16 + cc * 4 + j / 8)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(c.xbuf + xoff_512(rt, (c.cq * CW + cc * 32 + j) / 8)) =
+          make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
   rel(c.lane);
-  float* rstd_buf = reinterpret_cast<float*>(c.xbuf + 128 * 512);
-  rstd_buf[rt * 2 + c.half] = rstd_from_sum(ss0 + ss1, 128, kind == 0 ? p.q_eps : p.k_eps);
-  pair_bar_sync(c.bar_id);
+  double* ss_buf = reinterpret_cast<double*>(c.xbuf + 128 * 512);
+  ss_buf[rt * NQ + c.cq] = ss0 + ss1;
+  group_bar_sync(c.bar_id, NQ * 32);
   const int sub = c.lane & 15;
+  const int hh = c.cq / WPH;  // head within the tile
   const float* w = kind == 0 ? p.qn_w : p.kn_w;
+  const float eps = kind == 0 ? p.q_eps : p.k_eps;
   const float4 wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
   const float4 wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
   const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll 4
-  for (int it = 0; it < 16; ++it) {
-    const int r2 = c.quarter * 32 + it * 2 + (c.lane >> 4);
+  for (int it = 0; it < RPW / 2; ++it) {
+    const int r2 = c.quarter * 32 + (c.cq % WPH) * RPW + it * 2 + (c.lane >> 4);
     const int grow = c.row_base + r2;
     const int gr = grow < p.M ? grow : 0;
     const int64_t bi = gr / p.seq, si = gr % p.seq;
     const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cosp + bi * p.cs_b + si * 64 + sub * 4));
     const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sinp + bi * p.cs_b + si * 64 + sub * 4));
     float v[8];
-    load_bf16x8(c.xbuf + xoff_512(r2, c.half * 16 + sub), v);
-    const float rs = rstd_buf[r2 * 2 + c.half];
+    load_bf16x8(c.xbuf + xoff_512(r2, hh * 16 + sub), v);
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < WPH; ++k) ss += ss_buf[r2 * NQ + hh * WPH + k];
+    const float rs = rstd_from_sum(ss, 128, eps);
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = bf16_rne_alu(__fmul_rn(bf16_rne_alu(__fmul_rn(v[j], rs)), wv[j]));
     const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
@@ -531,7 +550,7 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
       v[2 * k] = bf16_rne_alu(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(b, sv[k])));
       v[2 * k + 1] = bf16_rne_alu(__fadd_rn(__fmul_rn(b, cv[k]), __fmul_rn(a, sv[k])));
     }
-    if (grow < p.M) store_bf16x8(p.y + (int64_t)grow * p.ldy + n0 + sub * 8, v);
+    if (grow < p.M) store_bf16x8(p.y + (int64_t)grow * p.ldy + (nb * 2 + hh) * 128 + sub * 8, v);
   }
 }
 
@@ -544,18 +563,22 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const EpiCtx& c, 
 
 // Stage the B rows of tile nb for this CTA (`part` 0/1 = which 128 tile
 // columns; the 1-CTA kernel stages both).  Standard tiles: 128 consecutive
-// weight rows.  SWIGLU tiles: 64 rows of w1 then the same 64 rows of w3.
+// weight rows.  SWIGLU tiles: twice 32 rows of w1 then the same 32 rows of w3.
 template <int EPI>
 __device__ __forceinline__ void load_b_part(uint8_t* dst, const CUtensorMap* b0, const CUtensorMap* b1, int nb,
                                             int part, int kx, uint64_t* bar, uint32_t pair_bar, bool pair) {
   if (EPI == EPI_SWIGLU) {
-    const int f = nb * 128 + part * 64;
-    if (pair) {
-      tma_load_2d_pair(dst, b0, pair_bar, kx, f);
-      tma_load_2d_pair(dst + SW_BOX_BYTES, b1, pair_bar, kx, f);
-    } else {
-      tma_load_2d(dst, b0, bar, kx, f);
-      tma_load_2d(dst + SW_BOX_BYTES, b1, bar, kx, f);
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int f = nb * 128 + part * 64 + jj * SW_BOX_ROWS;
+      uint8_t* d = dst + jj * 2 * SW_BOX_BYTES;
+      if (pair) {
+        tma_load_2d_pair(d, b0, pair_bar, kx, f);
+        tma_load_2d_pair(d + SW_BOX_BYTES, b1, pair_bar, kx, f);
+      } else {
+        tma_load_2d(d, b0, bar, kx, f);
+        tma_load_2d(d + SW_BOX_BYTES, b1, bar, kx, f);
+      }
     }
   } else {
     if (pair) tma_load_2d_pair(dst, b0, pair_bar, kx, nb * 256 + part * 128);
@@ -566,7 +589,7 @@ __device__ __forceinline__ void load_b_part(uint8_t* dst, const CUtensorMap* b0,
 // --- kernels -------------------------------------------------------------------
 
 template <int EPI>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1)
     gemm_w8a8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ CUtensorMap tmap_b2, const Params p) {
   constexpr int STAGES = Cfg<EPI>::S_STAGES;
@@ -591,7 +614,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], EPI_WARPS);
+      mbar_init(&tempty_bar[a], Cfg<EPI>::EPI_WARPS);
     }
     mbar_init(mma_done_bar, 1);
     *abort_flag = 0;
@@ -667,8 +690,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ---- epilogue: warps w and w+4 share TMEM lane quarter w%4 and split the columns
-    const int half = (warp - 2) >> 2;
+    // ---- epilogue: warps w, w+4, ... share TMEM lane quarter w%4 and split the columns
+    const int cq = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int bar_id = 1 + ((warp - 2) & 3);
     int accb = 0;
@@ -677,12 +700,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int ok = 1;
       if (lane == 0) ok = mbar_wait_bounded(&tfull_bar[accb], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-      if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = pair_bar_and(bar_id, ok);  // the pair agrees
+      if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = group_bar_and(bar_id, Cfg<EPI>::NQ * 32, ok);
       if (!ok) break;
       tc_fence_after();
       const int mb = tile % p.num_mb, nb = tile / p.num_mb;
       const EpiCtx c{tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN), mb * 128, quarter,
-                     half, lane, bar_id, xbuf};
+                     cq, lane, bar_id, xbuf};
       epilogue_tile<EPI>(p, c, nb, ReleaseLocal{&tempty_bar[accb]});
       accb ^= 1;
       if (accb == 0) acc_phase ^= 1u;
@@ -698,7 +721,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1)
     gemm_w8a8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_b2, const Params p) {
   constexpr int STAGES = Cfg<EPI>::P_STAGES;
@@ -727,7 +750,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 2 * EPI_WARPS);  // epilogue warps of both CTAs
+      mbar_init(&tempty_bar[a], 2 * Cfg<EPI>::EPI_WARPS);  // epilogue warps of both CTAs
     }
     mbar_init(mma_done_bar, 1);
     *abort_flag = 0;
@@ -810,8 +833,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     __syncwarp();
   } else {
-    // ---- epilogue (both CTAs): warps w and w+4 share lane quarter w%4, split the columns
-    const int half = (warp - 2) >> 2;
+    // ---- epilogue (both CTAs): warps w, w+4, ... share lane quarter w%4, split the columns
+    const int cq = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int bar_id = 1 + ((warp - 2) & 3);
     int accb = 0;
@@ -820,12 +843,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int ok = 1;
       if (lane == 0) ok = mbar_wait_bounded(&tfull_bar[accb], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-      if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = pair_bar_and(bar_id, ok);  // the pair agrees
+      if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = group_bar_and(bar_id, Cfg<EPI>::NQ * 32, ok);
       if (!ok) { aborted = true; break; }
       tc_fence_after();
       const int mb = tile % p.num_mb, nb = tile / p.num_mb;
       const EpiCtx c{tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN),
-                     mb * 256 + (int)rank * 128, quarter, half, lane, bar_id, xbuf};
+                     mb * 256 + (int)rank * 128, quarter, cq, lane, bar_id, xbuf};
       epilogue_tile<EPI>(p, c, nb, ReleaseLeader{mapa_rank(smem_u32(&tempty_bar[accb]), 0)});
       accb ^= 1;
       if (accb == 0) acc_phase ^= 1u;
@@ -921,7 +944,7 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
                  "%s: q/w must be 16-byte aligned", what);
   if (M == 0) return ZIB_OK;
   CUtensorMap ta, tb, tb2;
-  const uint32_t b_box = EPI == EPI_SWIGLU ? 64u : 128u;
+  const uint32_t b_box = EPI == EPI_SWIGLU ? (uint32_t)SW_BOX_ROWS : 128u;
   int st = make_map(&ta, q, K, M, ldq, 128u);
   if (st) return st;
   st = make_map(&tb, w, K, w_rows, ldw, b_box);
@@ -955,13 +978,13 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
     p.num_tiles = p.num_mb * p.num_nb;
     int clusters = sms / 2;
     if (clusters > p.num_tiles) clusters = p.num_tiles;
-    gemm_w8a8_pair_kernel<EPI><<<2 * clusters, NUM_THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
+    gemm_w8a8_pair_kernel<EPI><<<2 * clusters, Cfg<EPI>::THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
   } else {
     p.num_mb = (int)((M + 127) / 128);
     p.num_tiles = p.num_mb * p.num_nb;
     int grid = sms;
     if (grid > p.num_tiles) grid = p.num_tiles;
-    gemm_w8a8_kernel<EPI><<<grid, NUM_THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
+    gemm_w8a8_kernel<EPI><<<grid, Cfg<EPI>::THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
   }
   return zib_check_launch(what);
 }
