@@ -333,8 +333,8 @@ __device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int 
   if (EPI == EPI_BF16 && row_ok) sxb = p.sx[row];
   const uint32_t sx2 = (uint32_t)sxb | ((uint32_t)sxb << 16);
   const float sxf = __uint_as_float((uint32_t)sxb << 16);
-#pragma unroll 1
   constexpr int CH = 8 / Cfg<EPI>::NQ;  // 32-column chunks per warp
+#pragma unroll 1
   for (int ch = c.cq * CH; ch < c.cq * CH + CH; ++ch) {
     uint32_t r[32];
     tmem_row32(c.t_row + (uint32_t)(ch * 32), r);

@@ -1081,6 +1081,8 @@ static bool pipe_cfg(K kernel, int64_t n, int nin, int64_t rows, int warps, Pipe
 
 }  // namespace pipe
 
+#include "rows_warp.cuh"
+
 }  // namespace zib
 
 using namespace zib;
@@ -1133,7 +1135,13 @@ extern "C" int zib_act_quant(const void* x, int64_t ldx, void* q, int64_t ldq, v
         act_quant_kernel<CPT, HAD><<<(unsigned)M, l.threads, 0, st>>>(
             (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, K)));
   } else {
-    bool launched = false;
+    bool launched = wr::dispatch(K, [&](auto Rc, auto Mc, int cpl) {
+      constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
+      auto k = hadamard ? wr::act_quant_wr<R, MC, true> : wr::act_quant_wr<R, MC, false>;
+      k<<<wr::grid_for(k, R, cpl, M), 32 * wr::kWarps, wr::smem_for(cpl), st>>>((const uint16_t*)x, ldx, (int8_t*)q, ldq,
+                                                             (uint16_t*)sx, cpl, M);
+    });
+    if (!launched)
     ZIB_DISPATCH_W(pipe::pipe_warps(K), ZIB_DISPATCH_BOOL(hadamard, HAD,
         ZIB_PIPE_TRY((pipe::act_quant_pipe<W, HAD>), 1, M, K,
                      (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, K)));
@@ -1157,6 +1165,14 @@ extern "C" int zib_rms_norm(const void* x, int64_t ldx, const float* w, void* y,
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (vec)
+    launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
+      constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
+      auto k = wr::rmsnorm_wr<R, MC, 0, false>;
+      k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+          (const uint16_t*)x, ldx, w, nullptr, nullptr, 0, 1, (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps, cpl,
+          rows);
+    });
+  if (vec && !launched)
     ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_PIPE_TRY((pipe::rmsnorm_pipe<W, 0, false>), 1, rows, n,
         (const uint16_t*)x, ldx, w, nullptr, nullptr, 0, 1, (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps));
   if (!launched)
@@ -1180,6 +1196,14 @@ extern "C" int zib_rmsnorm_mod(const void* x, int64_t ldx, const float* w, const
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (vec)
+    launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
+      constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
+      auto k = wr::rmsnorm_wr<R, MC, 1, false>;
+      k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+          (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
+          (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps, cpl, rows);
+    });
+  if (vec && !launched)
     ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_PIPE_TRY((pipe::rmsnorm_pipe<W, 1, false>), 1, rows, n,
         (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
         (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps));
@@ -1205,7 +1229,14 @@ extern "C" int zib_rmsnorm_mod_quant(const void* x, int64_t ldx, const float* w,
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "rmsnorm_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = false;
+  bool launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
+    constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
+    auto k = hadamard ? wr::rmsnorm_wr<R, MC, 2, true> : wr::rmsnorm_wr<R, MC, 2, false>;
+    k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+        (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
+        nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, n, eps, cpl, rows);
+  });
+  if (!launched)
   ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_DISPATCH_BOOL(hadamard, HAD,
       ZIB_PIPE_TRY((pipe::rmsnorm_pipe<W, 2, HAD>), 1, rows, n,
           (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
@@ -1233,6 +1264,14 @@ extern "C" int zib_norm_gate_residual(const void* x, int64_t ldx, const void* r,
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (vec)
+    launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
+      constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
+      auto k = wr::ngr_wr<R, MC, false, false>;
+      k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+          (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
+          (uint16_t*)y, ldy, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, n, eps, eps, cpl, rows);
+    });
+  if (vec && !launched)
     ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_PIPE_TRY((pipe::ngr_pipe<W, false, false>), 1, rows, n,
         (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch,
         w, (uint16_t*)y, ldy, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, n, eps, eps));
@@ -1263,7 +1302,15 @@ extern "C" int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, cons
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "norm_gate_residual_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = false;
+  bool launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
+    constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
+    auto k = hadamard ? wr::ngr_wr<R, MC, true, true> : wr::ngr_wr<R, MC, true, false>;
+    k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+        (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
+        (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
+        (uint16_t*)sx, n, eps, eps2, cpl, rows);
+  });
+  if (!launched)
   ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_DISPATCH_BOOL(hadamard, HAD,
       ZIB_PIPE_TRY((pipe::ngr_pipe<W, true, HAD>), 1, rows, n,
           (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch,

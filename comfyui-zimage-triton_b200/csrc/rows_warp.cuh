@@ -1,0 +1,377 @@
+// Warp-per-row kernels: R warps per row (R = 1 for 3840 columns, 4 for
+// 10240), one read of every input and one write of every output.
+//
+// Lane l of warp r in a row's team owns the 16-byte chunks (8 bf16)
+//   c = 32 * cpl * r + l + 32 * k,   k = 0 .. cpl-1,
+// so every load and store instruction of a warp moves 512 contiguous bytes
+// and a 128-element Hadamard group (16 chunks) sits in lanes 0-15 or 16-31 of
+// one k (fwht128: 3 butterfly stages in-thread, 4 over xor shuffles; the same
+// adds in the same order as the other rotation kernels).  All of a row's
+// global loads are issued at once (an unrolled register array); the row then
+// lives in this warp's slice of shared memory (chunk k of lane l at
+// [k][l], conflict-free) and the heavy stages (norm, rotation, quantisation)
+// are rolled loops over it, which keeps the code small enough for the
+// instruction cache.  Row reductions are warp shuffles (plus one named
+// barrier across the R warps); there are no CTA-wide barriers.  Arithmetic and rounding points are those of the kernels
+// these replace (rms_norm.py:47-57, fused_norm_residual.py:58-73,
+// int8_linear.py:119-130); packed bf16x2 multiplies / adds are used only where
+// both operands are bf16, where the single rounding of the exact result equals
+// the reference's fp32 operation rounded to bf16.
+#pragma once
+
+#include <type_traits>
+
+namespace wr {
+
+constexpr int kWarps = 4;  // warps per CTA; a CTA runs kWarps / R rows at a time
+
+// --- packed bf16x2 helpers --------------------------------------------------------
+
+__device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t pack_exact(float lo, float hi) {  // both bf16-exact
+  return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
+}
+__device__ __forceinline__ uint32_t cvt2(float lo, float hi) {  // round each to bf16 (RNE)
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack8(const uint4& d, float v[8]) {
+  v[0] = lo_f(d.x); v[1] = hi_f(d.x); v[2] = lo_f(d.y); v[3] = hi_f(d.y);
+  v[4] = lo_f(d.z); v[5] = hi_f(d.z); v[6] = lo_f(d.w); v[7] = hi_f(d.w);
+}
+__device__ __forceinline__ uint4 pack8_exact(const float v[8]) {
+  return make_uint4(pack_exact(v[0], v[1]), pack_exact(v[2], v[3]), pack_exact(v[4], v[5]),
+                    pack_exact(v[6], v[7]));
+}
+__device__ __forceinline__ uint4 ld_cs(const void* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ uint4 ld_nc(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// |x| bit patterns of bf16 order like unsigned integers: running max of a chunk
+__device__ __forceinline__ uint32_t absmax8(const uint4& d, uint32_t m) {
+  m = __vmaxu2(m, d.x & 0x7FFF7FFFu);
+  m = __vmaxu2(m, d.y & 0x7FFF7FFFu);
+  m = __vmaxu2(m, d.z & 0x7FFF7FFFu);
+  m = __vmaxu2(m, d.w & 0x7FFF7FFFu);
+  return m;
+}
+__device__ __forceinline__ double sumsq8(const uint4& d) {  // bf16 squares are exact in fp32
+  float v[8];
+  unpack8(d, v);
+  double s = 0.0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += (double)(v[j] * v[j]);
+  return s;
+}
+
+// --- team of R warps working on one row ---------------------------------------------
+
+template <int R>
+struct Team {
+  int lane, wig, grp;
+  __device__ __forceinline__ Team() {
+    lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5;
+    wig = w % R;
+    grp = w / R;
+  }
+  __device__ __forceinline__ void sync() const {
+    if (R > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(R * 32) : "memory");
+  }
+  // exact in practice: every partial is an exact fp64 sum of exact fp32 squares
+  __device__ __forceinline__ double sum(double v, double* red) const {
+    v = warp_sum_f64(v);
+    if (R == 1) return v;
+    if (lane == 0) red[threadIdx.x >> 5] = v;
+    sync();
+    double r = 0.0;
+#pragma unroll
+    for (int k = 0; k < R; ++k) r += red[grp * R + k];
+    sync();
+    return r;
+  }
+  __device__ __forceinline__ uint32_t umax(uint32_t v, uint32_t* red) const {
+    v = __reduce_max_sync(0xFFFFFFFFu, v);
+    if (R == 1) return v;
+    if (lane == 0) red[threadIdx.x >> 5] = v;
+    sync();
+    uint32_t r = 0;
+#pragma unroll
+    for (int k = 0; k < R; ++k) r = max(r, red[grp * R + k]);
+    sync();
+    return r;
+  }
+  __device__ __forceinline__ int64_t chunk(int cpl, int k) const { return (int64_t)(wig * cpl + k) * 32 + lane; }
+  // element offset of this lane's first chunk in a row; chunk k is at + 256 * k
+  __device__ __forceinline__ int64_t first(int cpl) const { return ((int64_t)wig * cpl * 32 + lane) * 8; }
+};
+
+// rotate (optional) chunk d in place and fold its |max| (bf16 bits)
+template <bool HAD>
+__device__ __forceinline__ void rot_amax(uint4& d, uint32_t& m, int lane) {
+  if (HAD) {
+    float v[8];
+    unpack8(d, v);
+    pipe::fwht128(v, lane);
+    pipe::had_round8(v);
+    d = pack8_exact(v);
+  }
+  m = absmax8(d, m);
+}
+
+// y = bf16(bf16(x * rstd) * w) for one chunk; w points at the chunk's 8 fp32
+// weights (rms_norm.py:53-57)
+__device__ __forceinline__ uint4 norm_w(const uint4& d, float rstd, const float* __restrict__ w) {
+  float v[8], wv[8];
+  unpack8(d, v);
+  const float4 wa = __ldg(reinterpret_cast<const float4*>(w));
+  const float4 wb = __ldg(reinterpret_cast<const float4*>(w + 4));
+  wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
+  wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
+  uint32_t a[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t n2 = cvt2(__fmul_rn(v[2 * j], rstd), __fmul_rn(v[2 * j + 1], rstd));
+    a[j] = cvt2(__fmul_rn(lo_f(n2), wv[2 * j]), __fmul_rn(hi_f(n2), wv[2 * j + 1]));
+  }
+  return make_uint4(a[0], a[1], a[2], a[3]);
+}
+
+// y = bf16(y * bf16(1 + s)) (+ shift); scale/shift point at the chunk's 8
+// values (patching_comfyui.py:378, :401)
+__device__ __forceinline__ uint4 modulate(const uint4& y, const uint16_t* __restrict__ scale,
+                                          const uint16_t* __restrict__ shift) {
+  constexpr uint32_t kOne2 = 0x3F803F80u;  // bf16 (1.0, 1.0)
+  const uint4 s = ld_nc(scale);
+  uint4 r = make_uint4(hmul2(y.x, hadd2(kOne2, s.x)), hmul2(y.y, hadd2(kOne2, s.y)),
+                       hmul2(y.z, hadd2(kOne2, s.z)), hmul2(y.w, hadd2(kOne2, s.w)));
+  if (shift) {
+    const uint4 h = ld_nc(shift);
+    r = make_uint4(hadd2(r.x, h.x), hadd2(r.y, h.y), hadd2(r.z, h.z), hadd2(r.w, h.w));
+  }
+  return r;
+}
+
+// --- kernels ---------------------------------------------------------------------------
+
+// this warp's slice of the CTA's dynamic shared memory: cpl * 32 chunks
+__device__ __forceinline__ uint4* warp_slice(int cpl) {
+  extern __shared__ __align__(16) uint4 wr_smem[];
+  return wr_smem + (threadIdx.x >> 5) * cpl * 32 + (threadIdx.x & 31);
+}
+
+// load the lane's cpl chunks (all in flight at once) into the warp slice;
+// returns the lane's exact partial sum of squares when SS
+template <int MAXC, bool SS>
+__device__ __forceinline__ double stage_row(const uint16_t* __restrict__ src, uint4* sl, int cpl) {
+  uint4 d[MAXC];
+#pragma unroll
+  for (int k = 0; k < MAXC; ++k)
+    if (k < cpl) d[k] = ld_cs(src + 256 * k);
+  double ss = 0.0;
+#pragma unroll
+  for (int k = 0; k < MAXC; ++k) {
+    if (k < cpl) {
+      sl[32 * k] = d[k];
+      if (SS) ss += sumsq8(d[k]);
+    }
+  }
+  return ss;
+}
+
+// quantise the rotated row in the warp slice, store q and sx (int8_linear.py:129-130)
+template <int R>
+__device__ __forceinline__ void quant_row(const Team<R>& t, const uint4* sl, int cpl, uint32_t m2, uint32_t* redu,
+                                          int64_t row, int8_t* __restrict__ q, int64_t ldq,
+                                          uint16_t* __restrict__ sx) {
+  uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
+  m = t.umax(m, redu);
+  const float s = act_scale(__uint_as_float(m << 16));
+  const float rcp = __fdiv_rn(1.0f, s);
+  int8_t* qr = q + row * ldq + t.first(cpl);
+#pragma unroll 1
+  for (int k = 0; k < cpl; ++k) {
+    float v[8];
+    unpack8(sl[32 * k], v);
+    int qq[8];
+    pipe::quant8(v, s, rcp, qq);
+    pipe::store_i8x8_prmt(qr + 256 * k, qq);
+  }
+  if (t.wig == 0 && t.lane == 0) sx[row] = float_to_bf16_bits(s);
+}
+
+template <int R, int MAXC, bool HAD>
+__global__ void __launch_bounds__(32 * kWarps) act_quant_wr(const uint16_t* __restrict__ x, int64_t ldx,
+                                                            int8_t* __restrict__ q, int64_t ldq,
+                                                            uint16_t* __restrict__ sx, int cpl, int64_t rows) {
+  __shared__ uint32_t redu[kWarps];
+  const Team<R> t;
+  const int64_t f0 = t.first(cpl);
+  uint4* sl = warp_slice(cpl);
+  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
+       row += (int64_t)gridDim.x * (kWarps / R)) {
+    stage_row<MAXC, false>(x + row * ldx + f0, sl, cpl);
+    uint32_t m = 0;
+#pragma unroll 1
+    for (int k = 0; k < cpl; ++k) {
+      uint4 d = sl[32 * k];
+      rot_amax<HAD>(d, m, t.lane);
+      if (HAD) sl[32 * k] = d;
+    }
+    quant_row<R>(t, sl, cpl, m, redu, row, q, ldq, sx);
+    __syncwarp();
+  }
+}
+
+// MODE 0: rmsnorm -> bf16; 1: rmsnorm * (1+s) (+shift) -> bf16; 2: MODE 1 -> rotate / quant
+template <int R, int MAXC, int MODE, bool HAD>
+__global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
+    const uint16_t* __restrict__ x, int64_t ldx, const float* __restrict__ w, const uint16_t* __restrict__ scale,
+    const uint16_t* __restrict__ shift, int64_t ld_mod, int64_t rows_per_batch, uint16_t* __restrict__ y,
+    int64_t ldy, int8_t* __restrict__ q, int64_t ldq, uint16_t* __restrict__ sx, int64_t n, float eps, int cpl,
+    int64_t rows) {
+  __shared__ double redd[kWarps];
+  __shared__ uint32_t redu[kWarps];
+  const Team<R> t;
+  const int64_t f0 = t.first(cpl);
+  const float* wl = w + f0;
+  uint4* sl = warp_slice(cpl);
+  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
+       row += (int64_t)gridDim.x * (kWarps / R)) {
+    const double ss = stage_row<MAXC, true>(x + row * ldx + f0, sl, cpl);
+    const float rstd = rstd_from_sum(t.sum(ss, redd), (int)n, eps);
+    const int64_t mo = (row / rows_per_batch) * ld_mod + f0;
+    uint16_t* yr = MODE <= 1 ? y + row * ldy + f0 : nullptr;
+    uint32_t m = 0;
+#pragma unroll 1
+    for (int k = 0; k < cpl; ++k) {
+      uint4 v = norm_w(sl[32 * k], rstd, wl + 256 * k);
+      if (MODE >= 1) v = modulate(v, scale + mo + 256 * k, shift ? shift + mo + 256 * k : nullptr);
+      if (MODE <= 1) {
+        *reinterpret_cast<uint4*>(yr + 256 * k) = v;
+      } else {
+        rot_amax<HAD>(v, m, t.lane);
+        sl[32 * k] = v;
+      }
+    }
+    if (MODE == 2) quant_row<R>(t, sl, cpl, m, redu, row, q, ldq, sx);
+    __syncwarp();
+  }
+}
+
+// y = r + g * rmsnorm(x); FUSE: then rmsnorm(y; w2) * (1+s) (+shift) -> rotate / quant
+template <int R, int MAXC, bool FUSE, bool HAD>
+__global__ void __launch_bounds__(32 * kWarps) ngr_wr(
+    const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ r, int64_t ldr,
+    const uint16_t* __restrict__ gate, int64_t ld_gate, int64_t rows_per_batch, const float* __restrict__ w,
+    uint16_t* __restrict__ y, int64_t ldy, const float* __restrict__ w2, const uint16_t* __restrict__ scale,
+    const uint16_t* __restrict__ shift, int64_t ld_mod, int8_t* __restrict__ q, int64_t ldq,
+    uint16_t* __restrict__ sx, int64_t n, float eps, float eps2, int cpl, int64_t rows) {
+  __shared__ double redd[kWarps];
+  __shared__ uint32_t redu[kWarps];
+  const Team<R> t;
+  const int64_t f0 = t.first(cpl);
+  const float* wl = w + f0;
+  uint4* sl = warp_slice(cpl);
+  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
+       row += (int64_t)gridDim.x * (kWarps / R)) {
+    const double ss = stage_row<MAXC, true>(x + row * ldx + f0, sl, cpl);
+    const float rstd = rstd_from_sum(t.sum(ss, redd), (int)n, eps);
+    const int64_t b = row / rows_per_batch;
+    const uint16_t* gl = gate + b * ld_gate + f0;
+    const uint16_t* rr = r + row * ldr + f0;
+    uint16_t* yr = y + row * ldy + f0;
+    double ss2 = 0.0;
+#pragma unroll 4
+    for (int k = 0; k < cpl; ++k) {
+      const uint4 e = ld_cs(rr + 256 * k);
+      const uint4 a = norm_w(sl[32 * k], rstd, wl + 256 * k);
+      const uint4 g = ld_nc(gl + 256 * k);
+      // bf16(r + bf16(g * a)), fused_norm_residual.py:69-73
+      const uint4 v = make_uint4(hadd2(e.x, hmul2(g.x, a.x)), hadd2(e.y, hmul2(g.y, a.y)),
+                                 hadd2(e.z, hmul2(g.z, a.z)), hadd2(e.w, hmul2(g.w, a.w)));
+      *reinterpret_cast<uint4*>(yr + 256 * k) = v;
+      if (FUSE) {
+        sl[32 * k] = v;
+        ss2 += sumsq8(v);
+      }
+    }
+    if (FUSE) {
+      const float rstd2 = rstd_from_sum(t.sum(ss2, redd), (int)n, eps2);
+      const int64_t mo = b * ld_mod + f0;
+      const float* w2l = w2 + f0;
+      uint32_t m = 0;
+#pragma unroll 1
+      for (int k = 0; k < cpl; ++k) {
+        uint4 v = modulate(norm_w(sl[32 * k], rstd2, w2l + 256 * k), scale + mo + 256 * k,
+                           shift ? shift + mo + 256 * k : nullptr);
+        rot_amax<HAD>(v, m, t.lane);
+        sl[32 * k] = v;
+      }
+      quant_row<R>(t, sl, cpl, m, redu, row, q, ldq, sx);
+    }
+    __syncwarp();
+  }
+}
+
+// --- host side ---------------------------------------------------------------------------
+
+// Team size and chunks per lane for a row of n bf16: n % 256 == 0 and at most
+// MAXC (16) chunks per lane; false -> the caller uses another kernel.
+static inline bool pick(int64_t n, int* R, int* cpl) {
+  if (n <= 0 || n % 256) return false;
+  const int64_t t = n / 256;
+  for (int r = 1; r <= 4; r *= 2) {
+    if (t % r == 0 && t / r <= 16) {
+      *R = r;
+      *cpl = (int)(t / r);
+      return true;
+    }
+  }
+  return false;
+}
+
+// dynamic shared memory of a CTA: kWarps slices of cpl * 32 chunks
+static inline size_t smem_for(int cpl) { return (size_t)kWarps * cpl * 32 * 16; }
+
+template <class K>
+static int grid_for(K kernel, int R, int cpl, int64_t rows) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32 * kWarps, smem_for(cpl)) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  const int64_t need = (rows + (kWarps / R) - 1) / (kWarps / R);
+  const int64_t g = (int64_t)per_sm * pipe::num_sms();
+  return (int)(need < g ? need : g);
+}
+
+// Calls f(integral_constant<R>, integral_constant<MAXC>, cpl) for the team
+// size picked for n; false when n has no warp-row shape.
+template <class F>
+static bool dispatch(int64_t n, F&& f) {
+  int R, cpl;
+  if (!pick(n, &R, &cpl)) return false;
+  using std::integral_constant;
+  if (R == 1 && cpl <= 4) f(integral_constant<int, 1>{}, integral_constant<int, 4>{}, cpl);
+  else if (R == 1 && cpl <= 8) f(integral_constant<int, 1>{}, integral_constant<int, 8>{}, cpl);
+  else if (R == 1) f(integral_constant<int, 1>{}, integral_constant<int, 16>{}, cpl);
+  else if (R == 2) f(integral_constant<int, 2>{}, integral_constant<int, 16>{}, cpl);
+  else if (cpl <= 12) f(integral_constant<int, 4>{}, integral_constant<int, 12>{}, cpl);
+  else f(integral_constant<int, 4>{}, integral_constant<int, 16>{}, cpl);
+  return true;
+}
+
+}  // namespace wr
+
