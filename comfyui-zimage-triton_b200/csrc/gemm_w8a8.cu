@@ -540,17 +540,21 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
 #pragma unroll
     for (int k = 0; k < WPH; ++k) ss += ss_buf[r2 * NQ + hh * WPH + k];
     const float rs = rstd_from_sum(ss, 128, eps);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = bf16_rne_alu(__fmul_rn(bf16_rne_alu(__fmul_rn(v[j], rs)), wv[j]));
     const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
     const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+    uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float a = v[2 * k], b = v[2 * k + 1];
-      v[2 * k] = bf16_rne_alu(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(b, sv[k])));
-      v[2 * k + 1] = bf16_rne_alu(__fadd_rn(__fmul_rn(b, cv[k]), __fmul_rn(a, sv[k])));
+      // bf16(bf16(x * rstd) * w), then the pair rotation, each rounded to bf16
+      const uint32_t n2 = cvt_bf16x2(__fmul_rn(v[2 * k], rs), __fmul_rn(v[2 * k + 1], rs));
+      const uint32_t m2 = cvt_bf16x2(__fmul_rn(lo_f32(n2), wv[2 * k]), __fmul_rn(hi_f32(n2), wv[2 * k + 1]));
+      const float a = lo_f32(m2), b = hi_f32(m2);
+      o[k] = cvt_bf16x2(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(b, sv[k])),
+                        __fadd_rn(__fmul_rn(b, cv[k]), __fmul_rn(a, sv[k])));
     }
-    if (grow < p.M) store_bf16x8(p.y + (int64_t)grow * p.ldy + (nb * 2 + hh) * 128 + sub * 8, v);
+    if (grow < p.M)
+      *reinterpret_cast<uint4*>(p.y + (int64_t)grow * p.ldy + (nb * 2 + hh) * 128 + sub * 8) =
+          make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 

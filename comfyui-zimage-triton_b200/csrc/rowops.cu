@@ -1135,10 +1135,11 @@ extern "C" int zib_act_quant(const void* x, int64_t ldx, void* q, int64_t ldq, v
         act_quant_kernel<CPT, HAD><<<(unsigned)M, l.threads, 0, st>>>(
             (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, K)));
   } else {
-    bool launched = wr::dispatch(K, [&](auto Rc, auto Mc, int cpl) {
-      constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
-      auto k = hadamard ? wr::act_quant_wr<R, MC, true> : wr::act_quant_wr<R, MC, false>;
-      k<<<wr::grid_for(k, R, cpl, M), 32 * wr::kWarps, wr::smem_for(cpl), st>>>((const uint16_t*)x, ldx, (int8_t*)q, ldq,
+    bool launched = wr::dispatch(K, [&](auto Rc, int cpl) {
+      constexpr int R = decltype(Rc)::value;
+      auto k = hadamard ? wr::act_quant_wr<R, true> : wr::act_quant_wr<R, false>;
+      wr::set_smem(k, wr::smem_for(cpl, 1));
+      k<<<wr::grid_for(k, R, cpl, 1, M), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>((const uint16_t*)x, ldx, (int8_t*)q, ldq,
                                                              (uint16_t*)sx, cpl, M);
     });
     if (!launched)
@@ -1165,10 +1166,11 @@ extern "C" int zib_rms_norm(const void* x, int64_t ldx, const float* w, void* y,
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (vec)
-    launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
-      constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
-      auto k = wr::rmsnorm_wr<R, MC, 0, false>;
-      k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+    launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+      constexpr int R = decltype(Rc)::value;
+      auto k = wr::rmsnorm_wr<R, 0, false>;
+      wr::set_smem(k, wr::smem_for(cpl, 1));
+      k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
           (const uint16_t*)x, ldx, w, nullptr, nullptr, 0, 1, (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps, cpl,
           rows);
     });
@@ -1196,10 +1198,11 @@ extern "C" int zib_rmsnorm_mod(const void* x, int64_t ldx, const float* w, const
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (vec)
-    launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
-      constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
-      auto k = wr::rmsnorm_wr<R, MC, 1, false>;
-      k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+    launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+      constexpr int R = decltype(Rc)::value;
+      auto k = wr::rmsnorm_wr<R, 1, false>;
+      wr::set_smem(k, wr::smem_for(cpl, 1));
+      k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
           (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
           (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps, cpl, rows);
     });
@@ -1229,10 +1232,11 @@ extern "C" int zib_rmsnorm_mod_quant(const void* x, int64_t ldx, const float* w,
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "rmsnorm_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
-    constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
-    auto k = hadamard ? wr::rmsnorm_wr<R, MC, 2, true> : wr::rmsnorm_wr<R, MC, 2, false>;
-    k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+  bool launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+    constexpr int R = decltype(Rc)::value;
+    auto k = hadamard ? wr::rmsnorm_wr<R, 2, true> : wr::rmsnorm_wr<R, 2, false>;
+    wr::set_smem(k, wr::smem_for(cpl, 1));
+    k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
         (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
         nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, n, eps, cpl, rows);
   });
@@ -1264,10 +1268,11 @@ extern "C" int zib_norm_gate_residual(const void* x, int64_t ldx, const void* r,
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (vec)
-    launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
-      constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
-      auto k = wr::ngr_wr<R, MC, false, false>;
-      k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+    launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+      constexpr int R = decltype(Rc)::value;
+      auto k = wr::ngr_wr<R, false, false>;
+      wr::set_smem(k, wr::smem_for(cpl, 1));
+      k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
           (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
           (uint16_t*)y, ldy, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, n, eps, eps, cpl, rows);
     });
@@ -1302,10 +1307,11 @@ extern "C" int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, cons
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "norm_gate_residual_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = wr::dispatch(n, [&](auto Rc, auto Mc, int cpl) {
-    constexpr int R = decltype(Rc)::value, MC = decltype(Mc)::value;
-    auto k = hadamard ? wr::ngr_wr<R, MC, true, true> : wr::ngr_wr<R, MC, true, false>;
-    k<<<wr::grid_for(k, R, cpl, rows), 32 * wr::kWarps, wr::smem_for(cpl), st>>>(
+  bool launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+    constexpr int R = decltype(Rc)::value;
+    auto k = hadamard ? wr::ngr_wr<R, true, true> : wr::ngr_wr<R, true, false>;
+    wr::set_smem(k, wr::smem_for(cpl, 1));
+    k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
         (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
         (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
         (uint16_t*)sx, n, eps, eps2, cpl, rows);

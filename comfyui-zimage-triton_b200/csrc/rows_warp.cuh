@@ -6,11 +6,11 @@
 // so every load and store instruction of a warp moves 512 contiguous bytes
 // and a 128-element Hadamard group (16 chunks) sits in lanes 0-15 or 16-31 of
 // one k (fwht128: 3 butterfly stages in-thread, 4 over xor shuffles; the same
-// adds in the same order as the other rotation kernels).  All of a row's
-// global loads are issued at once (an unrolled register array); the row then
-// lives in this warp's slice of shared memory (chunk k of lane l at
-// [k][l], conflict-free) and the heavy stages (norm, rotation, quantisation)
-// are rolled loops over it, which keeps the code small enough for the
+// adds in the same order as the other rotation kernels).  A row is copied
+// into this warp's slice of shared memory with cp.async (chunk k of lane l at
+// [k][l], conflict-free; all of a row's copies in flight at once, no
+// registers held), and the heavy stages (norm, rotation, quantisation) are
+// rolled loops over it, which keeps the code small enough for the
 // instruction cache.  Row reductions are warp shuffles (plus one named
 // barrier across the R warps); there are no CTA-wide barriers.  Arithmetic and rounding points are those of the kernels
 // these replace (rms_norm.py:47-57, fused_norm_residual.py:58-73,
@@ -55,7 +55,6 @@ __device__ __forceinline__ uint4 pack8_exact(const float v[8]) {
   return make_uint4(pack_exact(v[0], v[1]), pack_exact(v[2], v[3]), pack_exact(v[4], v[5]),
                     pack_exact(v[6], v[7]));
 }
-__device__ __forceinline__ uint4 ld_cs(const void* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
 __device__ __forceinline__ uint4 ld_nc(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 // |x| bit patterns of bf16 order like unsigned integers: running max of a chunk
 __device__ __forceinline__ uint32_t absmax8(const uint4& d, uint32_t m) {
@@ -164,28 +163,32 @@ __device__ __forceinline__ uint4 modulate(const uint4& y, const uint16_t* __rest
 
 // --- kernels ---------------------------------------------------------------------------
 
-// this warp's slice of the CTA's dynamic shared memory: cpl * 32 chunks
-__device__ __forceinline__ uint4* warp_slice(int cpl) {
+// this warp's slice of the CTA's dynamic shared memory: `nbuf` row buffers of
+// cpl * 32 chunks each; returns this lane's slot in buffer 0 (buffer j at + j*cpl*32)
+__device__ __forceinline__ uint4* warp_slice(int cpl, int nbuf) {
   extern __shared__ __align__(16) uint4 wr_smem[];
-  return wr_smem + (threadIdx.x >> 5) * cpl * 32 + (threadIdx.x & 31);
+  return wr_smem + (threadIdx.x >> 5) * nbuf * cpl * 32 + (threadIdx.x & 31);
 }
 
-// load the lane's cpl chunks (all in flight at once) into the warp slice;
-// returns the lane's exact partial sum of squares when SS
-template <int MAXC, bool SS>
-__device__ __forceinline__ double stage_row(const uint16_t* __restrict__ src, uint4* sl, int cpl) {
-  uint4 d[MAXC];
-#pragma unroll
-  for (int k = 0; k < MAXC; ++k)
-    if (k < cpl) d[k] = ld_cs(src + 256 * k);
+// issue the copies of this lane's cpl chunks of a row into its slots
+__device__ __forceinline__ void copy_row(const uint16_t* __restrict__ src, uint4* sl, int cpl) {
+  const uint32_t dst = (uint32_t)__cvta_generic_to_shared(sl);
+#pragma unroll 4
+  for (int k = 0; k < cpl; ++k)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 512u * k), "l"(src + 256 * k)
+                 : "memory");
+}
+
+// wait for this lane's copies (each lane reads back only its own slots)
+__device__ __forceinline__ void copies_done() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// exact partial sum of squares of this lane's chunks
+__device__ __forceinline__ double row_sumsq(const uint4* sl, int cpl) {
   double ss = 0.0;
-#pragma unroll
-  for (int k = 0; k < MAXC; ++k) {
-    if (k < cpl) {
-      sl[32 * k] = d[k];
-      if (SS) ss += sumsq8(d[k]);
-    }
-  }
+#pragma unroll 4
+  for (int k = 0; k < cpl; ++k) ss += sumsq8(sl[32 * k]);
   return ss;
 }
 
@@ -210,17 +213,18 @@ __device__ __forceinline__ void quant_row(const Team<R>& t, const uint4* sl, int
   if (t.wig == 0 && t.lane == 0) sx[row] = float_to_bf16_bits(s);
 }
 
-template <int R, int MAXC, bool HAD>
+template <int R, bool HAD>
 __global__ void __launch_bounds__(32 * kWarps) act_quant_wr(const uint16_t* __restrict__ x, int64_t ldx,
                                                             int8_t* __restrict__ q, int64_t ldq,
                                                             uint16_t* __restrict__ sx, int cpl, int64_t rows) {
   __shared__ uint32_t redu[kWarps];
   const Team<R> t;
   const int64_t f0 = t.first(cpl);
-  uint4* sl = warp_slice(cpl);
+  uint4* sl = warp_slice(cpl, 1);
   for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
        row += (int64_t)gridDim.x * (kWarps / R)) {
-    stage_row<MAXC, false>(x + row * ldx + f0, sl, cpl);
+    copy_row(x + row * ldx + f0, sl, cpl);
+    copies_done();
     uint32_t m = 0;
 #pragma unroll 1
     for (int k = 0; k < cpl; ++k) {
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(32 * kWarps) act_quant_wr(const uint16_t* __re
 }
 
 // MODE 0: rmsnorm -> bf16; 1: rmsnorm * (1+s) (+shift) -> bf16; 2: MODE 1 -> rotate / quant
-template <int R, int MAXC, int MODE, bool HAD>
+template <int R, int MODE, bool HAD>
 __global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
     const uint16_t* __restrict__ x, int64_t ldx, const float* __restrict__ w, const uint16_t* __restrict__ scale,
     const uint16_t* __restrict__ shift, int64_t ld_mod, int64_t rows_per_batch, uint16_t* __restrict__ y,
@@ -245,11 +249,12 @@ __global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
   const Team<R> t;
   const int64_t f0 = t.first(cpl);
   const float* wl = w + f0;
-  uint4* sl = warp_slice(cpl);
+  uint4* sl = warp_slice(cpl, 1);
   for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
        row += (int64_t)gridDim.x * (kWarps / R)) {
-    const double ss = stage_row<MAXC, true>(x + row * ldx + f0, sl, cpl);
-    const float rstd = rstd_from_sum(t.sum(ss, redd), (int)n, eps);
+    copy_row(x + row * ldx + f0, sl, cpl);
+    copies_done();
+    const float rstd = rstd_from_sum(t.sum(row_sumsq(sl, cpl), redd), (int)n, eps);
     const int64_t mo = (row / rows_per_batch) * ld_mod + f0;
     uint16_t* yr = MODE <= 1 ? y + row * ldy + f0 : nullptr;
     uint32_t m = 0;
@@ -265,12 +270,12 @@ __global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
       }
     }
     if (MODE == 2) quant_row<R>(t, sl, cpl, m, redu, row, q, ldq, sx);
-    __syncwarp();
+    __syncwarp();  // the slot is rewritten by the next row's copies
   }
 }
 
 // y = r + g * rmsnorm(x); FUSE: then rmsnorm(y; w2) * (1+s) (+shift) -> rotate / quant
-template <int R, int MAXC, bool FUSE, bool HAD>
+template <int R, bool FUSE, bool HAD>
 __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
     const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ r, int64_t ldr,
     const uint16_t* __restrict__ gate, int64_t ld_gate, int64_t rows_per_batch, const float* __restrict__ w,
@@ -282,19 +287,20 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
   const Team<R> t;
   const int64_t f0 = t.first(cpl);
   const float* wl = w + f0;
-  uint4* sl = warp_slice(cpl);
+  uint4* sl = warp_slice(cpl, 1);  // x, then y
   for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
        row += (int64_t)gridDim.x * (kWarps / R)) {
-    const double ss = stage_row<MAXC, true>(x + row * ldx + f0, sl, cpl);
-    const float rstd = rstd_from_sum(t.sum(ss, redd), (int)n, eps);
+    const uint16_t* rr = r + row * ldr + f0;
+    copy_row(x + row * ldx + f0, sl, cpl);
+    copies_done();
+    const float rstd = rstd_from_sum(t.sum(row_sumsq(sl, cpl), redd), (int)n, eps);
     const int64_t b = row / rows_per_batch;
     const uint16_t* gl = gate + b * ld_gate + f0;
-    const uint16_t* rr = r + row * ldr + f0;
     uint16_t* yr = y + row * ldy + f0;
     double ss2 = 0.0;
 #pragma unroll 4
     for (int k = 0; k < cpl; ++k) {
-      const uint4 e = ld_cs(rr + 256 * k);
+      const uint4 e = __ldcs(reinterpret_cast<const uint4*>(rr + 256 * k));
       const uint4 a = norm_w(sl[32 * k], rstd, wl + 256 * k);
       const uint4 g = ld_nc(gl + 256 * k);
       // bf16(r + bf16(g * a)), fused_norm_residual.py:69-73
@@ -327,7 +333,8 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
 // --- host side ---------------------------------------------------------------------------
 
 // Team size and chunks per lane for a row of n bf16: n % 256 == 0 and at most
-// MAXC (16) chunks per lane; false -> the caller uses another kernel.
+// 16 chunks (8 KB of shared memory per row buffer) per warp; false -> the
+// caller uses another kernel.
 static inline bool pick(int64_t n, int* R, int* cpl) {
   if (n <= 0 || n % 256) return false;
   const int64_t t = n / 256;
@@ -341,13 +348,14 @@ static inline bool pick(int64_t n, int* R, int* cpl) {
   return false;
 }
 
-// dynamic shared memory of a CTA: kWarps slices of cpl * 32 chunks
-static inline size_t smem_for(int cpl) { return (size_t)kWarps * cpl * 32 * 16; }
+// dynamic shared memory of a CTA: kWarps slices of nbuf row buffers of cpl * 32 chunks
+static inline size_t smem_for(int cpl, int nbuf) { return (size_t)kWarps * nbuf * cpl * 32 * 16; }
 
 template <class K>
-static int grid_for(K kernel, int R, int cpl, int64_t rows) {
+static int grid_for(K kernel, int R, int cpl, int nbuf, int64_t rows) {
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32 * kWarps, smem_for(cpl)) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32 * kWarps, smem_for(cpl, nbuf)) !=
+          cudaSuccess ||
       per_sm < 1) {
     cudaGetLastError();
     per_sm = 1;
@@ -357,21 +365,22 @@ static int grid_for(K kernel, int R, int cpl, int64_t rows) {
   return (int)(need < g ? need : g);
 }
 
-// Calls f(integral_constant<R>, integral_constant<MAXC>, cpl) for the team
-// size picked for n; false when n has no warp-row shape.
+template <class K>
+static void set_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// Calls f(integral_constant<R>, cpl) for the team size picked for n; false when
+// n has no warp-row shape.
 template <class F>
 static bool dispatch(int64_t n, F&& f) {
   int R, cpl;
   if (!pick(n, &R, &cpl)) return false;
   using std::integral_constant;
-  if (R == 1 && cpl <= 4) f(integral_constant<int, 1>{}, integral_constant<int, 4>{}, cpl);
-  else if (R == 1 && cpl <= 8) f(integral_constant<int, 1>{}, integral_constant<int, 8>{}, cpl);
-  else if (R == 1) f(integral_constant<int, 1>{}, integral_constant<int, 16>{}, cpl);
-  else if (R == 2) f(integral_constant<int, 2>{}, integral_constant<int, 16>{}, cpl);
-  else if (cpl <= 12) f(integral_constant<int, 4>{}, integral_constant<int, 12>{}, cpl);
-  else f(integral_constant<int, 4>{}, integral_constant<int, 16>{}, cpl);
+  if (R == 1) f(integral_constant<int, 1>{}, cpl);
+  else if (R == 2) f(integral_constant<int, 2>{}, cpl);
+  else f(integral_constant<int, 4>{}, cpl);
   return true;
 }
 
 }  // namespace wr
-
