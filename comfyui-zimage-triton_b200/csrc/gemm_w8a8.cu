@@ -446,8 +446,7 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
     load_bf16x8(c.xbuf + xoff_256(r2, sub), v);
     fwht8(v);
     fwht_cross16(v, c.lane);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = mul_round_bf16(v[j], kHBf16);
+    had_round8(v);
     const int grow = c.row_base + r2;
     if (grow < p.M) store_bf16x8(p.y + (int64_t)grow * p.ldy + nb * 128 + sub * 8, v);
   }

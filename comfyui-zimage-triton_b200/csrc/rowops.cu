@@ -641,32 +641,6 @@ __device__ __forceinline__ double cta_sum(double v, double* red) {
 
 // --- cheap exact roundings ------------------------------------------------------
 
-__device__ __forceinline__ void bf16_round2(float& a, float& b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  uint32_t w = *reinterpret_cast<uint32_t*>(&h);
-  a = __uint_as_float(w << 16);
-  b = __uint_as_float(w & 0xFFFF0000u);
-}
-
-__device__ __forceinline__ void had_round8(float v[8]) {
-  float p[8];
-  bool tie = false;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    p[j] = __fmul_rn(v[j], kHBf16);
-    tie |= (__float_as_uint(p[j]) & 0xFFFFu) == 0x8000u;
-  }
-  if (__any_sync(0xFFFFFFFFu, tie)) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = mul_round_bf16(v[j], kHBf16);
-    return;
-  }
-#pragma unroll
-  for (int j = 0; j < 8; j += 2) bf16_round2(p[j], p[j + 1]);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = p[j];
-}
-
 __device__ __forceinline__ void quant8(const float v[8], float s, float rcp, int q[8]) {
   float t[8];
   bool near = false;

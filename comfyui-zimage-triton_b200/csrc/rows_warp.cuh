@@ -122,7 +122,7 @@ __device__ __forceinline__ void rot_amax(uint4& d, uint32_t& m, int lane) {
     float v[8];
     unpack8(d, v);
     pipe::fwht128(v, lane);
-    pipe::had_round8(v);
+    had_round8(v);
     d = pack8_exact(v);
   }
   m = absmax8(d, m);

@@ -82,9 +82,9 @@ __device__ __forceinline__ float act_scale(float amax_bf16) {
 // --- bit-reproducible fp32 exp / sigmoid / tanh ---------------------------
 // exp(x) by Cody & Waite two-constant range reduction, x = k*ln2 + r with
 // |r| <= ln2/2, and the degree-7 Taylor polynomial of e^r evaluated by Horner,
-// then an exact scaling by 2^k.  Only separately rounded IEEE multiplies and
-// adds are used (no FMA contraction), so the oracle replays it exactly with
-// numpy float32 arithmetic.  Accuracy: within 2 ulp of exp on [-87, 88].
+// then an exact scaling by 2^k.  Only IEEE fp32 operations with one rounding
+// each (multiplies, adds, fused multiply-adds) are used, so the oracle replays
+// it exactly.  Accuracy: within 2 ulp of exp on [-87, 88].
 constexpr float kInvLn2 = 1.44269502f;
 constexpr float kLn2Hi = 0.693145751953125f;   // 16 significant bits: k*kLn2Hi is exact
 constexpr float kLn2Lo = 1.42860677e-06f;
@@ -101,16 +101,16 @@ __device__ __forceinline__ float zib_expf(float x) {
   const float t = __fadd_rn(__fmul_rn(x, kInvLn2), 12582912.0f);
   const int ki = (int)__float_as_uint(t) - 0x4B400000;
   const float k = __fsub_rn(t, 12582912.0f);
-  float r = __fsub_rn(x, __fmul_rn(k, kLn2Hi));
-  r = __fsub_rn(r, __fmul_rn(k, kLn2Lo));
+  float r = __fmaf_rn(-k, kLn2Hi, x);
+  r = __fmaf_rn(-k, kLn2Lo, r);
   float p = kExpC7;
-  p = __fadd_rn(__fmul_rn(p, r), kExpC6);
-  p = __fadd_rn(__fmul_rn(p, r), kExpC5);
-  p = __fadd_rn(__fmul_rn(p, r), kExpC4);
-  p = __fadd_rn(__fmul_rn(p, r), kExpC3);
-  p = __fadd_rn(__fmul_rn(p, r), 0.5f);
-  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
-  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  p = __fmaf_rn(p, r, kExpC6);
+  p = __fmaf_rn(p, r, kExpC5);
+  p = __fmaf_rn(p, r, kExpC4);
+  p = __fmaf_rn(p, r, kExpC3);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
   // p * 2^k exactly: for x in [-87, 88], k is in [-126, 127] and p in [0.70, 1.42]
   // (p >= 1 when k = -126, since x >= -87 > -126 ln2), so the result is a normal
   // number and adding k to the exponent field equals ldexp
@@ -185,6 +185,38 @@ __device__ __forceinline__ void store_i8x8(void* p, const int q[8]) {
   uint32_t a = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
   uint32_t b = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
   *reinterpret_cast<uint2*>(p) = make_uint2(a, b);
+}
+
+// --- cheap exact roundings --------------------------------------------------
+
+// round a pair of fp32 values to bf16 (RNE), results as fp32
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  uint32_t w = *reinterpret_cast<uint32_t*>(&h);
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xFFFF0000u);
+}
+
+// v[j] = mul_round_bf16(v[j], kHBf16) for 8 values: one RN multiply + packed
+// rounding, with the exact-residual fix-up only when some lane of the warp has
+// a product on a bf16 midpoint (every lane of the warp must call this)
+__device__ __forceinline__ void had_round8(float v[8]) {
+  float p[8];
+  bool tie = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    p[j] = __fmul_rn(v[j], kHBf16);
+    tie |= (__float_as_uint(p[j]) & 0xFFFFu) == 0x8000u;
+  }
+  if (__any_sync(0xFFFFFFFFu, tie)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = mul_round_bf16(v[j], kHBf16);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) bf16_round2(p[j], p[j + 1]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = p[j];
 }
 
 // --- Walsh-Hadamard transform over 128 (Sylvester order) ------------------

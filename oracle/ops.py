@@ -269,11 +269,13 @@ def norm_gate_residual(x, residual, gate, w, eps: float = 1e-5):
 # fp32 exp / sigmoid / tanh with a fixed operation order
 # ---------------------------------------------------------------------------
 # exp by Cody & Waite two-constant range reduction (x = k ln2 + r, |r| <= ln2/2)
-# and the degree-7 Taylor polynomial of e^r in Horner form, then an exact
-# scaling by 2^k; every step is one IEEE fp32 operation, so this restatement
-# and the CUDA kernels produce identical bits.  The reference computes these
-# functions with Triton's / torch's own fp32 implementations (swiglu.py:55,
-# adaln_modulation.py:73-74, patching_comfyui.py:371-372); all agree to a few ulp.
+# and the degree-7 Taylor polynomial of e^r in Horner form with fused
+# multiply-adds, then an exact scaling by 2^k; every step is one IEEE fp32
+# operation (fma_f32 below restates the fused multiply-add exactly), so this
+# restatement and the CUDA kernels produce identical bits.  The reference
+# computes these functions with Triton's / torch's own fp32 implementations
+# (swiglu.py:55, adaln_modulation.py:73-74, patching_comfyui.py:371-372); all
+# agree to a few ulp.
 
 _F = np.float32
 EXP_C = [_F(1.98412701e-04), _F(1.38888892e-03), _F(8.33333377e-03), _F(4.16666679e-02),
@@ -283,14 +285,38 @@ TANH_C = [_F(-8.86323552e-03), _F(2.18694880e-02), _F(-5.39682545e-02), _F(1.333
           _F(-3.33333343e-01)]
 
 
+def fma_f32(a, b, c) -> np.ndarray:
+    """IEEE fp32 fused multiply-add, RN(a*b + c) with a single rounding.
+
+    a*b is exact in fp64 (2 x 24 significant bits); TwoSum gives prod + c = s + err
+    exactly; RN32(s + err) equals RN32(s) unless s is exactly halfway between two
+    fp32 values, where the sign of err picks the neighbour.
+    """
+    a64 = np.asarray(a, dtype=_F).astype(np.float64)
+    b64 = np.asarray(b, dtype=_F).astype(np.float64)
+    c64 = np.asarray(c, dtype=_F).astype(np.float64)
+    prod = a64 * b64
+    s = prod + c64
+    bb = s - prod
+    err = (prod - (s - bb)) + (c64 - bb)
+    r = s.astype(_F)
+    r64 = r.astype(np.float64)
+    other = 2.0 * s - r64                      # the other fp32 neighbour when s is a midpoint
+    tie = (s != r64) & (other.astype(_F).astype(np.float64) == other) & (err != 0)
+    up = np.maximum(r64, other)
+    dn = np.minimum(r64, other)
+    fixed = np.where(err > 0, up, dn).astype(_F)
+    return np.where(tie, fixed, r).astype(_F)
+
+
 def exp_f32(x: np.ndarray) -> np.ndarray:
     x = np.minimum(np.maximum(np.asarray(x, dtype=_F), _F(-87.0)), _F(88.0))
     k = np.rint(x * INV_LN2).astype(_F)
-    r = (x - k * LN2_HI).astype(_F)
-    r = (r - k * LN2_LO).astype(_F)
+    r = fma_f32(-k, LN2_HI, x)
+    r = fma_f32(-k, LN2_LO, r)
     p = np.full_like(r, EXP_C[0])
     for c in EXP_C[1:]:
-        p = (p * r).astype(_F) + c
+        p = fma_f32(p, r, c)
     return np.ldexp(p.astype(_F), k.astype(np.int32)).astype(_F)
 
 
