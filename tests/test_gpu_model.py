@@ -226,3 +226,24 @@ def test_reference_policy_mixed_bf16_and_int8_layers(cuda):
         y = m(x.cuda(), t.cuda(), fm.cuda()).cpu()
     assert torch.isfinite(y.float()).all()
     assert "_zib_cache" in m.layers[1].__dict__ and "_zib_cache" not in m.layers[0].__dict__
+
+
+def test_captured_step_replays_the_eager_step(cuda):
+    """One CUDA graph per step (zimage_b200.graph.CapturedStep) gives the eager step's bits."""
+    from zimage_b200.graph import CapturedStep
+
+    dim, heads, ffn = 1024, 8, 2816
+    m, _ = _small_model(2, dim, heads, ffn)
+    _patch(m)
+    x, t, fm, _ = _inputs(2, 8, 8, 16, dim)
+    xd, td, fmd = x.cuda(), t.cuda(), fm.cuda()
+    with torch.no_grad():
+        want = m(xd, td, fmd).clone()
+        x2 = (xd.float() * 0.5).to(torch.bfloat16)
+        want2 = m(x2, td, fmd).clone()
+    cap = CapturedStep(lambda a, b: m(a, b, fmd), xd, td)
+    assert torch.equal(cap(xd, td), want)
+    assert torch.equal(cap(x2, td).clone(), want2)   # new inputs are copied in before the replay
+    assert torch.equal(cap(x.pin_memory(), t.pin_memory()), want)  # host inputs, copied in
+    with pytest.raises(ValueError):
+        cap(xd[:1], td)
