@@ -40,6 +40,10 @@ DIM, HEADS, FFN, LAYERS, ADALN = 3840, 30, 10240, 30, 256
 GRID, N_TXT, B_CFG = 64, 512, 2
 SEQ = GRID * GRID + N_TXT
 INT8_DATASHEET_TOPS = 4500.0  # B200 dense INT8 (no INT8 entry in MEASURED_PEAKS.json)
+# DRAM bytes (read + write) per launch of each GEMM entry point at the step shapes, from
+# one ncu capture (profiles/gemm_w8a8_epilogues_9216rows.md)
+NCU_TRAFFIC = {"zib_gemm_w8a8_swiglu_had": 287554304, "zib_gemm_w8a8_qk_norm_rope": 285878784}
+NCU_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/gemm_w8a8_epilogues_9216rows.md"
 WORKLOAD = ("30-layer S3-DiT step at 1024x1024 (4096 image + 512 text tokens), CFG pair B=2, "
             "all linears W8A8+Hadamard128, bf16 SDPA")
 
@@ -345,8 +349,15 @@ def run_ours(args) -> None:
         torch.cuda.synchronize()
     gem = pc.GEMM_EVENTS
     pc.GEMM_EVENTS = None
-    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gem)
-    gemm_ops = sum(o for _, _, o in gem)
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _, _ in gem)
+    gemm_ops = sum(o for _, _, o, _ in gem)
+    per_kernel = {}
+    for a_, b_, o_, name_ in gem:
+        k = per_kernel.setdefault(name_, {"launches": 0, "ms": 0.0, "ops": 0})
+        k["launches"] += 1
+        k["ms"] += a_.elapsed_time(b_)
+        k["ops"] += o_
+    dominant = max(per_kernel, key=lambda k: per_kernel[k]["ms"]) if per_kernel else None
     if world > 1:
         t = torch.tensor([elapsed], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -388,7 +399,13 @@ def run_ours(args) -> None:
 
     if rank == 0:
         ms_step = elapsed / args.steps
-        achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+        dk = per_kernel.get(dominant) if dominant else None
+        achieved = dk["ops"] / (dk["ms"] * 1e-3) / 1e12 if dk and dk["ms"] > 0 else None
+        gemm_tops = gemm_ops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+        kernels = {k: {"launches": v["launches"], "avg_launch_us": round(v["ms"] * 1e3 / v["launches"], 2),
+                       "tops": round(v["ops"] / (v["ms"] * 1e-3) / 1e12, 1),
+                       "frac": round(v["ops"] / (v["ms"] * 1e-3) / 1e12 / INT8_DATASHEET_TOPS, 4)}
+                   for k, v in per_kernel.items()}
         peaks = _peaks()
         rec = {
             "metric": METRIC, "value": round(ms_step / world, 3), "unit": "ms", "n_gpus": world,
@@ -399,7 +416,7 @@ def run_ours(args) -> None:
                        "parallelism": f"dp{world} (images)",
                        "cuda_graph": cap is not None,
                        "l2": "no flush: 5.4 GB int8 weights streamed per step >> 126 MB L2"},
-            "roofline": {"kernel": "zib_gemm_w8a8 (tcgen05 kind::i8)", "bound": "tensor",
+            "roofline": {"kernel": f"{dominant} (tcgen05 kind::i8)", "bound": "tensor",
                          "achieved": None if achieved is None else round(achieved, 1),
                          "peak": INT8_DATASHEET_TOPS, "unit": "TOPS",
                          "frac": None if achieved is None else round(achieved / INT8_DATASHEET_TOPS, 4),
@@ -407,11 +424,15 @@ def run_ours(args) -> None:
                          "int_mm_measured_tops": None if int_mm_tops is None else round(int_mm_tops, 1),
                          "frac_of_int_mm": None if (achieved is None or not int_mm_tops)
                          else round(achieved / int_mm_tops, 4),
-                         "launches": len(gem), "avg_launch_us": round(gemm_ms * 1e3 / max(1, len(gem)), 2),
+                         "launches": per_kernel[dominant]["launches"] if dominant else 0,
+                         "avg_launch_us": kernels[dominant]["avg_launch_us"] if dominant else None,
+                         "traffic": NCU_TRAFFIC.get(dominant),
+                         "traffic_source": NCU_TRAFFIC_SOURCE,
+                         "all_gemms_tops": None if gemm_tops is None else round(gemm_tops, 1),
                          "gemm_share_of_step": round((gemm_ms / gemm_steps) / max(elapsed / args.steps, 1e-9), 4),
+                         "gemm_kernels": kernels,
                          "timing": "CUDA events around each GEMM launch" + (
-                             "" if cap is None else " in eager steps right after the graph-timed region"),
-                         "traffic": None},
+                             "" if cap is None else " in eager steps right after the graph-timed region")},
             "e2e": {"value": round(e2e_ms / args.steps / world, 3), "unit": "ms",
                     "h2d_bytes_per_step": xh.numel() * 2 + th.numel() * 2,
                     "d2h_bytes_per_step": yh.numel() * 2},

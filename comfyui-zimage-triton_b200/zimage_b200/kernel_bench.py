@@ -49,14 +49,14 @@ def _empty(*shape, dtype=torch.bfloat16):
     return torch.empty(*shape, dtype=dtype, device="cuda")
 
 
-def case_act_quant(M=M_TOK, K=D):
+def case_act_quant(M=M_TOK, K=D, had=1):
     x, q, sx = _bf16(M, K), _empty(M, K, dtype=torch.int8), _empty(M)
     st = _lib.stream_of(x)
 
     def run():
-        _lib.call("zib_act_quant", x.data_ptr(), K, q.data_ptr(), K, sx.data_ptr(), None, M, K, 1, st)
+        _lib.call("zib_act_quant", x.data_ptr(), K, q.data_ptr(), K, sx.data_ptr(), None, M, K, had, st)
 
-    return run, M * K * 2 + M * K + M * 2, f"[{M},{K}] bf16 -> int8"
+    return run, M * K * 2 + M * K + M * 2, f"[{M},{K}] bf16 -> {'rot128 -> ' if had else ''}int8"
 
 
 def case_rmsnorm_mod_quant(M=M_TOK, Dm=D):
@@ -206,6 +206,7 @@ CASES = {
     "act_quant": (lambda: case_act_quant(), "hbm"),
     "act_quant_m1024": (lambda: case_act_quant(1024, D), "hbm"),
     "act_quant_k10240": (lambda: case_act_quant(M_TOK, F), "hbm"),
+    "act_quant_plain_k10240": (lambda: case_act_quant(M_TOK, F, had=0), "hbm"),
     "rmsnorm_mod_quant": (lambda: case_rmsnorm_mod_quant(), "hbm"),
     "norm_gate_residual_mod_quant": (lambda: case_norm_gate_residual_mod_quant(), "hbm"),
     "norm_gate_residual": (lambda: case_norm_gate_residual(), "hbm"),

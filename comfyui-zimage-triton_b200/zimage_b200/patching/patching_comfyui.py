@@ -271,8 +271,8 @@ def _block_cache(block: nn.Module):
     return c
 
 
-# When a list, every fused-path GEMM appends (start_event, end_event, 2*M*N*K)
-# recorded on its launch stream (used by the benchmark's roofline figures).
+# When a list, every fused-path GEMM appends (start_event, end_event, 2*M*N*K,
+# entry point name) recorded on its launch stream (the benchmark's roofline figures).
 GEMM_EVENTS: list | None = None
 
 
@@ -284,7 +284,7 @@ def _timed_call(name: str, ops_count: int, *args) -> None:
     _lib.call(name, *args)
     if ev is not None:
         e1.record()
-        ev.append((e0, e1, ops_count))
+        ev.append((e0, e1, ops_count, name))
 
 
 def _gemm(q8, sx, lin_w, lin_s, y, M, N, K, stream):
