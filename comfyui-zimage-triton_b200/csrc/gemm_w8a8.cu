@@ -86,6 +86,7 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 struct Params {
   int M, N, K;  // N: output columns (SWIGLU: features)
   int num_mb, num_nb, num_kb, num_tiles;
+  int n_fast;  // tile order: 0 = M-blocks fastest (B read once), 1 = N-blocks fastest (A read once)
   const uint16_t* sx;
   const uint16_t* sw;   // per weight row (SWIGLU: w1 scales)
   const uint16_t* sw2;  // SWIGLU: w3 scales
@@ -589,6 +590,19 @@ __device__ __forceinline__ void load_b_part(uint8_t* dst, const CUtensorMap* b0,
   }
 }
 
+// Tile t -> (M-block, N-block).  Consecutive tiles run concurrently on the
+// persistent CTAs, so the fastest-varying block index decides which operand
+// stays resident in L2 while the other one streams.
+__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mb, int& nb) {
+  if (p.n_fast) {
+    mb = tile / p.num_nb;
+    nb = tile % p.num_nb;
+  } else {
+    mb = tile % p.num_mb;
+    nb = tile / p.num_mb;
+  }
+}
+
 // --- kernels -------------------------------------------------------------------
 
 template <int EPI>
@@ -643,7 +657,8 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1)
       uint32_t phase = 0, pend_mask = 0, pend_parity = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile % p.num_mb, nb = tile / p.num_mb;
+        int mb, nb;
+        tile_coords(p, tile, mb, nb);
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           uint8_t* st = smem + stage * S_STAGE_BYTES;
@@ -706,7 +721,8 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1)
       if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = group_bar_and(bar_id, Cfg<EPI>::NQ * 32, ok);
       if (!ok) break;
       tc_fence_after();
-      const int mb = tile % p.num_mb, nb = tile / p.num_mb;
+      int mb, nb;
+        tile_coords(p, tile, mb, nb);
       const EpiCtx c{tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN), mb * 128, quarter,
                      cq, lane, bar_id, xbuf};
       epilogue_tile<EPI>(p, c, nb, ReleaseLocal{&tempty_bar[accb]});
@@ -781,7 +797,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
       uint32_t phase = 0, pend_mask = 0, pend_parity = 0;
       bool ok = true;
       for (int tile = cluster_id; tile < p.num_tiles && ok; tile += nclusters) {
-        const int mb = tile % p.num_mb, nb = tile / p.num_mb;
+        int mb, nb;
+        tile_coords(p, tile, mb, nb);
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
@@ -849,7 +866,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
       if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = group_bar_and(bar_id, Cfg<EPI>::NQ * 32, ok);
       if (!ok) { aborted = true; break; }
       tc_fence_after();
-      const int mb = tile % p.num_mb, nb = tile / p.num_mb;
+      int mb, nb;
+        tile_coords(p, tile, mb, nb);
       const EpiCtx c{tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN),
                      mb * 256 + (int)rank * 128, quarter, cq, lane, bar_id, xbuf};
       epilogue_tile<EPI>(p, c, nb, ReleaseLeader{mapa_rank(smem_u32(&tempty_bar[accb]), 0)});
@@ -975,6 +993,10 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
     }
     attr_set[pair][EPI][dev] = true;
   }
+  // The operand that is read once per wave of concurrent tiles is the one whose
+  // block index varies fastest: stream the smaller one, keep the larger one resident.
+  const int64_t a_bytes = M * K, b_bytes = (int64_t)w_rows * K * (EPI == EPI_SWIGLU ? 2 : 1);
+  p.n_fast = a_bytes > b_bytes ? 1 : 0;
   const int sms = num_sms_for_current_device();
   if (pair) {
     p.num_mb = (int)((M + 255) / 256);

@@ -72,7 +72,8 @@ def gemm_variant(request):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 256, 128), (7, 40, 32), (200, 300, 160), (257, 513, 384),
-                                   (128, 256, 3840), (300, 1024, 10240), (1024, 11520, 3840)])
+                                   (128, 256, 3840), (300, 1024, 10240), (1024, 11520, 3840),
+                                   (2000, 300, 1024)])  # last: A larger than B -> N-blocks-first tile order
 def test_gemm_int32_accumulators_bitexact(cuda, gemm_variant, M, N, K):
     q = _rand_i8((M, K), 1)
     w = _rand_i8((N, K), 2)
@@ -88,7 +89,7 @@ def test_gemm_int32_accumulators_bitexact(cuda, gemm_variant, M, N, K):
 
 @pytest.mark.parametrize("M,N,K,bias", [(48, 256, 384, True), (129, 300, 256, False),
                                         (512, 3840, 3840, False), (64, 20480, 3840, True),
-                                        (600, 1000, 512, True)])
+                                        (600, 1000, 512, True), (2304, 520, 1024, False)])
 def test_gemm_dequant_epilogue_bitexact(cuda, gemm_variant, M, N, K, bias):
     x = seeded_x(M, K, seed=3)
     w = seeded_w(N, K, seed=4)
@@ -106,7 +107,8 @@ def test_gemm_dequant_epilogue_bitexact(cuda, gemm_variant, M, N, K, bias):
     assert torch.equal(y[:, :N].cpu(), want)
 
 
-@pytest.mark.parametrize("M,F,K", [(48, 128, 384), (129, 384, 256), (300, 1280, 3840), (1024, 10240, 3840)])
+@pytest.mark.parametrize("M,F,K", [(48, 128, 384), (129, 384, 256), (300, 1280, 3840), (1024, 10240, 3840),
+                                   (1100, 128, 256)])
 def test_gemm_swiglu_hadamard_epilogue(cuda, gemm_variant, M, F, K):
     """w1/w3 GEMMs + SwiGLU + w2-input rotation in one launch vs the oracle's composition."""
     x = seeded_x(M, K, seed=13)
