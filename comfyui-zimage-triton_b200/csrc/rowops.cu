@@ -658,8 +658,10 @@ __device__ __forceinline__ void quant8(const float v[8], float s, float rcp, int
   for (int j = 0; j < 8; j += 2) bf16_round2(t[j], t[j + 1]);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    int i = __float_as_int(__fadd_rn(t[j], 12582912.0f)) - 0x4B400000;  // rint via 1.5*2^23
-    q[j] = max(min(i, 127), -128);
+    // round half to even and saturate to [-128, 127] in one conversion (low byte is stored)
+    int i;
+    asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(i) : "f"(t[j]));
+    q[j] = i;
   }
 }
 
