@@ -30,7 +30,8 @@ def _restore_original_forwards(transformer) -> None:  # noqa: ANN001
         if hasattr(module, "_original_silu_gating"):
             module._forward_silu_gating = module._original_silu_gating
             delattr(module, "_original_silu_gating")
-        module.__dict__.pop("_zib_cache", None)
+        for key in ("_zib_cache", "_zib_next", "_zib_fused_ok"):
+            module.__dict__.pop(key, None)
 
     for name, child in list(transformer.named_modules()):
         original = getattr(child, "_original_module", None)

@@ -247,3 +247,23 @@ def test_captured_step_replays_the_eager_step(cuda):
     assert torch.equal(cap(x.pin_memory(), t.pin_memory()), want)  # host inputs, copied in
     with pytest.raises(ValueError):
         cap(xd[:1], td)
+
+
+def test_block_handoff_equals_per_block_path(cuda):
+    """The block-final norm fused with the next block's first norm + quantisation is bit-identical."""
+    from zimage_b200.patching import patching_comfyui as pc
+
+    dim, heads, ffn = 1024, 8, 2816
+    m, _ = _small_model(3, dim, heads, ffn)
+    _patch(m)
+    assert m.layers[0].__dict__["_zib_next"] is m.layers[1] and m.layers[2].__dict__["_zib_next"] is None
+    x, t, fm, _ = _inputs(2, 8, 8, 16, dim)
+    with torch.no_grad():
+        y_handoff = m(x.cuda(), t.cuda(), fm.cuda())
+        assert pc._HANDOFF is None  # consumed by the next block, none left after the last one
+        pc.ENABLE_BLOCK_HANDOFF = False
+        try:
+            y_plain = m(x.cuda(), t.cuda(), fm.cuda())
+        finally:
+            pc.ENABLE_BLOCK_HANDOFF = True
+    assert torch.equal(y_handoff, y_plain)
