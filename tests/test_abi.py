@@ -48,6 +48,17 @@ def test_host_validation_before_launch():
     assert lib.zib_gemm_w8a8(16, 24, 16, 24, 16, 16, None, 16, 8, 4, 8, 24, None) == _lib.ZIB_ERR_ALIGNMENT
     assert lib.zib_qknorm_rope(16, 0, 0, 0, 16, 0, 0, 0, 16, 16, 0, None, 1, 1, 1, 64, 1e-5, None) == \
         _lib.ZIB_ERR_INVALID_ARG
+    # fused-epilogue GEMMs: features not a multiple of the 128-group; odd head count
+    assert lib.zib_gemm_w8a8_swiglu_had(16, 128, 16, 16, 128, 16, 16, 16, 16, 200, 8, 200, 128, None) == \
+        _lib.ZIB_ERR_INVALID_ARG
+    assert lib.zib_gemm_w8a8_qk_norm_rope(16, 128, 16, 128, 16, 16, 16, 1152, 8, 1152, 128, 16, 16, 1e-5, 1e-5,
+                                          16, 16, 0, 8, 3, None) == _lib.ZIB_ERR_INVALID_ARG
+    # M not a multiple of the sequence length
+    assert lib.zib_gemm_w8a8_qk_norm_rope(16, 128, 16, 128, 16, 16, 16, 768, 9, 768, 128, 16, 16, 1e-5, 1e-5,
+                                          16, 16, 0, 8, 2, None) == _lib.ZIB_ERR_INVALID_ARG
+    # misaligned output of the SwiGLU epilogue
+    assert lib.zib_gemm_w8a8_swiglu_had(16, 128, 16, 16, 128, 16, 16, 16, 18, 128, 8, 128, 128, None) == \
+        _lib.ZIB_ERR_ALIGNMENT
     with pytest.raises(ValueError):
         _lib.check(_lib.ZIB_ERR_INVALID_ARG, "x")
     with pytest.raises(RuntimeError):
