@@ -371,16 +371,22 @@ def run_ours(args) -> None:
     if world > 1:
         dist.barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    yhs = [yh] + [torch.empty_like(yh).pin_memory() for _ in range(min(args.steps, 2) - 1)]
+    torch.cuda.synchronize()
     f0.record()
-    for _ in range(args.steps):
-        if cap is not None:
-            yd = cap(xh, th)  # H2D straight into the graph's input buffers, then replay
-        else:
+    if cap is not None:
+        # host inputs in / outputs out on a copy stream, overlapped with the graph replays
+        from zimage_b200.graph import run_steps_overlapped
+
+        run_steps_overlapped(cap, [(xh, th)] * args.steps, [yhs[i % len(yhs)] for i in range(args.steps)])
+        yd = cap.static_out
+    else:
+        for _ in range(args.steps):
             xd = xh.to(dev, non_blocking=True)
             td = th.to(dev, non_blocking=True)
             with torch.no_grad():
                 yd = model(xd, td, freqs)
-        yh.copy_(yd, non_blocking=True)
+            yh.copy_(yd, non_blocking=True)
     gather(yd)
     f1.record()
     torch.cuda.synchronize()

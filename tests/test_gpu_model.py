@@ -267,3 +267,24 @@ def test_block_handoff_equals_per_block_path(cuda):
         finally:
             pc.ENABLE_BLOCK_HANDOFF = True
     assert torch.equal(y_handoff, y_plain)
+
+
+def test_overlapped_host_io_steps_match_sequential(cuda):
+    """run_steps_overlapped (copy stream for host I/O) gives every step's exact output."""
+    from zimage_b200.graph import CapturedStep, run_steps_overlapped
+
+    dim, heads, ffn = 1024, 8, 2816
+    m, _ = _small_model(1, dim, heads, ffn)
+    _patch(m)
+    x, t, fm, _ = _inputs(2, 8, 8, 16, dim)
+    fmd = fm.cuda()
+    xs = [(x * s).to(torch.bfloat16).pin_memory() for s in (1.0, 0.5, -0.25)]
+    tp = t.pin_memory()
+    with torch.no_grad():
+        want = [m(xi.cuda(), t.cuda(), fmd).cpu() for xi in xs]
+    cap = CapturedStep(lambda a, b: m(a, b, fmd), xs[0].cuda(), t.cuda())
+    outs = [torch.empty_like(w).pin_memory() for w in want]
+    run_steps_overlapped(cap, [(xi, tp) for xi in xs], outs)
+    torch.cuda.synchronize()
+    for o, w in zip(outs, want):
+        assert torch.equal(o, w)
