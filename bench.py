@@ -39,7 +39,8 @@ METRIC = "DiT step ms at 1024² (6B, W8A8); INT8 GEMM TOPS and % of peak"
 DIM, HEADS, FFN, LAYERS, ADALN = 3840, 30, 10240, 30, 256
 GRID, N_TXT, B_CFG = 64, 512, 2
 SEQ = GRID * GRID + N_TXT
-INT8_DATASHEET_TOPS = 4500.0  # B200 dense INT8 (no INT8 entry in MEASURED_PEAKS.json)
+INT8_DATASHEET_TOPS = 4500.0  # B200 dense INT8, datasheet (the measured peaks hold bf16 and HBM only)
+HBM_FALLBACK_GBS = 6650.0  # STREAM-style copy measured earlier on this hardware, used without MEASURED_PEAKS.json
 # DRAM bytes (read + write) per launch of each GEMM entry point at the step shapes, from
 # one ncu capture (profiles/gemm_w8a8_epilogues_9216rows.md)
 NCU_TRAFFIC = {"zib_gemm_w8a8_swiglu_had": 287554304, "zib_gemm_w8a8_qk_norm_rope": 285878784}
@@ -426,7 +427,9 @@ def run_ours(args) -> None:
                          "achieved": None if achieved is None else round(achieved, 1),
                          "peak": INT8_DATASHEET_TOPS, "unit": "TOPS",
                          "frac": None if achieved is None else round(achieved / INT8_DATASHEET_TOPS, 4),
-                         "peak_source": "B200 datasheet dense INT8 (MEASURED_PEAKS.json has no INT8 entry)",
+                         "peak_source": "B200 datasheet dense INT8 (no measured INT8 peak: "
+                                        + ("MEASURED_PEAKS.json has bf16/HBM only)" if peaks
+                                           else "MEASURED_PEAKS.json absent)"),
                          "int_mm_measured_tops": None if int_mm_tops is None else round(int_mm_tops, 1),
                          "frac_of_int_mm": None if (achieved is None or not int_mm_tops)
                          else round(achieved / int_mm_tops, 4),
@@ -447,7 +450,8 @@ def run_ours(args) -> None:
             "int_ops_per_step": _int_ops_per_step(),
             "setup_s": round(setup_s, 1),
             "device_error": err,
-            "hbm_peak_gbs": peaks.get("hbm_gbs"),
+            "hbm_peak_gbs": peaks.get("hbm_gbs", HBM_FALLBACK_GBS),
+            "hbm_peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
         }
         if cpu:
             rec["cpu_baseline"] = cpu
