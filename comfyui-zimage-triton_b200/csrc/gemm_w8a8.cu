@@ -38,6 +38,7 @@
 // ZIB_ERR_TIMEOUT in a device error word, drains its in-flight TMA loads and
 // MMAs, frees TMEM and exits.
 #include "zib_async.cuh"
+#include "rot_pack.cuh"
 
 #include <cuda.h>
 #include <mutex>
@@ -428,10 +429,8 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
     for (int t = 0; t < 8; ++t) {
       const uint32_t g2 = dequant2(rg[2 * t], rg[2 * t + 1], sx2, s1[t]);
       const uint32_t u2 = dequant2(ru[2 * t], ru[2 * t + 1], sx2, s3[t]);
-      const float g0 = lo_f32(g2), g1 = hi_f32(g2);
       // silu in fp32, rounded to bf16; times up, rounded to bf16 (swiglu.py:51-58)
-      const uint32_t sl2 = cvt_bf16x2(__fmul_rn(g0, zib_sigmoidf(g0)), __fmul_rn(g1, zib_sigmoidf(g1)));
-      v[t] = mul_bf16x2(sl2, u2);
+      v[t] = mul_bf16x2(px::silu_bf16x2(g2), u2);
     }
     const int ch = c.cq * 4 + g * 2;
     *reinterpret_cast<uint4*>(c.xbuf + xoff_256(rt, ch)) = make_uint4(v[0], v[1], v[2], v[3]);
@@ -443,13 +442,11 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
 #pragma unroll 2
   for (int it = 0; it < 4; ++it) {
     const int r2 = c.quarter * 32 + c.cq * 8 + it * 2 + (c.lane >> 4);
-    float v[8];
-    load_bf16x8(c.xbuf + xoff_256(r2, sub), v);
-    fwht8(v);
-    fwht_cross16(v, c.lane);
-    had_round8(v);
+    px::f2 P[4];
+    px::fwht128(*reinterpret_cast<const uint4*>(c.xbuf + xoff_256(r2, sub)), P, c.lane);
+    const uint4 o = px::had_round(P);
     const int grow = c.row_base + r2;
-    if (grow < p.M) store_bf16x8(p.y + (int64_t)grow * p.ldy + nb * 128 + sub * 8, v);
+    if (grow < p.M) *reinterpret_cast<uint4*>(p.y + (int64_t)grow * p.ldy + nb * 128 + sub * 8) = o;
   }
 }
 
@@ -507,9 +504,7 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         o[t] = dequant2(r[j + 2 * t], r[j + 2 * t + 1], sx2, wv[t]);
-        const float a = lo_f32(o[t]), b = hi_f32(o[t]);
-        ss0 += (double)(a * a);  // bf16 squares are exact in fp32; the fp64 sums are exact
-        ss1 += (double)(b * b);
+        px::sumsq_acc(o[t], ss0, ss1);  // exact squares; the fp64 sums are exact in practice
       }
       *reinterpret_cast<uint4*>(c.xbuf + xoff_512(rt, (c.cq * CW + cc * 32 + j) / 8)) =
           make_uint4(o[0], o[1], o[2], o[3]);
@@ -525,7 +520,7 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
   const float eps = kind == 0 ? p.q_eps : p.k_eps;
   const float4 wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
   const float4 wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
-  const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+  const px::f2 W[4] = {px::mk(wa.x, wa.y), px::mk(wa.z, wa.w), px::mk(wb.x, wb.y), px::mk(wb.z, wb.w)};
 #pragma unroll 4
   for (int it = 0; it < RPW / 2; ++it) {
     const int r2 = c.quarter * 32 + (c.cq % WPH) * RPW + it * 2 + (c.lane >> 4);
@@ -534,20 +529,22 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
     const int64_t bi = gr / p.seq, si = gr % p.seq;
     const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cosp + bi * p.cs_b + si * 64 + sub * 4));
     const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sinp + bi * p.cs_b + si * 64 + sub * 4));
-    float v[8];
-    load_bf16x8(c.xbuf + xoff_512(r2, hh * 16 + sub), v);
+    const uint4 xv = *reinterpret_cast<const uint4*>(c.xbuf + xoff_512(r2, hh * 16 + sub));
     double ss = 0.0;
 #pragma unroll
     for (int k = 0; k < WPH; ++k) ss += ss_buf[r2 * NQ + hh * WPH + k];
     const float rs = rstd_from_sum(ss, 128, eps);
+    const px::f2 RS = px::mk(rs, rs);
     const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
     const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      // bf16(bf16(x * rstd) * w), then the pair rotation, each rounded to bf16
-      const uint32_t n2 = cvt_bf16x2(__fmul_rn(v[2 * k], rs), __fmul_rn(v[2 * k + 1], rs));
-      const uint32_t m2 = cvt_bf16x2(__fmul_rn(lo_f32(n2), wv[2 * k]), __fmul_rn(hi_f32(n2), wv[2 * k + 1]));
+      // bf16(bf16(x * rstd) * w), then the pair rotation, each rounded to bf16 (the
+      // rotation's products and sums stay scalar: packed, they may be contracted)
+      const uint32_t n2 = px::to_bf16x2(px::mul(px::from_bf16x2(xw[k]), RS));
+      const uint32_t m2 = px::to_bf16x2(px::mul(px::from_bf16x2(n2), W[k]));
       const float a = lo_f32(m2), b = hi_f32(m2);
       o[k] = cvt_bf16x2(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(b, sv[k])),
                         __fadd_rn(__fmul_rn(b, cv[k]), __fmul_rn(a, sv[k])));

@@ -6,6 +6,7 @@
 // butterfly stages plus 4 xor-shuffle stages.  Every kernel keeps the
 // reference's bf16 rounding points; see zib_common.cuh.
 #include "zib_async.cuh"
+#include "rot_pack.cuh"
 
 #include <stdio.h>
 
@@ -1106,27 +1107,21 @@ extern "C" int zib_act_quant(const void* x, int64_t ldx, void* q, int64_t ldq, v
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(K / 8, &l), ZIB_ERR_TOO_LARGE, "act_quant: K=%lld exceeds 65536", (long long)K);
   cudaStream_t st = (cudaStream_t)stream;
-  if (x_rot) {  // debug output of the rotation: the direct-load kernel writes it
-    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
-        act_quant_kernel<CPT, HAD><<<(unsigned)M, l.threads, 0, st>>>(
-            (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, K)));
-  } else {
-    bool launched = wr::dispatch(K, [&](auto Rc, int cpl) {
-      constexpr int R = decltype(Rc)::value;
-      auto k = hadamard ? wr::act_quant_wr<R, true> : wr::act_quant_wr<R, false>;
-      wr::set_smem(k, wr::smem_for(cpl, 1));
-      k<<<wr::grid_for(k, R, cpl, 1, M), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>((const uint16_t*)x, ldx, (int8_t*)q, ldq,
-                                                             (uint16_t*)sx, cpl, M);
-    });
-    if (!launched)
+  bool launched = wr::dispatch(K, [&](auto Rc, int cpl) {
+    constexpr int R = decltype(Rc)::value;
+    auto k = hadamard ? wr::act_quant_wr<R, true> : wr::act_quant_wr<R, false>;
+    wr::set_smem(k, wr::smem_for(cpl, 1));
+    k<<<wr::grid_for(k, R, cpl, 1, M), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+        (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, cpl, M);
+  });
+  if (!launched && !x_rot)
     ZIB_DISPATCH_W(pipe::pipe_warps(K), ZIB_DISPATCH_BOOL(hadamard, HAD,
         ZIB_PIPE_TRY((pipe::act_quant_pipe<W, HAD>), 1, M, K,
                      (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, K)));
-    if (!launched)
-      ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
-          act_quant_kernel<CPT, HAD><<<(unsigned)M, l.threads, 0, st>>>(
-              (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, nullptr, K)));
-  }
+  if (!launched)  // other widths, or the rotated copy requested (direct-load kernel)
+    ZIB_DISPATCH_CPT(l.cpt, ZIB_DISPATCH_BOOL(hadamard, HAD,
+        act_quant_kernel<CPT, HAD><<<(unsigned)M, l.threads, 0, st>>>(
+            (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, K)));
   return zib_check_launch("act_quant");
 }
 

@@ -5,8 +5,9 @@
 //   c = 32 * cpl * r + l + 32 * k,   k = 0 .. cpl-1,
 // so every load and store instruction of a warp moves 512 contiguous bytes
 // and a 128-element Hadamard group (16 chunks) sits in lanes 0-15 or 16-31 of
-// one k (fwht128: 3 butterfly stages in-thread, 4 over xor shuffles; the same
-// adds in the same order as the other rotation kernels).  A row is copied
+// one k (px::fwht128: 3 butterfly stages in-thread, 4 over xor shuffles; the
+// same adds in the same order as the other rotation kernels, two fp32 lanes
+// per packed instruction).  A row is copied
 // into this warp's slice of shared memory with cp.async (chunk k of lane l at
 // [k][l], conflict-free; all of a row's copies in flight at once, no
 // registers held), and the heavy stages (norm, rotation, quantisation) are
@@ -29,9 +30,6 @@ constexpr int kWarps = 4;  // warps per CTA; a CTA runs kWarps / R rows at a tim
 
 __device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-__device__ __forceinline__ uint32_t pack_exact(float lo, float hi) {  // both bf16-exact
-  return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
-}
 __device__ __forceinline__ uint32_t cvt2(float lo, float hi) {  // round each to bf16 (RNE)
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -51,27 +49,7 @@ __device__ __forceinline__ void unpack8(const uint4& d, float v[8]) {
   v[0] = lo_f(d.x); v[1] = hi_f(d.x); v[2] = lo_f(d.y); v[3] = hi_f(d.y);
   v[4] = lo_f(d.z); v[5] = hi_f(d.z); v[6] = lo_f(d.w); v[7] = hi_f(d.w);
 }
-__device__ __forceinline__ uint4 pack8_exact(const float v[8]) {
-  return make_uint4(pack_exact(v[0], v[1]), pack_exact(v[2], v[3]), pack_exact(v[4], v[5]),
-                    pack_exact(v[6], v[7]));
-}
 __device__ __forceinline__ uint4 ld_nc(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
-// |x| bit patterns of bf16 order like unsigned integers: running max of a chunk
-__device__ __forceinline__ uint32_t absmax8(const uint4& d, uint32_t m) {
-  m = __vmaxu2(m, d.x & 0x7FFF7FFFu);
-  m = __vmaxu2(m, d.y & 0x7FFF7FFFu);
-  m = __vmaxu2(m, d.z & 0x7FFF7FFFu);
-  m = __vmaxu2(m, d.w & 0x7FFF7FFFu);
-  return m;
-}
-__device__ __forceinline__ double sumsq8(const uint4& d) {  // bf16 squares are exact in fp32
-  float v[8];
-  unpack8(d, v);
-  double s = 0.0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) s += (double)(v[j] * v[j]);
-  return s;
-}
 
 // --- team of R warps working on one row ---------------------------------------------
 
@@ -117,47 +95,21 @@ struct Team {
 
 // rotate (optional) chunk d in place and fold its |max| (bf16 bits)
 template <bool HAD>
-__device__ __forceinline__ void rot_amax(uint4& d, uint32_t& m, int lane) {
+__device__ __forceinline__ void rot_amax(uint4& d, px::AbsMax& am, int lane) {
   if (HAD) {
-    float v[8];
-    unpack8(d, v);
-    pipe::fwht128(v, lane);
-    had_round8(v);
-    d = pack8_exact(v);
+    px::f2 P[4];
+    px::fwht128(d, P, lane);
+    d = px::had_round(P);
   }
-  m = absmax8(d, m);
+  am.add(d);
 }
 
-// y = bf16(bf16(x * rstd) * w) for one chunk; w points at the chunk's 8 fp32
-// weights (rms_norm.py:53-57)
-__device__ __forceinline__ uint4 norm_w(const uint4& d, float rstd, const float* __restrict__ w) {
-  float v[8], wv[8];
-  unpack8(d, v);
-  const float4 wa = __ldg(reinterpret_cast<const float4*>(w));
-  const float4 wb = __ldg(reinterpret_cast<const float4*>(w + 4));
-  wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
-  wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
-  uint32_t a[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t n2 = cvt2(__fmul_rn(v[2 * j], rstd), __fmul_rn(v[2 * j + 1], rstd));
-    a[j] = cvt2(__fmul_rn(lo_f(n2), wv[2 * j]), __fmul_rn(hi_f(n2), wv[2 * j + 1]));
-  }
-  return make_uint4(a[0], a[1], a[2], a[3]);
-}
-
-// y = bf16(y * bf16(1 + s)) (+ shift); scale/shift point at the chunk's 8
-// values (patching_comfyui.py:378, :401)
-__device__ __forceinline__ uint4 modulate(const uint4& y, const uint16_t* __restrict__ scale,
-                                          const uint16_t* __restrict__ shift) {
+// bf16(y * bf16(1 + s)) (+ h) with the chunk's scale s and shift h already loaded
+__device__ __forceinline__ uint4 modulate(const uint4& y, const uint4& s, const uint4& h, bool has_shift) {
   constexpr uint32_t kOne2 = 0x3F803F80u;  // bf16 (1.0, 1.0)
-  const uint4 s = ld_nc(scale);
   uint4 r = make_uint4(hmul2(y.x, hadd2(kOne2, s.x)), hmul2(y.y, hadd2(kOne2, s.y)),
                        hmul2(y.z, hadd2(kOne2, s.z)), hmul2(y.w, hadd2(kOne2, s.w)));
-  if (shift) {
-    const uint4 h = ld_nc(shift);
-    r = make_uint4(hadd2(r.x, h.x), hadd2(r.y, h.y), hadd2(r.z, h.z), hadd2(r.w, h.w));
-  }
+  if (has_shift) r = make_uint4(hadd2(r.x, h.x), hadd2(r.y, h.y), hadd2(r.z, h.z), hadd2(r.w, h.w));
   return r;
 }
 
@@ -179,6 +131,16 @@ __device__ __forceinline__ void copy_row(const uint16_t* __restrict__ src, uint4
                  : "memory");
 }
 
+// pull this warp's part of a row into L2 ahead of its copies (one bulk
+// prefetch by lane 0; rows are 16-byte aligned)
+template <int R>
+__device__ __forceinline__ void prefetch_row(const Team<R>& t, const uint16_t* row_base, int cpl) {
+  if (t.lane == 0)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(row_base + (int64_t)t.wig * cpl * 256),
+                 "r"((uint32_t)cpl * 512u)
+                 : "memory");
+}
+
 // wait for this lane's copies (each lane reads back only its own slots)
 __device__ __forceinline__ void copies_done() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
@@ -188,7 +150,7 @@ __device__ __forceinline__ void copies_done() {
 __device__ __forceinline__ double row_sumsq(const uint4* sl, int cpl) {
   double ss = 0.0;
 #pragma unroll 4
-  for (int k = 0; k < cpl; ++k) ss += sumsq8(sl[32 * k]);
+  for (int k = 0; k < cpl; ++k) ss += px::sumsq_chunk(sl[32 * k]);
   return ss;
 }
 
@@ -203,36 +165,34 @@ __device__ __forceinline__ void quant_row(const Team<R>& t, const uint4* sl, int
   const float rcp = __fdiv_rn(1.0f, s);
   int8_t* qr = q + row * ldq + t.first(cpl);
 #pragma unroll 1
-  for (int k = 0; k < cpl; ++k) {
-    float v[8];
-    unpack8(sl[32 * k], v);
-    int qq[8];
-    pipe::quant8(v, s, rcp, qq);
-    pipe::store_i8x8_prmt(qr + 256 * k, qq);
-  }
+  for (int k = 0; k < cpl; ++k) *reinterpret_cast<uint2*>(qr + 256 * k) = px::quant_chunk(sl[32 * k], rcp);
   if (t.wig == 0 && t.lane == 0) sx[row] = float_to_bf16_bits(s);
 }
 
 template <int R, bool HAD>
 __global__ void __launch_bounds__(32 * kWarps) act_quant_wr(const uint16_t* __restrict__ x, int64_t ldx,
                                                             int8_t* __restrict__ q, int64_t ldq,
-                                                            uint16_t* __restrict__ sx, int cpl, int64_t rows) {
+                                                            uint16_t* __restrict__ sx, uint16_t* __restrict__ xr,
+                                                            int cpl, int64_t rows) {
   __shared__ uint32_t redu[kWarps];
   const Team<R> t;
   const int64_t f0 = t.first(cpl);
   uint4* sl = warp_slice(cpl, 1);
-  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
-       row += (int64_t)gridDim.x * (kWarps / R)) {
+  const int64_t step = (int64_t)gridDim.x * (kWarps / R);
+  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows; row += step) {
+    // this warp's next row into L2 (measured: helps the plain quantiser, slows the rotating kernels)
+    if (!HAD && row + step < rows) prefetch_row(t, x + (row + step) * ldx, cpl);
     copy_row(x + row * ldx + f0, sl, cpl);
     copies_done();
-    uint32_t m = 0;
+    px::AbsMax m;
 #pragma unroll 1
     for (int k = 0; k < cpl; ++k) {
       uint4 d = sl[32 * k];
       rot_amax<HAD>(d, m, t.lane);
       if (HAD) sl[32 * k] = d;
+      if (xr) *reinterpret_cast<uint4*>(xr + row * ldq + f0 + 256 * k) = d;  // optional rotated copy
     }
-    quant_row<R>(t, sl, cpl, m, redu, row, q, ldq, sx);
+    quant_row<R>(t, sl, cpl, m.packed(), redu, row, q, ldq, sx);
     __syncwarp();
   }
 }
@@ -250,18 +210,20 @@ __global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
   const int64_t f0 = t.first(cpl);
   const float* wl = w + f0;
   uint4* sl = warp_slice(cpl, 1);
-  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
-       row += (int64_t)gridDim.x * (kWarps / R)) {
+  const int64_t step = (int64_t)gridDim.x * (kWarps / R);
+  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows; row += step) {
     copy_row(x + row * ldx + f0, sl, cpl);
     copies_done();
     const float rstd = rstd_from_sum(t.sum(row_sumsq(sl, cpl), redd), (int)n, eps);
     const int64_t mo = (row / rows_per_batch) * ld_mod + f0;
     uint16_t* yr = MODE <= 1 ? y + row * ldy + f0 : nullptr;
-    uint32_t m = 0;
+    px::AbsMax m;
 #pragma unroll 1
     for (int k = 0; k < cpl; ++k) {
-      uint4 v = norm_w(sl[32 * k], rstd, wl + 256 * k);
-      if (MODE >= 1) v = modulate(v, scale + mo + 256 * k, shift ? shift + mo + 256 * k : nullptr);
+      uint4 v = px::norm_w(sl[32 * k], rstd, wl + 256 * k);
+      if (MODE >= 1)
+        v = modulate(v, ld_nc(scale + mo + 256 * k), shift ? ld_nc(shift + mo + 256 * k) : make_uint4(0, 0, 0, 0),
+                     shift != nullptr);
       if (MODE <= 1) {
         *reinterpret_cast<uint4*>(yr + 256 * k) = v;
       } else {
@@ -269,7 +231,7 @@ __global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
         sl[32 * k] = v;
       }
     }
-    if (MODE == 2) quant_row<R>(t, sl, cpl, m, redu, row, q, ldq, sx);
+    if (MODE == 2) quant_row<R>(t, sl, cpl, m.packed(), redu, row, q, ldq, sx);
     __syncwarp();  // the slot is rewritten by the next row's copies
   }
 }
@@ -288,8 +250,8 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
   const int64_t f0 = t.first(cpl);
   const float* wl = w + f0;
   uint4* sl = warp_slice(cpl, 1);  // x, then y
-  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows;
-       row += (int64_t)gridDim.x * (kWarps / R)) {
+  const int64_t step = (int64_t)gridDim.x * (kWarps / R);
+  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows; row += step) {
     const uint16_t* rr = r + row * ldr + f0;
     copy_row(x + row * ldx + f0, sl, cpl);
     copies_done();
@@ -301,7 +263,7 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
 #pragma unroll 4
     for (int k = 0; k < cpl; ++k) {
       const uint4 e = __ldcs(reinterpret_cast<const uint4*>(rr + 256 * k));
-      const uint4 a = norm_w(sl[32 * k], rstd, wl + 256 * k);
+      const uint4 a = px::norm_w(sl[32 * k], rstd, wl + 256 * k);
       const uint4 g = ld_nc(gl + 256 * k);
       // bf16(r + bf16(g * a)), fused_norm_residual.py:69-73
       const uint4 v = make_uint4(hadd2(e.x, hmul2(g.x, a.x)), hadd2(e.y, hmul2(g.y, a.y)),
@@ -309,22 +271,22 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
       *reinterpret_cast<uint4*>(yr + 256 * k) = v;
       if (FUSE) {
         sl[32 * k] = v;
-        ss2 += sumsq8(v);
+        ss2 += px::sumsq_chunk(v);
       }
     }
     if (FUSE) {
       const float rstd2 = rstd_from_sum(t.sum(ss2, redd), (int)n, eps2);
       const int64_t mo = b * ld_mod + f0;
       const float* w2l = w2 + f0;
-      uint32_t m = 0;
+      px::AbsMax m;
 #pragma unroll 1
       for (int k = 0; k < cpl; ++k) {
-        uint4 v = modulate(norm_w(sl[32 * k], rstd2, w2l + 256 * k), scale + mo + 256 * k,
-                           shift ? shift + mo + 256 * k : nullptr);
+        uint4 v = modulate(px::norm_w(sl[32 * k], rstd2, w2l + 256 * k), ld_nc(scale + mo + 256 * k),
+                           shift ? ld_nc(shift + mo + 256 * k) : make_uint4(0, 0, 0, 0), shift != nullptr);
         rot_amax<HAD>(v, m, t.lane);
         sl[32 * k] = v;
       }
-      quant_row<R>(t, sl, cpl, m, redu, row, q, ldq, sx);
+      quant_row<R>(t, sl, cpl, m.packed(), redu, row, q, ldq, sx);
     }
     __syncwarp();
   }

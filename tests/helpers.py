@@ -55,3 +55,23 @@ def ztree():
 
     torch.manual_seed(0)
     return ZTree()
+
+
+def midpoint_rows(n_pool: int = 4096, K: int = 3840, seed: int = 11, n_rows: int = 48):
+    """Rows of a seeded pool whose rotation reaches the exact-residual rounding path.
+
+    Returns (x, tie_mask): up to ``n_rows`` rows whose fp32 rotation product
+    p = fwht(x) * bf16(1/sqrt(128)) sits exactly on a bf16 midpoint (low 16 bits 0x8000),
+    where rounding p to bf16 would differ from rounding the exact product; tie_mask
+    marks those positions.
+    """
+    import numpy as np
+
+    from oracle import ops
+
+    x = seeded_x(n_pool, K, seed=seed)
+    v = ops.fwht_f64(x.float().numpy().reshape(n_pool, K // 128, 128)).reshape(n_pool, K)
+    p = v.astype(np.float32) * np.float32(ops.H_BF16)
+    tie = (p.view(np.uint32) & 0xFFFF) == 0x8000
+    rows = np.flatnonzero(tie.any(1))[:n_rows]
+    return x[torch.from_numpy(rows)], torch.from_numpy(tie[rows])

@@ -49,6 +49,23 @@ def test_act_quant_vs_reference_matmul_rotation(cuda):
     assert int((q.int() - rq.int()).abs().max()) <= 1
 
 
+def test_act_quant_midpoint_rows_bitexact(cuda):
+    """Rows whose fp32 rotation products sit exactly on bf16 midpoints: the exact-residual
+    rounding (int8_linear.py:124-126 rounds the exact product once) in the row kernels."""
+    from helpers import midpoint_rows
+
+    x, tie = midpoint_rows()
+    assert int(tie.sum()) >= x.shape[0] > 0
+    q, sx, xr = _act_quant(x)
+    oq, osx, oxr = ops.act_quant_had128(x)
+    assert torch.equal(xr[tie], oxr[tie])
+    assert (xr != oxr).float().mean().item() <= 1e-5
+    rq, rs = ops.quantize_rotated(xr)
+    assert torch.equal(q, rq) and torch.equal(sx, rs.flatten())
+    q2, sx2, _ = _act_quant(x, want_rot=False)
+    assert torch.equal(q2, q) and torch.equal(sx2, sx)
+
+
 @pytest.mark.parametrize("M,K", [(3, 200), (64, 3840), (17, 8)])
 def test_act_quant_plain_bitexact(cuda, M, K):
     x = seeded_x(M, K, seed=7)

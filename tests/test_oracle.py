@@ -109,6 +109,35 @@ def test_exact_rotation_vs_reference_matmul_rate():
     assert int((q1.int() - q2.int()).abs().max()) <= 1
 
 
+def test_reciprocal_quotient_rounds_like_division():
+    """bf16(RN(v * RN(1/s))) == bf16(RN(v / s)) for every bf16 v with |v| <= 130 s and every
+    bf16 scale significand at eight exponents (int8_linear.py:130 divides; the kernels multiply
+    by the reciprocal and need no check)."""
+    def bf16_bits(f):
+        b = f.view(np.uint32).astype(np.uint64)
+        return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+    allv = (np.arange(65536, dtype=np.uint32) << 16).view(np.float32)
+    allv = allv[np.isfinite(allv)]
+    checked = 0
+    for e in (-30, -24, -10, -3, 0, 5, 20, 60):
+        for ms in range(128, 256):
+            s = np.float32(ms * 2.0 ** (e - 7))
+            v = allv[np.abs(allv) <= np.float32(130.0) * s]
+            t = v * (np.float32(1.0) / s)
+            q = (v.astype(np.float64) / np.float64(s)).astype(np.float32)  # 53 >= 2*24 + 2: one rounding
+            assert np.array_equal(bf16_bits(t), bf16_bits(q)), (e, ms)
+            checked += v.size
+    assert checked > 30_000_000
+
+
+def test_midpoint_rows_reach_the_exact_path():
+    from helpers import midpoint_rows
+
+    x, tie = midpoint_rows(n_pool=1024)
+    assert x.shape[0] >= 4 and int(tie.sum()) >= x.shape[0]
+
+
 def test_rope_table_layout():
     pos = ops.zimage_positions(4, 4, 8)
     assert pos.shape == (24, 3)
