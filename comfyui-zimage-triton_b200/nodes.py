@@ -30,7 +30,7 @@ def _restore_original_forwards(transformer) -> None:  # noqa: ANN001
         if hasattr(module, "_original_silu_gating"):
             module._forward_silu_gating = module._original_silu_gating
             delattr(module, "_original_silu_gating")
-        for key in ("_zib_cache", "_zib_next", "_zib_fused_ok"):
+        for key in ("_zib_cache", "_zib_next", "_zib_fused_ok", "_zib_adaln_stack"):
             module.__dict__.pop(key, None)
 
     for name, child in list(transformer.named_modules()):

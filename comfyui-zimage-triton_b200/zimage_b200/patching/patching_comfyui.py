@@ -331,7 +331,7 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
         # attention_norm1 -> *(1+scale_msa) -> rotate -> quantise            (:378)
         q8 = torch.empty(M, D, dtype=i8, device=dev)
         sx = torch.empty(M, dtype=bf, device=dev)
-        _lib.call("zib_rmsnorm_mod_quant", x.data_ptr(), D, c["an1"].data_ptr(), raw.data_ptr(), None, 4 * D, S,
+        _lib.call("zib_rmsnorm_mod_quant", x.data_ptr(), D, c["an1"].data_ptr(), raw.data_ptr(), None, raw.stride(0), S,
                   q8.data_ptr(), D, sx.data_ptr(), M, D, float(c["eps_an1"]), 1, stream)
     # QKV projection with per-head Q/K RMSNorm + RoPE in the epilogue     (:180-190)
     nqkv = attn.qkv._w_int8.shape[0]
@@ -363,8 +363,8 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
     q8f = torch.empty(M, D, dtype=i8, device=dev)
     sxf = torch.empty(M, dtype=bf, device=dev)
     _lib.call("zib_norm_gate_residual_mod_quant", attn_out.data_ptr(), D, x.data_ptr(), D, gates.data_ptr(),
-              2 * D, S, c["an2"].data_ptr(), x1.data_ptr(), D, c["fn1"].data_ptr(),
-              raw.data_ptr() + 2 * D * esz, None, 4 * D, q8f.data_ptr(), D, sxf.data_ptr(), M, D,
+              gates.stride(0), S, c["an2"].data_ptr(), x1.data_ptr(), D, c["fn1"].data_ptr(),
+              raw.data_ptr() + 2 * D * esz, None, raw.stride(0), q8f.data_ptr(), D, sxf.data_ptr(), M, D,
               float(c["eps_an2"]), float(c["eps_fn1"]), 1, stream)
     # w1 and w3 GEMMs + SwiGLU + w2-input rotation in one launch, then quantise   (swiglu.py:51-58)
     x_rot = torch.empty(M, F_, dtype=bf, device=dev)
@@ -382,15 +382,16 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
     cn = _handoff_target(nxt, D)
     if cn is None:
         _lib.call("zib_norm_gate_residual", ffn_out.data_ptr(), D, x1.data_ptr(), D, gates.data_ptr() + D * esz,
-                  2 * D, S, c["fn2"].data_ptr(), x2.data_ptr(), D, M, D, float(c["eps_fn2"]), stream)
+                  gates.stride(0), S, c["fn2"].data_ptr(), x2.data_ptr(), D, M, D, float(c["eps_fn2"]), stream)
         return x2.view(B, S, D)
     # ... fused with the next block's attention_norm1 * (1 + its scale_msa) -> rotate -> quantise
     raw_n, gates_n = _adaln(nxt, adaln_input, B, D, stream)
     q8n = torch.empty(M, D, dtype=i8, device=dev)
     sxn = torch.empty(M, dtype=bf, device=dev)
     _lib.call("zib_norm_gate_residual_mod_quant", ffn_out.data_ptr(), D, x1.data_ptr(), D,
-              gates.data_ptr() + D * esz, 2 * D, S, c["fn2"].data_ptr(), x2.data_ptr(), D, cn["an1"].data_ptr(),
-              raw_n.data_ptr(), None, 4 * D, q8n.data_ptr(), D, sxn.data_ptr(), M, D, float(c["eps_fn2"]),
+              gates.data_ptr() + D * esz, gates.stride(0), S, c["fn2"].data_ptr(), x2.data_ptr(), D,
+              cn["an1"].data_ptr(), raw_n.data_ptr(), None, raw_n.stride(0), q8n.data_ptr(), D, sxn.data_ptr(), M, D,
+              float(c["eps_fn2"]),
               float(cn["eps_an1"]), 1, stream)
     out = x2.view(B, S, D)
     _HANDOFF = {"block": nxt, "x": (out.data_ptr(), out._version, tuple(out.shape)),
@@ -399,8 +400,106 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
     return out
 
 
+# All blocks of a block list take their adaLN modulation from the same input, so
+# one rotation + quantisation of that input and one GEMM over the stacked int8
+# weights give every block's modulation (_AdaLNStack).
+ENABLE_ADALN_STACK = True
+
+
+class _AdaLNStack:
+    """The adaLN linears of one block list as a single W8A8 GEMM.
+
+    Column for column the stacked GEMM is each block's own W8A8 linear
+    (int8_linear.py:114-138: same quantised input rows, int32 sums, scales and
+    bias), so the modulations are identical to the per-block ones.  The blocks'
+    int8 weights and scales become row slices of the stack (no second copy); the
+    stack is rebuilt if any of them changes.  One evaluation per adaLN input is
+    kept, together with a reference to that input, so its memory cannot be
+    reused by another tensor while the result is held.
+    """
+
+    def __init__(self, blocks):
+        self.blocks = list(blocks)
+        self.pos = {id(b): i for i, b in enumerate(self.blocks)}
+        self.key = None
+        self.memo = None
+
+    def _lins(self):
+        lins = []
+        for b in self.blocks:
+            seq = getattr(b, "adaLN_modulation", None)
+            mods = list(seq.children()) if isinstance(seq, nn.Sequential) else []
+            if len(mods) != 1:
+                return None
+            lin = mods[0]
+            if not (getattr(lin, "_int8_quantized", False) and hasattr(lin, "_w_int8") and lin._w_int8.is_cuda
+                    and lin._w_scale.dtype == torch.bfloat16 and lin.bias is not None
+                    and lin.bias.dtype == torch.bfloat16 and lin.bias.is_cuda):
+                return None
+            lins.append(lin)
+        if len({(tuple(l._w_int8.shape), bool(l._int8_use_hadamard)) for l in lins}) != 1:
+            return None
+        return lins
+
+    @staticmethod
+    def _key(lins):
+        return tuple((l._w_int8.data_ptr(), l._w_int8._version, l._w_scale.data_ptr(), l._w_scale._version,
+                      l.bias.data_ptr(), l.bias._version) for l in lins)
+
+    def _build(self, lins):
+        N = lins[0]._w_int8.shape[0]
+        w = torch.cat([l._w_int8 for l in lins]).contiguous()
+        sw = torch.cat([l._w_scale for l in lins]).contiguous()
+        for i, l in enumerate(lins):
+            l._buffers["_w_int8"] = w[i * N:(i + 1) * N]
+            l._buffers["_w_scale"] = sw[i * N:(i + 1) * N]
+        self.w, self.sw = w, sw
+        self.bias = torch.cat([l.bias.detach() for l in lins]).contiguous()
+        self.N, self.K = N, lins[0]._w_int8.shape[1]
+        self.had = bool(lins[0]._int8_use_hadamard)
+        self.key = self._key(lins)
+        self.memo = None
+
+    def get(self, block: nn.Module, x: torch.Tensor, B: int, D: int, stream):
+        """(raw [B, 4D], gates [B, 2, D]) of `block` as strided views, or None (not applicable)."""
+        i = self.pos.get(id(block))
+        lins = self._lins() if i is not None else None
+        if lins is None:
+            return None
+        if self.key != self._key(lins):
+            self._build(lins)
+        N, K, L = self.N, self.K, len(self.blocks)
+        if (N != 4 * D or x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2
+                or tuple(x.shape) != (B, K)):
+            return None
+        m = self.memo
+        if m is None or m[0] is not x or m[1] != x._version:
+            x2 = x.contiguous()
+            q = torch.empty(B, K, dtype=torch.int8, device=x.device)
+            sx = torch.empty(B, dtype=torch.bfloat16, device=x.device)
+            _lib.call("zib_act_quant", x2.data_ptr(), K, q.data_ptr(), K, sx.data_ptr(), None, B, K,
+                      1 if self.had else 0, stream)
+            raw_all = torch.empty(B, L * N, dtype=torch.bfloat16, device=x.device)
+            _lib.call("zib_gemm_w8a8", q.data_ptr(), K, self.w.data_ptr(), K, sx.data_ptr(), self.sw.data_ptr(),
+                      self.bias.data_ptr(), raw_all.data_ptr(), L * N, B, L * N, K, stream)
+            # rows (b, l) of raw_all are consecutive 4D-wide rows: one gates launch for all
+            gates_all = torch.empty(B * L, 2, D, dtype=torch.bfloat16, device=x.device)
+            _lib.call("zib_adaln_gates", raw_all.data_ptr(), N, gates_all.data_ptr(), B * L, D, stream)
+            self.memo = m = (x, x._version, raw_all, gates_all)
+        return m[2].view(B, L, N)[:, i], m[3].view(B, L, 2, D)[:, i]
+
+
 def _adaln(block: nn.Module, adaln_input: torch.Tensor, B: int, D: int, stream):
-    """adaLN: raw [B, 4D]; gates tanh'd once (patching_comfyui.py:368-372)."""
+    """adaLN: raw [B, 4D] and gates [B, 2, D], tanh'd once (patching_comfyui.py:368-372).
+
+    Both may be row-strided views (the stacked evaluation): pass stride(0) as their
+    leading dimension.
+    """
+    st = block.__dict__.get("_zib_adaln_stack") if ENABLE_ADALN_STACK else None
+    if st is not None:
+        r = st.get(block, adaln_input, B, D, stream)
+        if r is not None:
+            return r
     raw = block.adaLN_modulation(adaln_input).reshape(B, 4 * D).contiguous()
     gates = torch.empty(B, 2, D, dtype=torch.bfloat16, device=raw.device)
     _lib.call("zib_adaln_gates", raw.data_ptr(), 4 * D, gates.data_ptr(), B, D, stream)
@@ -501,6 +600,9 @@ def _patch_block_forward_comfyui(model: nn.Module, stats: dict, enable_adaln: bo
             if len(blocks) == len(lst):
                 for a, b in zip(blocks, blocks[1:] + [None]):
                     a.__dict__["_zib_next"] = b
+                stack = _AdaLNStack(blocks)
+                for a in blocks:
+                    a.__dict__["_zib_adaln_stack"] = stack
 
 
 def apply_triton_kernels_comfyui(model: nn.Module, enable_fused_norm: bool = True, enable_swiglu: bool = True,

@@ -269,6 +269,30 @@ def test_block_handoff_equals_per_block_path(cuda):
     assert torch.equal(y_handoff, y_plain)
 
 
+def test_stacked_adaln_equals_per_block(cuda):
+    """One rotation + quantisation + GEMM for every block's adaLN linear gives the per-block
+    modulations bit for bit; the blocks' int8 weights become slices of the stack."""
+    from zimage_b200.patching import patching_comfyui as pc
+
+    dim, heads, ffn = 1024, 8, 2816
+    m, _ = _small_model(3, dim, heads, ffn)
+    _patch(m)
+    st = m.layers[0].__dict__["_zib_adaln_stack"]
+    assert all(b.__dict__["_zib_adaln_stack"] is st for b in m.layers)
+    x, t, fm, _ = _inputs(2, 8, 8, 16, dim)
+    with torch.no_grad():
+        y_stack = m(x.cuda(), t.cuda(), fm.cuda())
+        assert st.memo is not None
+        lin1 = m.layers[1].adaLN_modulation[0]
+        assert lin1._w_int8.data_ptr() == st.w.data_ptr() + lin1._w_int8.numel()
+        pc.ENABLE_ADALN_STACK = False
+        try:
+            y_plain = m(x.cuda(), t.cuda(), fm.cuda())
+        finally:
+            pc.ENABLE_ADALN_STACK = True
+    assert torch.equal(y_stack, y_plain)
+
+
 def test_overlapped_host_io_steps_match_sequential(cuda):
     """run_steps_overlapped (copy stream for host I/O) gives every step's exact output."""
     from zimage_b200.graph import CapturedStep, run_steps_overlapped
