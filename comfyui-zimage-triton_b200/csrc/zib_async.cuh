@@ -66,13 +66,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the thread sleep up to `hint_ns` (woken when the phase
+// completes): a waiting warp re-polls rarely instead of spinning on issue slots
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kWaitSleepNs = 1000000u;  // 1 ms per poll; the bounded waits check their limit between polls
+
 // Bounded wait; returns false after the timeout (error word set) or when
 // *abort_flag is raised by another waiter.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
     if (abort_flag && *abort_flag) return false;
     if (globaltimer() - t0 > kWaitTimeoutNs) {
       if (abort_flag) *abort_flag = 1;
@@ -85,7 +100,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // Bounded wait that never raises anything (used while draining after an abort).
 __device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) {
     if (globaltimer() - t0 > kWaitTimeoutNs) return;
   }
 }
