@@ -413,9 +413,10 @@ class _AdaLNStack:
     (int8_linear.py:114-138: same quantised input rows, int32 sums, scales and
     bias), so the modulations are identical to the per-block ones.  The blocks'
     int8 weights and scales become row slices of the stack (no second copy); the
-    stack is rebuilt if any of them changes.  One evaluation per adaLN input is
-    kept, together with a reference to that input, so its memory cannot be
-    reused by another tensor while the result is held.
+    stack is rebuilt if any of them changes.  The first block of the list
+    evaluates the stack; the later blocks of the same pass reuse that evaluation
+    when they get the same adaLN input tensor (held by reference, so its memory
+    cannot be reused by another tensor meanwhile) at the same version.
     """
 
     def __init__(self, blocks):
@@ -473,7 +474,9 @@ class _AdaLNStack:
                 or tuple(x.shape) != (B, K)):
             return None
         m = self.memo
-        if m is None or m[0] is not x or m[1] != x._version:
+        # the first block recomputes: one evaluation per pass over the list, never reused
+        # by a later forward even when it is given the same input tensor
+        if i == 0 or m is None or m[0] is not x or m[1] != x._version:
             x2 = x.contiguous()
             q = torch.empty(B, K, dtype=torch.int8, device=x.device)
             sx = torch.empty(B, dtype=torch.bfloat16, device=x.device)

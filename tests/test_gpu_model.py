@@ -283,6 +283,9 @@ def test_stacked_adaln_equals_per_block(cuda):
     with torch.no_grad():
         y_stack = m(x.cuda(), t.cuda(), fm.cuda())
         assert st.memo is not None
+        first = st.memo[2]
+        assert torch.equal(m(x.cuda(), t.cuda(), fm.cuda()), y_stack)
+        assert st.memo[2] is not first  # every forward evaluates the stack again
         lin1 = m.layers[1].adaLN_modulation[0]
         assert lin1._w_int8.data_ptr() == st.w.data_ptr() + lin1._w_int8.numel()
         pc.ENABLE_ADALN_STACK = False
