@@ -104,6 +104,12 @@ struct Params {
   const float* sinp;
   int64_t cs_b;
   int seq, heads;
+  // split-K tail (plain and int32 epilogues of the pair kernel): work units
+  // [0, tail_start) are whole tiles; the remaining tiles run as `splits` units
+  // each over a slice of K, whose int32 partial tiles meet in `ws`
+  int num_units, tail_start, splits;
+  int32_t* ws;        // [tail tile][cta rank][split][128 x 256] int32 partials
+  int* counters;      // [tail tile][cta rank] arrivals, back to 0 after the last one
 };
 
 // --- PTX wrappers ------------------------------------------------------------
@@ -326,6 +332,64 @@ struct ReleaseLeader {
   }
 };
 
+// one 32-column chunk of plain dequant (+bias) or raw int32 output for one row
+template <int EPI>
+__device__ __forceinline__ void epi_chunk(const Params& p, int row, int n0, const uint32_t (&r)[32],
+                                          uint32_t sx2, float sxf) {
+  const bool full = n0 + 32 <= p.N;
+  if (EPI == EPI_I32) {
+    int32_t* dst = p.acc + (int64_t)row * p.ldacc + n0;
+    if (full && (p.ldacc % 4) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<int4*>(dst + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
+    } else {
+      for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (int)r[j];
+    }
+  } else if (full && !p.bias) {
+    uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      const uint4 w = ldg_u4(p.sw + n0 + j);
+      uint4 o;
+      o.x = dequant2(r[j], r[j + 1], sx2, w.x);
+      o.y = dequant2(r[j + 2], r[j + 3], sx2, w.y);
+      o.z = dequant2(r[j + 4], r[j + 5], sx2, w.z);
+      o.w = dequant2(r[j + 6], r[j + 7], sx2, w.w);
+      *reinterpret_cast<uint4*>(dst + j) = o;
+    }
+  } else {
+    float out[32];
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float swv[8], bv[8];
+      if (full) {
+        load_bf16x8_nc(p.sw + n0 + j, swv);
+        if (p.bias) load_bf16x8_nc(p.bias + n0 + j, bv);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int n = n0 + j + t;
+          swv[t] = n < p.N ? bf16_bits_to_float(p.sw[n]) : 0.0f;
+          bv[t] = (p.bias && n < p.N) ? bf16_bits_to_float(p.bias[n]) : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        float v = dequant(r[j + t], sxf, swv[t]);
+        if (p.bias) v = bf16_rne_alu(__fadd_rn(v, bv[t]));
+        out[j + t] = v;
+      }
+    }
+    uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
+    if (full) {
+      store_row_bf16(dst, out, 32);
+    } else {
+      for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (uint16_t)(__float_as_uint(out[j]) >> 16);
+    }
+  }
+}
+
 // plain dequant (+bias) or raw int32: this thread's row, columns [256/NQ * cq, +256/NQ)
 template <int EPI, class Rel>
 __device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
@@ -342,60 +406,76 @@ __device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int 
     tmem_row32(c.t_row + (uint32_t)(ch * 32), r);
     const int n0 = nb * BN + ch * 32;
     if (!row_ok || n0 >= p.N) continue;
-    const bool full = n0 + 32 <= p.N;
-    if (EPI == EPI_I32) {
-      int32_t* dst = p.acc + (int64_t)row * p.ldacc + n0;
-      if (full && (p.ldacc % 4) == 0) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<int4*>(dst + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
-      } else {
-        for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (int)r[j];
-      }
-    } else if (full && !p.bias) {
-      uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        const uint4 w = ldg_u4(p.sw + n0 + j);
-        uint4 o;
-        o.x = dequant2(r[j], r[j + 1], sx2, w.x);
-        o.y = dequant2(r[j + 2], r[j + 3], sx2, w.y);
-        o.z = dequant2(r[j + 4], r[j + 5], sx2, w.z);
-        o.w = dequant2(r[j + 6], r[j + 7], sx2, w.w);
-        *reinterpret_cast<uint4*>(dst + j) = o;
-      }
-    } else {
-      float out[32];
-#pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        float swv[8], bv[8];
-        if (full) {
-          load_bf16x8_nc(p.sw + n0 + j, swv);
-          if (p.bias) load_bf16x8_nc(p.bias + n0 + j, bv);
-        } else {
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const int n = n0 + j + t;
-            swv[t] = n < p.N ? bf16_bits_to_float(p.sw[n]) : 0.0f;
-            bv[t] = (p.bias && n < p.N) ? bf16_bits_to_float(p.bias[n]) : 0.0f;
-          }
-        }
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          float v = dequant(r[j + t], sxf, swv[t]);
-          if (p.bias) v = bf16_rne_alu(__fadd_rn(v, bv[t]));
-          out[j + t] = v;
-        }
-      }
-      uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
-      if (full) {
-        store_row_bf16(dst, out, 32);
-      } else {
-        for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (uint16_t)(__float_as_uint(out[j]) >> 16);
-      }
-    }
+    epi_chunk<EPI>(p, row, n0, r, sx2, sxf);
   }
   rel(c.lane);
+}
+
+constexpr int kSplitBar = 6;  // named barrier over all epilogue warps of a CTA (ids 1-4: lane quarters)
+
+// Split-K tail unit of the pair kernel (plain / int32 epilogues).  Every split
+// stores its int32 partial for this CTA's 128 rows, releases the accumulator,
+// and counts itself in; the split that arrives last for the tile (whichever
+// it is) sums the partials of all splits and runs the ordinary epilogue on
+// the sums.  Integer sums are exact in any order, so the output is the one
+// the whole-K tile produces.  Partials are laid out [chunk][4-column group]
+// [row] of int4 so that a warp's stores and loads are 512 contiguous bytes.
+template <int EPI, class Rel>
+__device__ __forceinline__ void epi_split(const Params& p, const EpiCtx& c, int nb, int tail_idx, int split,
+                                          int rank, const Rel& rel) {
+  __shared__ int s_last;
+  constexpr int CH = 8 / Cfg<EPI>::NQ;
+  const int rt = c.quarter * 32 + c.lane;
+  int4* slots = reinterpret_cast<int4*>(p.ws + (int64_t)(tail_idx * 2 + rank) * p.splits * (128 * 256));
+  constexpr int kSlotInt4 = 128 * 256 / 4;
+#pragma unroll 1
+  for (int ch = c.cq * CH; ch < c.cq * CH + CH; ++ch) {
+    uint32_t r[32];
+    tmem_row32(c.t_row + (uint32_t)(ch * 32), r);
+    int4* dst = slots + (int64_t)split * kSlotInt4 + (ch * 8) * 128 + rt;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      __stcg(dst + j * 128, make_int4((int)r[4 * j], (int)r[4 * j + 1], (int)r[4 * j + 2], (int)r[4 * j + 3]));
+  }
+  rel(c.lane);
+  __threadfence();
+  group_bar_sync(kSplitBar, Cfg<EPI>::EPI_WARPS * 32);
+  if (c.cq == 0 && c.quarter == 0 && c.lane == 0) {
+    int* ctr = p.counters + tail_idx * 2 + rank;
+    const int last = atomicAdd(ctr, 1) == p.splits - 1;
+    if (last) *ctr = 0;  // every split of this tile has arrived: ready for the next launch
+    s_last = last;
+  }
+  group_bar_sync(kSplitBar, Cfg<EPI>::EPI_WARPS * 32);
+  if (!s_last) return;
+  __threadfence();
+  const int row = c.row_base + rt;
+  const bool row_ok = row < p.M;
+  uint16_t sxb = 0;
+  if (EPI == EPI_BF16 && row_ok) sxb = p.sx[row];
+  const uint32_t sx2 = (uint32_t)sxb | ((uint32_t)sxb << 16);
+  const float sxf = __uint_as_float((uint32_t)sxb << 16);
+#pragma unroll 1
+  for (int ch = c.cq * CH; ch < c.cq * CH + CH; ++ch) {
+    const int n0 = nb * BN + ch * 32;
+    if (!row_ok || n0 >= p.N) continue;
+    uint32_t r[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] = 0u;
+#pragma unroll 1
+    for (int sp = 0; sp < p.splits; ++sp) {
+      const int4* src = slots + (int64_t)sp * kSlotInt4 + (ch * 8) * 128 + rt;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int4 v = __ldcg(src + j * 128);
+        r[4 * j] += (uint32_t)v.x;
+        r[4 * j + 1] += (uint32_t)v.y;
+        r[4 * j + 2] += (uint32_t)v.z;
+        r[4 * j + 3] += (uint32_t)v.w;
+      }
+    }
+    epi_chunk<EPI>(p, row, n0, r, sx2, sxf);
+  }
 }
 
 // SWIGLU.  Phase 1 (thread = row): column quarter cq holds gate (cols
@@ -600,6 +680,16 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mb, 
   }
 }
 
+// Work unit u -> tile, K-block range and split index (-1: the whole tile).
+struct Unit {
+  int tile, kb0, kb1, split;
+};
+__device__ __forceinline__ Unit unit_of(const Params& p, int u) {
+  if (u < p.tail_start) return Unit{u, 0, p.num_kb, -1};
+  const int v = u - p.tail_start, sp = v % p.splits;
+  return Unit{p.tail_start + v / p.splits, sp * p.num_kb / p.splits, (sp + 1) * p.num_kb / p.splits, sp};
+}
+
 // --- kernels -------------------------------------------------------------------
 
 template <int EPI>
@@ -793,10 +883,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
       int stage = 0;
       uint32_t phase = 0, pend_mask = 0, pend_parity = 0;
       bool ok = true;
-      for (int tile = cluster_id; tile < p.num_tiles && ok; tile += nclusters) {
+      for (int u = cluster_id; u < p.num_units && ok; u += nclusters) {
+        const Unit w = unit_of(p, u);
         int mb, nb;
-        tile_coords(p, tile, mb, nb);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        tile_coords(p, w.tile, mb, nb);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * P_STAGE_BYTES);
@@ -823,11 +914,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       const uint32_t base = smem_u32(smem);
-      for (int tile = cluster_id; tile < p.num_tiles && ok; tile += nclusters) {
+      for (int u = cluster_id; u < p.num_units && ok; u += nclusters) {
+        const Unit w = unit_of(p, u);
         if (!mbar_wait_bounded(&tempty_bar[accb], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(accb * BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = sdesc_sw128(base + stage * P_STAGE_BYTES);
@@ -835,7 +927,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k)
             umma_i8_pair(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4),
-                         idesc_i8(256, 256), (kb | k) != 0 ? 1u : 0u);
+                         idesc_i8(256, 256), (kb != w.kb0 || k != 0) ? 1u : 0u);
           umma_commit_pair(&empty_bar[stage], (uint16_t)3);  // frees the stage in both CTAs
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -856,18 +948,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
     const int bar_id = 1 + ((warp - 2) & 3);
     int accb = 0;
     uint32_t acc_phase = 0;
-    for (int tile = cluster_id; tile < p.num_tiles; tile += nclusters) {
+    for (int u = cluster_id; u < p.num_units; u += nclusters) {
+      const Unit w = unit_of(p, u);
       int ok = 1;
       if (lane == 0) ok = mbar_wait_bounded(&tfull_bar[accb], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      // with split units in the launch, every epilogue warp of the CTA agrees on every unit, so
+      // that no warp can be left alone at the split epilogue's barrier after another one stopped
       if (EPI == EPI_SWIGLU || EPI == EPI_QKROPE) ok = group_bar_and(bar_id, Cfg<EPI>::NQ * 32, ok);
+      else if (p.splits > 1) ok = group_bar_and(kSplitBar, Cfg<EPI>::EPI_WARPS * 32, ok);
       if (!ok) { aborted = true; break; }
       tc_fence_after();
       int mb, nb;
-        tile_coords(p, tile, mb, nb);
+      tile_coords(p, w.tile, mb, nb);
       const EpiCtx c{tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(accb * BN),
                      mb * 256 + (int)rank * 128, quarter, cq, lane, bar_id, xbuf};
-      epilogue_tile<EPI>(p, c, nb, ReleaseLeader{mapa_rank(smem_u32(&tempty_bar[accb]), 0)});
+      const ReleaseLeader rel{mapa_rank(smem_u32(&tempty_bar[accb]), 0)};
+      if constexpr (EPI == EPI_BF16 || EPI == EPI_I32) {
+        if (w.split >= 0) epi_split<EPI>(p, c, nb, w.tile - p.tail_start, w.split, (int)rank, rel);
+        else epilogue_tile<EPI>(p, c, nb, rel);
+      } else {
+        epilogue_tile<EPI>(p, c, nb, rel);
+      }
       accb ^= 1;
       if (accb == 0) acc_phase ^= 1u;
     }
@@ -948,6 +1050,84 @@ static int num_sms_for_current_device() {
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+// --- split-K tail ------------------------------------------------------------
+// A launch of T tiles on C persistent CTA pairs runs ceil(T / C) waves; when the
+// last wave is short (R = T mod C tiles), those R tiles are split along K into
+// S = min(C / R, 4) units so that the last wave is ~1/S as long.  The partial
+// int32 tiles meet in a per-device workspace (one slot per unit and CTA of the
+// pair, 128 KB each) with one arrival counter per tail tile and CTA; the last
+// arrival resets its counter.  The workspace is allocated on first use outside
+// stream capture (sized for one unit per CTA pair) and kept; launches of split
+// GEMMs that overlap on different streams of one device would share it, so
+// such callers turn splitting off (zib_gemm_set_split(0)).
+static bool g_split_enabled = true;
+constexpr int kSplitMinKBlocks = 48;  // K >= 6144
+struct SplitWs {
+  int32_t* ws = nullptr;
+  int* ctr = nullptr;
+  int units = 0;
+};
+static std::mutex g_split_mu;
+static SplitWs g_split_ws[64];
+
+static const SplitWs* split_workspace(int units, cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_split_mu);
+  SplitWs& w = g_split_ws[dev];
+  if (w.units >= units) return &w;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;  // no allocation inside a capture: this launch runs unsplit
+  }
+  int32_t* ws = nullptr;
+  int* ctr = nullptr;
+  if (cudaMalloc(&ws, (size_t)units * 2 * 128 * 256 * sizeof(int32_t)) != cudaSuccess ||
+      cudaMalloc(&ctr, (size_t)units * 2 * sizeof(int)) != cudaSuccess ||
+      cudaMemset(ctr, 0, (size_t)units * 2 * sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    if (ws) cudaFree(ws);
+    if (ctr) cudaFree(ctr);
+    return nullptr;
+  }
+  if (w.ws) {  // a larger replacement: the old buffers may still be in use by queued launches
+    cudaDeviceSynchronize();
+    cudaFree(w.ws);
+    cudaFree(w.ctr);
+  }
+  w.ws = ws;
+  w.ctr = ctr;
+  w.units = units;
+  return &w;
+}
+
+// Decide the split of the last wave (pair kernel, plain and int32 epilogues).
+static void plan_split(Params& p, int clusters, cudaStream_t st) {
+  p.num_units = p.num_tiles;
+  p.tail_start = p.num_tiles;
+  p.splits = 1;
+  const int T = p.num_tiles, C = clusters;
+  // The last unit of a split tile re-reads every partial (S x 128 KB per CTA) before its
+  // epilogue; that only pays off for long tiles (measured: K = 10240 gains 5%, K = 3840 loses 4%).
+  if (!g_split_enabled || T <= C || T % C == 0 || p.num_kb < kSplitMinKBlocks) return;
+  const int R = T % C;
+  int S = C / R;
+  if (S > 4) S = 4;
+  if (S > p.num_kb / 2) S = p.num_kb / 2;  // at least two K-blocks per split
+  if (S < 2) return;
+  const SplitWs* w = split_workspace(C, st);
+  if (!w) return;
+  p.tail_start = T - R;
+  p.splits = S;
+  p.num_units = p.tail_start + R * S;
+  p.ws = w->ws;
+  p.counters = w->ctr;
+}
+
 // Common checks + tensor maps + launch.  w2 is the second B operand (SWIGLU: w3).
 template <int EPI>
 static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int64_t ldw, int64_t w_rows, Params p,
@@ -1000,10 +1180,17 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
     p.num_tiles = p.num_mb * p.num_nb;
     int clusters = sms / 2;
     if (clusters > p.num_tiles) clusters = p.num_tiles;
+    p.num_units = p.num_tiles;
+    p.tail_start = p.num_tiles;
+    p.splits = 1;
+    if (EPI == EPI_BF16 || EPI == EPI_I32) plan_split(p, clusters, (cudaStream_t)stream);
     gemm_w8a8_pair_kernel<EPI><<<2 * clusters, Cfg<EPI>::THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
   } else {
     p.num_mb = (int)((M + 127) / 128);
     p.num_tiles = p.num_mb * p.num_nb;
+    p.num_units = p.num_tiles;
+    p.tail_start = p.num_tiles;
+    p.splits = 1;
     int grid = sms;
     if (grid > p.num_tiles) grid = p.num_tiles;
     gemm_w8a8_kernel<EPI><<<grid, Cfg<EPI>::THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
@@ -1101,6 +1288,26 @@ extern "C" int zib_gemm_w8a8_qk_norm_rope(const void* q, int64_t ldq, const void
   p.seq = (int)seq;
   p.heads = (int)heads;
   return zib::gemm::launch<zib::gemm::EPI_QKROPE>(q, ldq, wq, nullptr, ldw, N, p, stream, "gemm_w8a8_qk_norm_rope");
+}
+
+extern "C" int zib_gemm_set_split(int enable) {
+  zib::gemm::g_split_enabled = enable != 0;
+  return ZIB_OK;
+}
+
+// zero every split-K arrival counter (after a device error left a launch unfinished)
+void zib_gemm_split_reset() {
+  std::lock_guard<std::mutex> lk(zib::gemm::g_split_mu);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  for (int d = 0; d < 64; ++d) {
+    zib::gemm::SplitWs& w = zib::gemm::g_split_ws[d];
+    if (!w.ctr) continue;
+    cudaSetDevice(d);
+    cudaMemset(w.ctr, 0, (size_t)w.units * 2 * sizeof(int));
+  }
+  cudaSetDevice(dev);
+  cudaGetLastError();
 }
 
 extern "C" int zib_gemm_set_variant(int variant) {

@@ -42,11 +42,13 @@ extern "C" const char* zib_last_error(void) { return g_last_error; }
 
 // per-translation-unit device error words (see zib_async.cuh)
 int zib_err_read_clear_gemm();
+void zib_gemm_split_reset();
 int zib_err_read_clear_rows();
 
 extern "C" int zib_device_error_read_clear(void) {
   int a = zib_err_read_clear_gemm();
   int b = zib_err_read_clear_rows();
+  if (a) zib_gemm_split_reset();  // a stopped GEMM may have left split-K counters mid-count
   return a ? a : b;
 }
 

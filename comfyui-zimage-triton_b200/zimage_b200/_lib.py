@@ -42,6 +42,7 @@ SIGNATURES: dict[str, list] = {
     "zib_gemm_w8a8_qk_norm_rope": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP,
                                    _F32, _F32, _VP, _VP, _I64, _I64, _I64, _VP],
     "zib_gemm_set_variant": [_I32],
+    "zib_gemm_set_split": [_I32],
     "zib_weight_prep": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _VP],
     "zib_rms_norm": [_VP, _I64, _VP, _VP, _I64, _I64, _I64, _F32, _VP],
     "zib_rmsnorm_mod": [_VP, _I64, _VP, _VP, _VP, _I64, _I64, _VP, _I64, _I64, _I64, _F32, _VP],

@@ -122,6 +122,15 @@ ZIB_API int zib_gemm_w8a8_qk_norm_rope(const void* q, int64_t ldq, const void* w
  * bit-identical across variants.  No reference counterpart (tuning knob). */
 ZIB_API int zib_gemm_set_variant(int variant);
 
+/* Split-K tail for zib_gemm_w8a8 and zib_gemm_w8a8_acc_i32 with 2-CTA tiles
+ * (on by default): when the last wave of tiles is short and K >= 6144, its
+ * tiles run as 2-4 units over slices of K whose int32 partials are summed by
+ * the last unit to finish (bit-identical results).  Uses a per-device workspace of 256 KB
+ * per CTA pair (~19 MB on B200), allocated on first use outside stream capture;
+ * launches that overlap on different streams of one device must turn it off.
+ * No reference counterpart (tuning knob). */
+ZIB_API int zib_gemm_set_split(int enable);
+
 /* Offline weight prep: rotate_weight (hadamard.py:47-75) in exact arithmetic
  * rounded to fp32, then _quantize_weight_per_channel (int8_linear.py:67-73).
  * w: bf16 [N,K] stride ldw -> wq int8 [N,K] stride ldq, sw bf16 [N]

@@ -124,6 +124,46 @@ def test_gemm_dequant_epilogue_bitexact(cuda, gemm_variant, M, N, K, bias):
     assert torch.equal(y[:, :N].cpu(), want)
 
 
+@pytest.mark.parametrize("M,N,K,check_oracle", [(2560, 2048, 6144, True), (1024, 11520, 10240, False),
+                                                (9216, 3840, 10240, False)])
+def test_gemm_split_tail_equals_unsplit(cuda, M, N, K, check_oracle):
+    """Short last wave of 2-CTA tiles run as K-split units whose int32 partials the last unit sums:
+    identical to the unsplit GEMM (and the oracle), on two calls in a row (the arrival counters
+    return to zero), for the int32 and the dequant + bias epilogues."""
+    lib = _lib.load()
+    q = _rand_i8((M, K), 11)
+    w = _rand_i8((N, K), 12)
+    sx = (torch.rand(M, generator=torch.Generator().manual_seed(13)) * 0.02 + 0.001).to(torch.bfloat16)
+    sw = (torch.rand(N, generator=torch.Generator().manual_seed(14)) * 0.02 + 0.001).to(torch.bfloat16)
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(15)) * 0.5).to(torch.bfloat16)
+    qd, wd, sxd, swd, bd = q.cuda(), w.cuda(), sx.cuda(), sw.cuda(), b.cuda()
+    st = _lib.stream_of(qd)
+
+    def run(split):
+        assert lib.zib_gemm_set_split(split) == 0
+        acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+        y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        _lib.call("zib_gemm_w8a8_acc_i32", qd.data_ptr(), K, wd.data_ptr(), K, acc.data_ptr(), N, M, N, K, st)
+        _lib.call("zib_gemm_w8a8", qd.data_ptr(), K, wd.data_ptr(), K, sxd.data_ptr(), swd.data_ptr(),
+                  bd.data_ptr(), y.data_ptr(), N, M, N, K, st)
+        torch.cuda.synchronize()
+        assert _lib.device_error_read_clear() == 0
+        return acc.cpu(), y.cpu()
+
+    try:
+        a1, y1 = run(1)
+        a2, y2 = run(1)
+        a0, y0 = run(0)
+    finally:
+        lib.zib_gemm_set_split(1)
+    assert torch.equal(a1, a0) and torch.equal(a2, a0)
+    assert torch.equal(y1, y0) and torch.equal(y2, y0)
+    if check_oracle:
+        want = ops.gemm_acc_i32(q, w)
+        assert torch.equal(a1, want)
+        assert torch.equal(y1, ops.dequant_epilogue(want, sx, sw, b))
+
+
 @pytest.mark.parametrize("M,F,K", [(48, 128, 384), (129, 384, 256), (300, 1280, 3840), (1024, 10240, 3840),
                                    (1100, 128, 256)])
 def test_gemm_swiglu_hadamard_epilogue(cuda, gemm_variant, M, F, K):
