@@ -1105,6 +1105,74 @@ static const SplitWs* split_workspace(int units, cudaStream_t st) {
   return &w;
 }
 
+// The allocation-free variant (zib_gemm_w8a8_static_scratch): the same partial
+// slots and counters in static device arrays of fixed size, 64 units (16 MB)
+// of partials and 128 counters.  The counters start at zero (static
+// initialisation) and every completed launch leaves them at zero.
+constexpr int kStaticSplitUnits = 64;
+static __device__ __align__(256) int32_t g_static_split_ws[kStaticSplitUnits * 2 * 128 * 256];
+static __device__ __align__(256) int g_static_split_ctr[kStaticSplitUnits * 2];
+struct StaticScratch {
+  int32_t* ws = nullptr;
+  int* ctr = nullptr;
+};
+static StaticScratch g_static_scratch[64];
+
+// Device addresses of the static scratch on the current device, looked up once
+// per device (cudaGetSymbolAddress; the first call belongs before any capture).
+static int static_scratch(const StaticScratch** out, const char* what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    zib_set_error("%s: no usable current device", what);
+    return ZIB_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lk(g_split_mu);
+  StaticScratch& s = g_static_scratch[dev];
+  if (!s.ws) {
+    void* ws = nullptr;
+    void* ctr = nullptr;
+    e = cudaGetSymbolAddress(&ws, g_static_split_ws);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&ctr, g_static_split_ctr);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      zib_set_error("%s: cudaGetSymbolAddress of the split-K scratch failed: %s", what, cudaGetErrorString(e));
+      return ZIB_ERR_LAUNCH;
+    }
+    s.ws = static_cast<int32_t*>(ws);
+    s.ctr = static_cast<int*>(ctr);
+  }
+  *out = &s;
+  return ZIB_OK;
+}
+
+// Split of the last wave into exactly `splits` units per tile in the static
+// scratch; a tail that needs more than it holds is refused before any launch.
+static int plan_split_static(Params& p, int clusters, int splits, const char* what) {
+  p.num_units = p.num_tiles;
+  p.tail_start = p.num_tiles;
+  p.splits = 1;
+  const int T = p.num_tiles, C = clusters;
+  if (splits <= 1 || T <= C || T % C == 0) return ZIB_OK;  // no short last wave to split
+  const int R = T % C;
+  ZIB_HOST_CHECK(splits <= p.num_kb, ZIB_ERR_INVALID_ARG, "%s: %d splits exceed the %d K-blocks of 128", what,
+                 splits, p.num_kb);
+  ZIB_HOST_CHECK(R * splits <= kStaticSplitUnits, ZIB_ERR_TOO_LARGE,
+                 "%s: the last wave's %d tiles x %d splits need %d KB of split-K scratch; the static area holds "
+                 "%d KB (%d units)",
+                 what, R, splits, R * splits * 256, kStaticSplitUnits * 256, kStaticSplitUnits);
+  const StaticScratch* sc = nullptr;
+  const int st = static_scratch(&sc, what);
+  if (st) return st;
+  p.tail_start = T - R;
+  p.splits = splits;
+  p.num_units = p.tail_start + R * splits;
+  p.ws = sc->ws;
+  p.counters = sc->ctr;
+  return ZIB_OK;
+}
+
 // Decide the split of the last wave (pair kernel, plain and int32 epilogues).
 static void plan_split(Params& p, int clusters, cudaStream_t st) {
   p.num_units = p.num_tiles;
@@ -1131,7 +1199,7 @@ static void plan_split(Params& p, int clusters, cudaStream_t st) {
 // Common checks + tensor maps + launch.  w2 is the second B operand (SWIGLU: w3).
 template <int EPI>
 static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int64_t ldw, int64_t w_rows, Params p,
-                  void* stream, const char* what) {
+                  void* stream, const char* what, int static_splits = 0) {
   const int64_t M = p.M, K = p.K;
   ZIB_HOST_CHECK(q && w && (EPI != EPI_SWIGLU || w2), ZIB_ERR_INVALID_ARG, "%s: null operand", what);
   ZIB_HOST_CHECK(M >= 0 && p.N > 0 && K > 0, ZIB_ERR_INVALID_ARG, "%s: bad shape M=%d N=%d K=%d", what, p.M, p.N,
@@ -1183,7 +1251,14 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
     p.num_units = p.num_tiles;
     p.tail_start = p.num_tiles;
     p.splits = 1;
-    if (EPI == EPI_BF16 || EPI == EPI_I32) plan_split(p, clusters, (cudaStream_t)stream);
+    if (EPI == EPI_BF16 || EPI == EPI_I32) {
+      if (static_splits > 0) {
+        const int st = plan_split_static(p, clusters, static_splits, what);
+        if (st) return st;
+      } else {
+        plan_split(p, clusters, (cudaStream_t)stream);
+      }
+    }
     gemm_w8a8_pair_kernel<EPI><<<2 * clusters, Cfg<EPI>::THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
   } else {
     p.num_mb = (int)((M + 127) / 128);
@@ -1225,6 +1300,26 @@ extern "C" int zib_gemm_w8a8(const void* q, int64_t ldq, const void* wq, int64_t
   p.y = (uint16_t*)y;
   p.ldy = ldy;
   return zib::gemm::launch<zib::gemm::EPI_BF16>(q, ldq, wq, nullptr, ldw, N, p, stream, "gemm_w8a8");
+}
+
+extern "C" int zib_gemm_w8a8_static_scratch(const void* q, int64_t ldq, const void* wq, int64_t ldw, const void* sx,
+                                            const void* sw, const void* bias, void* y, int64_t ldy, int64_t M,
+                                            int64_t N, int64_t K, int splits, void* stream) {
+  ZIB_HOST_CHECK(splits >= 1 && splits <= 4, ZIB_ERR_INVALID_ARG,
+                 "gemm_w8a8_static_scratch: splits must be 1 to 4 (got %d)", splits);
+  ZIB_HOST_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), ZIB_ERR_TOO_LARGE,
+                 "gemm_w8a8_static_scratch: too large");
+  ZIB_HOST_CHECK(sx && sw && y && ldy >= N, ZIB_ERR_INVALID_ARG, "gemm_w8a8_static_scratch: bad epilogue operands");
+  ZIB_HOST_CHECK(ldy % 8 == 0 && aligned16(y) && aligned16(sw) && (!bias || aligned16(bias)), ZIB_ERR_ALIGNMENT,
+                 "gemm_w8a8_static_scratch: y/sw/bias must be 16-byte aligned and ldy %% 8 == 0");
+  zib::gemm::Params p = zib::gemm::base_params(M, N, K);
+  p.sx = (const uint16_t*)sx;
+  p.sw = (const uint16_t*)sw;
+  p.bias = (const uint16_t*)bias;
+  p.y = (uint16_t*)y;
+  p.ldy = ldy;
+  return zib::gemm::launch<zib::gemm::EPI_BF16>(q, ldq, wq, nullptr, ldw, N, p, stream, "gemm_w8a8_static_scratch",
+                                                splits);
 }
 
 extern "C" int zib_gemm_w8a8_acc_i32(const void* q, int64_t ldq, const void* wq, int64_t ldw, void* acc,
@@ -1302,9 +1397,11 @@ void zib_gemm_split_reset() {
   cudaGetDevice(&dev);
   for (int d = 0; d < 64; ++d) {
     zib::gemm::SplitWs& w = zib::gemm::g_split_ws[d];
-    if (!w.ctr) continue;
+    zib::gemm::StaticScratch& sc = zib::gemm::g_static_scratch[d];
+    if (!w.ctr && !sc.ctr) continue;
     cudaSetDevice(d);
-    cudaMemset(w.ctr, 0, (size_t)w.units * 2 * sizeof(int));
+    if (w.ctr) cudaMemset(w.ctr, 0, (size_t)w.units * 2 * sizeof(int));
+    if (sc.ctr) cudaMemset(sc.ctr, 0, sizeof(zib::gemm::g_static_split_ctr));
   }
   cudaSetDevice(dev);
   cudaGetLastError();
