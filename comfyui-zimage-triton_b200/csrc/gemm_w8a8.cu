@@ -70,10 +70,10 @@ struct Cfg {
   static constexpr int NQ = EPI_WARPS / 4;
   static constexpr int THREADS = (2 + EPI_WARPS) * 32;
   // SWIGLU: 128 rows x 128 features bf16.
-  // QKROPE: 128 rows x 256 columns bf16 + partial sums of squares fp64 [128][NQ].
-  static constexpr int XBUF = EPI == EPI_SWIGLU ? 128 * 256 : (EPI == EPI_QKROPE ? 128 * 512 + 128 * NQ * 8 : 0);
+  // QKROPE: 128 rows x 256 columns bf16.
+  static constexpr int XBUF = EPI == EPI_SWIGLU ? 128 * 256 : (EPI == EPI_QKROPE ? 128 * 512 : 0);
   static constexpr int S_STAGES = EPI == EPI_QKROPE ? 3 : 4;
-  static constexpr int P_STAGES = EPI == EPI_QKROPE ? 4 : 6;
+  static constexpr int P_STAGES = EPI == EPI_QKROPE ? 5 : 6;
   static constexpr int S_SMEM = S_STAGES * S_STAGE_BYTES + 1024 + 256 + XBUF;
   static constexpr int P_SMEM = P_STAGES * P_STAGE_BYTES + 1024 + 256 + XBUF;
   static_assert(S_SMEM <= MAX_SMEM && P_SMEM <= MAX_SMEM, "shared memory per CTA");
@@ -533,16 +533,17 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
 // QKROPE: the tile holds heads hb = 2*nb and 2*nb+1 of the [Q | K | V]
 // projection (the head count is even, so both have the same kind); column
 // part cq is tile columns [CW*cq, CW*cq + CW), CW = 256/NQ.
-// Phase 1 (thread = row): dequantised columns -> staging tile, and the exact
-// partial sum of squares.  Phase 2 (16 lanes per row, 8 values each): rstd
-// from the head's exact partial sums, bf16(bf16(x * rstd) * w),
-// interleaved-pair RoPE, coalesced store.
+// Phase 1 (thread = row, one warp per head): dequantised columns -> staging
+// tile, the row's exact sum of squares and its rstd.  Phase 2 (16 lanes per
+// row, 8 values each, the row's rstd by shuffle from its phase-1 lane):
+// bf16(bf16(x * rstd) * w), interleaved-pair RoPE, coalesced store.
 template <class Rel>
 __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
   constexpr int NQ = Cfg<EPI_QKROPE>::NQ;
   constexpr int CW = 256 / NQ;        // columns per warp
   constexpr int WPH = NQ / 2;         // warps per head
   constexpr int RPW = 32 / WPH;       // phase-2 rows per warp
+  static_assert(WPH == 1, "one epilogue warp per head: phase 1 completes each row's sum of squares");
   const int rt = c.quarter * 32 + c.lane;
   const int row = c.row_base + rt;
   const bool row_ok = row < p.M;
@@ -591,13 +592,14 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
     }
   }
   rel(c.lane);
-  double* ss_buf = reinterpret_cast<double*>(c.xbuf + 128 * 512);
-  ss_buf[rt * NQ + c.cq] = ss0 + ss1;
-  group_bar_sync(c.bar_id, NQ * 32);
+  // one warp per head: this thread's row of the head is complete, so its rstd is
+  // formed here once and handed to phase 2's lanes by shuffle
+  const float eps = kind == 0 ? p.q_eps : p.k_eps;
+  const float rs_own = rstd_from_sum(ss0 + ss1, 128, eps);
+  __syncwarp();  // the staging rows this warp wrote are read back by other lanes of it
   const int sub = c.lane & 15;
   const int hh = c.cq / WPH;  // head within the tile
   const float* w = kind == 0 ? p.qn_w : p.kn_w;
-  const float eps = kind == 0 ? p.q_eps : p.k_eps;
   const float4 wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
   const float4 wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
   const px::f2 W[4] = {px::mk(wa.x, wa.y), px::mk(wa.z, wa.w), px::mk(wb.x, wb.y), px::mk(wb.z, wb.w)};
@@ -610,10 +612,7 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
     const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cosp + bi * p.cs_b + si * 64 + sub * 4));
     const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sinp + bi * p.cs_b + si * 64 + sub * 4));
     const uint4 xv = *reinterpret_cast<const uint4*>(c.xbuf + xoff_512(r2, hh * 16 + sub));
-    double ss = 0.0;
-#pragma unroll
-    for (int k = 0; k < WPH; ++k) ss += ss_buf[r2 * NQ + hh * WPH + k];
-    const float rs = rstd_from_sum(ss, 128, eps);
+    const float rs = __shfl_sync(0xFFFFFFFFu, rs_own, it * 2 + (c.lane >> 4));  // row r2's owner lane
     const px::f2 RS = px::mk(rs, rs);
     const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
     const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
