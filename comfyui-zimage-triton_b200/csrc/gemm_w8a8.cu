@@ -73,7 +73,7 @@ struct Cfg {
   // QKROPE: 128 rows x 256 columns bf16.
   static constexpr int XBUF = EPI == EPI_SWIGLU ? 128 * 256 : (EPI == EPI_QKROPE ? 128 * 512 : 0);
   static constexpr int S_STAGES = EPI == EPI_QKROPE ? 3 : 4;
-  static constexpr int P_STAGES = EPI == EPI_QKROPE ? 5 : 6;
+  static constexpr int P_STAGES = EPI == EPI_QKROPE ? 5 : (EPI == EPI_SWIGLU ? 6 : 7);
   static constexpr int S_SMEM = S_STAGES * S_STAGE_BYTES + 1024 + 256 + XBUF;
   static constexpr int P_SMEM = P_STAGES * P_STAGE_BYTES + 1024 + 256 + XBUF;
   static_assert(S_SMEM <= MAX_SMEM && P_SMEM <= MAX_SMEM, "shared memory per CTA");
