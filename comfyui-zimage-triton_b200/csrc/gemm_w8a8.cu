@@ -481,9 +481,10 @@ __device__ __forceinline__ void epi_split(const Params& p, const EpiCtx& c, int 
 // SWIGLU.  Phase 1 (thread = row): column quarter cq holds gate (cols
 // 64cq..64cq+31) and up (64cq+32..64cq+63) of features 128*nb + 32*cq + [0, 32);
 // the bf16 SwiGLU values go to the staging tile [128 rows][128 features].
-// Phase 2 (16 lanes per row): Walsh-Hadamard over the 128 features of a row
-// (index bits 0..2 in-thread, 3..6 by xor shuffles, the act_quant kernels'
-// order), times bf16(1/sqrt(128)) correctly rounded, stored to x_rot.
+// Phase 2 (8 lanes per row, two chunks each): Walsh-Hadamard over the 128
+// features of a row (index bits 0..2 and 6 in-thread, 3..5 by xor shuffles,
+// in the act_quant kernels' order), times bf16(1/sqrt(128)) correctly
+// rounded, stored to x_rot.
 template <class Rel>
 __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
   static_assert(Cfg<EPI_SWIGLU>::NQ == 4, "SWIGLU column quarters");
@@ -518,15 +519,20 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
   }
   rel(c.lane);  // accumulator read: the MMA may refill this buffer
   group_bar_sync(c.bar_id, 128);
-  const int sub = c.lane & 15;
-#pragma unroll 2
-  for (int it = 0; it < 4; ++it) {
-    const int r2 = c.quarter * 32 + c.cq * 8 + it * 2 + (c.lane >> 4);
-    px::f2 P[4];
-    px::fwht128(*reinterpret_cast<const uint4*>(c.xbuf + xoff_256(r2, sub)), P, c.lane);
-    const uint4 o = px::had_round(P);
+  const int sub = c.lane & 7;  // 8 lanes per row, chunks sub and sub + 8 (fwht128_pair)
+#pragma unroll 1
+  for (int it = 0; it < 2; ++it) {
+    const int r2 = c.quarter * 32 + c.cq * 8 + it * 4 + (c.lane >> 3);
+    px::f2 A[4], B[4];
+    px::fwht128_pair(*reinterpret_cast<const uint4*>(c.xbuf + xoff_256(r2, sub)),
+                     *reinterpret_cast<const uint4*>(c.xbuf + xoff_256(r2, sub + 8)), A, B, c.lane);
+    const uint4 oa = px::had_round(A), ob = px::had_round(B);
     const int grow = c.row_base + r2;
-    if (grow < p.M) *reinterpret_cast<uint4*>(p.y + (int64_t)grow * p.ldy + nb * 128 + sub * 8) = o;
+    if (grow < p.M) {
+      uint16_t* dst = p.y + (int64_t)grow * p.ldy + nb * 128 + sub * 8;
+      *reinterpret_cast<uint4*>(dst) = oa;
+      *reinterpret_cast<uint4*>(dst + 64) = ob;
+    }
   }
 }
 

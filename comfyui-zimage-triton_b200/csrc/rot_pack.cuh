@@ -182,6 +182,58 @@ __device__ __forceinline__ void fwht128(const uint4& d, f2 P[4], int lane) {
   }
 }
 
+// The same transform with two chunks per lane: A = chunk i and B = chunk i + 8
+// of a 128-group (index bit 6 tells them apart) held by 8 consecutive lanes
+// (bits 3..5).  Bits 0..2 in-thread on each chunk, bits 3..5 over xor shuffles
+// (m = 1, 2, 4), bit 6 in-thread between A and B: the stages, operands and
+// order of fwht128, with three shuffle stages instead of four.  Every lane of
+// the warp must call this.
+__device__ __forceinline__ void fwht128_pair(const uint4& a, const uint4& b, f2 A[4], f2 B[4], int lane) {
+  const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    A[k] = bfly0(wa[k]);
+    B[k] = bfly0(wb[k]);
+  }
+  {
+    const f2 t0 = add(A[0], A[1]), t1 = sub(A[0], A[1]), t2 = add(A[2], A[3]), t3 = sub(A[2], A[3]);
+    A[0] = add(t0, t2);
+    A[2] = sub(t0, t2);
+    A[1] = add(t1, t3);
+    A[3] = sub(t1, t3);
+  }
+  {
+    const f2 t0 = add(B[0], B[1]), t1 = sub(B[0], B[1]), t2 = add(B[2], B[3]), t3 = sub(B[2], B[3]);
+    B[0] = add(t0, t2);
+    B[2] = sub(t0, t2);
+    B[1] = add(t1, t3);
+    B[3] = sub(t1, t3);
+  }
+#pragma unroll
+  for (int m = 1; m < 8; m <<= 1) {
+    const float sg = (lane & m) ? -1.0f : 1.0f;
+    const f2 SG = mk(sg, sg);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float lo, hi;
+      split(A[k], lo, hi);
+      float olo = __shfl_xor_sync(0xFFFFFFFFu, lo, m);
+      float ohi = __shfl_xor_sync(0xFFFFFFFFu, hi, m);
+      A[k] = fma(A[k], SG, mk(olo, ohi));
+      split(B[k], lo, hi);
+      olo = __shfl_xor_sync(0xFFFFFFFFu, lo, m);
+      ohi = __shfl_xor_sync(0xFFFFFFFFu, hi, m);
+      B[k] = fma(B[k], SG, mk(olo, ohi));
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {  // bit 6: A + B (lower), A - B (upper)
+    const f2 s = add(A[k], B[k]);
+    B[k] = sub(A[k], B[k]);
+    A[k] = s;
+  }
+}
+
 // bf16 chunk of the correctly rounded products P * bf16(1/sqrt(128)).  The
 // fp32 product rounded to bf16 is the correct rounding unless it sits exactly
 // on a bf16 midpoint (low 16 bits 0x8000); if any lane of the warp has one,

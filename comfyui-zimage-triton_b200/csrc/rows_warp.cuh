@@ -93,6 +93,41 @@ struct Team {
   __device__ __forceinline__ int64_t first(int cpl) const { return ((int64_t)wig * cpl * 32 + lane) * 8; }
 };
 
+// Rotation pass over this warp's chunks of a row (slots base[0 .. 32*cpl)):
+// each step takes 64 chunks, four 128-groups of 16 chunks, and gives a group
+// to 8 lanes with two chunks each (i and i + 8: fwht128_pair, three shuffle
+// stages instead of four).  `src(c)` produces the bf16 chunk c to rotate;
+// the rotated chunk goes back to slot c, into the |max|, and to `sink(c, v)`.
+// Lanes of a group past the end work on chunks 0-15 and discard the results
+// (every lane must take part in the shuffles).  The slots are read and written
+// across lanes: the caller syncs the warp before and after.
+template <class Src, class Sink>
+__device__ __forceinline__ void rotate_pairs(uint4* base, int cpl, int lane, px::AbsMax& am, const Src& src,
+                                             const Sink& sink) {
+  const int n = 32 * cpl;
+  const int off = 16 * (lane >> 3) + (lane & 7);
+#pragma unroll 1
+  for (int c0 = 0; c0 < n; c0 += 64) {
+    const bool valid = c0 + off < n;  // whole 16-chunk groups: chunk i valid <=> chunk i + 8 valid
+    const int ca = valid ? c0 + off : (lane & 7);
+    px::f2 A[4], B[4];
+    px::fwht128_pair(src(ca), src(ca + 8), A, B, lane);
+    const uint4 ra = px::had_round(A), rb = px::had_round(B);
+    if (valid) {
+      base[ca] = ra;
+      base[ca + 8] = rb;
+      am.add(ra);
+      am.add(rb);
+      sink(ca, ra);
+      sink(ca + 8, rb);
+    }
+  }
+}
+
+struct NoSink {
+  __device__ __forceinline__ void operator()(int, const uint4&) const {}
+};
+
 // rotate (optional) chunk d in place and fold its |max| (bf16 bits)
 template <bool HAD>
 __device__ __forceinline__ void rot_amax(uint4& d, px::AbsMax& am, int lane) {
@@ -185,12 +220,22 @@ __global__ void __launch_bounds__(32 * kWarps) act_quant_wr(const uint16_t* __re
     copy_row(x + row * ldx + f0, sl, cpl);
     copies_done();
     px::AbsMax m;
+    if (HAD) {
+      uint4* base = sl - t.lane;
+      uint16_t* xrr = xr ? xr + row * ldq + (f0 - 8 * t.lane) : nullptr;  // optional rotated copy
+      __syncwarp();  // chunks copied by other lanes
+      rotate_pairs(base, cpl, t.lane, m, [&](int c) { return base[c]; },
+                   [&](int c, const uint4& v) {
+                     if (xrr) *reinterpret_cast<uint4*>(xrr + 8 * c) = v;
+                   });
+      __syncwarp();
+    } else {
 #pragma unroll 1
-    for (int k = 0; k < cpl; ++k) {
-      uint4 d = sl[32 * k];
-      rot_amax<HAD>(d, m, t.lane);
-      if (HAD) sl[32 * k] = d;
-      if (xr) *reinterpret_cast<uint4*>(xr + row * ldq + f0 + 256 * k) = d;  // optional rotated copy
+      for (int k = 0; k < cpl; ++k) {
+        const uint4 d = sl[32 * k];
+        m.add(d);
+        if (xr) *reinterpret_cast<uint4*>(xr + row * ldq + f0 + 256 * k) = d;  // optional copy
+      }
     }
     quant_row<R>(t, sl, cpl, m.packed(), redu, row, q, ldq, sx);
     __syncwarp();
@@ -218,6 +263,18 @@ __global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
     const int64_t mo = (row / rows_per_batch) * ld_mod + f0;
     uint16_t* yr = MODE <= 1 ? y + row * ldy + f0 : nullptr;
     px::AbsMax m;
+    if (MODE == 2 && HAD) {
+      uint4* base = sl - t.lane;
+      const int64_t c0 = f0 - 8 * t.lane, m0 = mo - 8 * t.lane;  // element offsets of the warp's chunk 0
+      __syncwarp();  // chunks copied by other lanes
+      rotate_pairs(base, cpl, t.lane, m,
+                   [&](int c) {
+                     return modulate(px::norm_w(base[c], rstd, w + c0 + 8 * c), ld_nc(scale + m0 + 8 * c),
+                                     shift ? ld_nc(shift + m0 + 8 * c) : make_uint4(0, 0, 0, 0), shift != nullptr);
+                   },
+                   NoSink{});
+      __syncwarp();
+    } else
 #pragma unroll 1
     for (int k = 0; k < cpl; ++k) {
       uint4 v = px::norm_w(sl[32 * k], rstd, wl + 256 * k);
@@ -279,6 +336,7 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
       const int64_t mo = b * ld_mod + f0;
       const float* w2l = w2 + f0;
       px::AbsMax m;
+      // one chunk per lane here: the paired rotation measured 2% slower in this kernel
 #pragma unroll 1
       for (int k = 0; k < cpl; ++k) {
         uint4 v = modulate(px::norm_w(sl[32 * k], rstd2, w2l + 256 * k), ld_nc(scale + mo + 256 * k),
