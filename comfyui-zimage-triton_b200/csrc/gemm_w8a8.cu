@@ -602,6 +602,9 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
   // formed here once and handed to phase 2's lanes by shuffle
   const float eps = kind == 0 ? p.q_eps : p.k_eps;
   const float rs_own = rstd_from_sum(ss0 + ss1, 128, eps);
+  // this row's offset in the cos/sin tables (batch bi, position si; 32-bit, checked on the host)
+  const int gr_own = row_ok ? row : 0;
+  const int tab_own = (gr_own / p.seq) * (int)p.cs_b + (gr_own % p.seq) * 64;
   __syncwarp();  // the staging rows this warp wrote are read back by other lanes of it
   const int sub = c.lane & 15;
   const int hh = c.cq / WPH;  // head within the tile
@@ -613,12 +616,12 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
   for (int it = 0; it < RPW / 2; ++it) {
     const int r2 = c.quarter * 32 + (c.cq % WPH) * RPW + it * 2 + (c.lane >> 4);
     const int grow = c.row_base + r2;
-    const int gr = grow < p.M ? grow : 0;
-    const int64_t bi = gr / p.seq, si = gr % p.seq;
-    const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cosp + bi * p.cs_b + si * 64 + sub * 4));
-    const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sinp + bi * p.cs_b + si * 64 + sub * 4));
+    const int owner = it * 2 + (c.lane >> 4);  // row r2's phase-1 lane
+    const int tab = __shfl_sync(0xFFFFFFFFu, tab_own, owner) + sub * 4;
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(p.cosp + tab));
+    const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sinp + tab));
     const uint4 xv = *reinterpret_cast<const uint4*>(c.xbuf + xoff_512(r2, hh * 16 + sub));
-    const float rs = __shfl_sync(0xFFFFFFFFu, rs_own, it * 2 + (c.lane >> 4));  // row r2's owner lane
+    const float rs = __shfl_sync(0xFFFFFFFFu, rs_own, owner);
     const px::f2 RS = px::mk(rs, rs);
     const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
     const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
@@ -1368,6 +1371,8 @@ extern "C" int zib_gemm_w8a8_qk_norm_rope(const void* q, int64_t ldq, const void
   ZIB_HOST_CHECK(heads > 0 && heads % 2 == 0 && N == 3 * heads * 128 && seq > 0 && M % seq == 0,
                  ZIB_ERR_INVALID_ARG,
                  "gemm_w8a8_qk_norm_rope: needs N = 3*heads*128 with an even head count and M a multiple of seq");
+  ZIB_HOST_CHECK(cs_b >= 0 && (M / seq) * cs_b + seq * 64 < (1ll << 31), ZIB_ERR_TOO_LARGE,
+                 "gemm_w8a8_qk_norm_rope: cos/sin tables beyond 2^31 elements");
   ZIB_HOST_CHECK(sx && sw && y && ldy >= N && q_norm_w && k_norm_w && cosp && sinp, ZIB_ERR_INVALID_ARG,
                  "gemm_w8a8_qk_norm_rope: bad operands");
   ZIB_HOST_CHECK(ldy % 8 == 0 && aligned16(y) && aligned16(sw) && aligned16(q_norm_w) && aligned16(k_norm_w) &&
