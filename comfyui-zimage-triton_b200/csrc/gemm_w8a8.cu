@@ -1395,6 +1395,27 @@ extern "C" int zib_gemm_w8a8_qk_norm_rope(const void* q, int64_t ldq, const void
   return zib::gemm::launch<zib::gemm::EPI_QKROPE>(q, ldq, wq, nullptr, ldw, N, p, stream, "gemm_w8a8_qk_norm_rope");
 }
 
+// Self-test of the bounded-wait path: one thread waits on an mbarrier that
+// nothing arrives at, so the wait gives up after its limit (2 s), records
+// ZIB_ERR_TIMEOUT in the device error word and returns; nothing faults, traps
+// or hangs, and the context stays usable.
+__global__ void selftest_wait_kernel() {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    zib::mbar_init(&bar, 1);
+    abort_flag = 0;
+    zib::mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)zib::mbar_wait_bounded(&bar, 0, &abort_flag);
+}
+
+extern "C" int zib_selftest_bounded_wait(void* stream) {
+  selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>();
+  return zib_check_launch("selftest_bounded_wait");
+}
+
 extern "C" int zib_gemm_set_split(int enable) {
   zib::gemm::g_split_enabled = enable != 0;
   return ZIB_OK;

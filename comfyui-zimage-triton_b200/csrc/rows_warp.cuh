@@ -51,6 +51,13 @@ __device__ __forceinline__ void unpack8(const uint4& d, float v[8]) {
 }
 __device__ __forceinline__ uint4 ld_nc(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
+// row / rows_per_batch, in 32 bits whenever both fit (the common case)
+__device__ __forceinline__ int64_t batch_of(int64_t row, int64_t rows_per_batch) {
+  if ((uint64_t)row <= 0xFFFFFFFFull && (uint64_t)rows_per_batch <= 0xFFFFFFFFull)
+    return (int64_t)((uint32_t)row / (uint32_t)rows_per_batch);
+  return row / rows_per_batch;
+}
+
 // --- team of R warps working on one row ---------------------------------------------
 
 template <int R>
@@ -260,7 +267,7 @@ __global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
     copy_row(x + row * ldx + f0, sl, cpl);
     copies_done();
     const float rstd = rstd_from_sum(t.sum(row_sumsq(sl, cpl), redd), (int)n, eps);
-    const int64_t mo = (row / rows_per_batch) * ld_mod + f0;
+    const int64_t mo = batch_of(row, rows_per_batch) * ld_mod + f0;
     uint16_t* yr = MODE <= 1 ? y + row * ldy + f0 : nullptr;
     px::AbsMax m;
     if (MODE == 2 && HAD) {
@@ -313,7 +320,7 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
     copy_row(x + row * ldx + f0, sl, cpl);
     copies_done();
     const float rstd = rstd_from_sum(t.sum(row_sumsq(sl, cpl), redd), (int)n, eps);
-    const int64_t b = row / rows_per_batch;
+    const int64_t b = batch_of(row, rows_per_batch);
     const uint16_t* gl = gate + b * ld_gate + f0;
     uint16_t* yr = y + row * ldy + f0;
     double ss2 = 0.0;

@@ -35,6 +35,7 @@ SIGNATURES: dict[str, list] = {
     "zib_last_error": [],
     "zib_device_check": [_I32],
     "zib_device_error_read_clear": [],
+    "zib_selftest_bounded_wait": [_VP],
     "zib_act_quant": [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I32, _VP],
     "zib_gemm_w8a8": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP],
     "zib_gemm_w8a8_acc_i32": [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _VP],

@@ -54,6 +54,11 @@ ZIB_API int zib_device_check(int dev);
  * kernel whose bounded wait expired: ZIB_ERR_TIMEOUT).  Synchronising; not for
  * the hot path.  Returns 0 when no kernel reported an error. */
 ZIB_API int zib_device_error_read_clear(void);
+/* Launches one thread that waits on a barrier nothing arrives at: the bounded
+ * wait of the GEMM and row kernels expires (2 s), the device error word reads
+ * ZIB_ERR_TIMEOUT afterwards, and the context stays usable.  Exercises the
+ * failure path without a fault.  No counterpart in the reference. */
+ZIB_API int zib_selftest_bounded_wait(void* stream);
 
 /* ---------------------------------------------------------------------------
  * W8A8 + Hadamard linear (replaces _make_w8a8_hadamard_forward._forward,

@@ -74,6 +74,20 @@ def test_act_quant_plain_bitexact(cuda, M, K):
     assert torch.equal(q, oq) and torch.equal(sx, osx.flatten())
 
 
+def test_bounded_wait_expires_and_the_context_stays_usable(cuda):
+    """A wait that nothing satisfies gives up after its limit and reports ZIB_ERR_TIMEOUT through
+    the device error word; the next kernels run normally."""
+    assert _lib.device_error_read_clear() == 0
+    _lib.call("zib_selftest_bounded_wait", torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert _lib.device_error_read_clear() == _lib.ZIB_ERR_TIMEOUT
+    assert _lib.device_error_read_clear() == 0
+    x = seeded_x(64, 3840, seed=31)
+    q, sx, _ = _act_quant(x, want_rot=False)
+    oq, osx, _ = ops.act_quant_had128(x)
+    assert torch.equal(q, oq) and torch.equal(sx, osx.flatten())
+
+
 def _rand_i8(shape, seed):
     g = torch.Generator().manual_seed(seed)
     return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
