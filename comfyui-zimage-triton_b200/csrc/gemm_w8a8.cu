@@ -1113,10 +1113,15 @@ static const SplitWs* split_workspace(int units, cudaStream_t st) {
   return &w;
 }
 
-// The allocation-free variant (zib_gemm_w8a8_static_scratch): the same partial
-// slots and counters in static device arrays of fixed size, 64 units (16 MB)
-// of partials and 128 counters.  The counters start at zero (static
-// initialisation) and every completed launch leaves them at zero.
+// The allocation-free variant (zib_gemm_w8a8_static_scratch), for callers that
+// must not allocate device memory (a host framework that owns it through its
+// own pool and budget, a stream capture in progress, a loop that cannot take
+// the device synchronisation of cudaMalloc/cudaFree): the same partial slots
+// and counters in static device arrays of fixed size, 64 units (16 MB) of
+// partials and 128 counters, held by every GPU that loads the library.  Host
+// code reaches them only through cudaGetSymbolAddress (static_scratch below);
+// the counters start at zero (static initialisation) and every completed
+// launch leaves them at zero.
 constexpr int kStaticSplitUnits = 64;
 static __device__ __align__(256) int32_t g_static_split_ws[kStaticSplitUnits * 2 * 128 * 256];
 static __device__ __align__(256) int g_static_split_ctr[kStaticSplitUnits * 2];

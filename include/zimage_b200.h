@@ -136,20 +136,26 @@ ZIB_API int zib_gemm_set_variant(int variant);
  * No reference counterpart (tuning knob). */
 ZIB_API int zib_gemm_set_split(int enable);
 
-/* zib_gemm_w8a8 whose split-K tail uses a static device scratch area instead
- * of the allocated workspace, so the call allocates nothing.  `splits` (1-4)
- * is the number of K-slices each tile of a short last wave runs as (2-CTA
- * tiles, M > 128; 1 = no split, and launches without a short last wave run
- * unsplit).  The scratch holds 64 units of 256 KB (16 MB of device memory per
- * GPU for every process that loads this library) and 128 arrival counters: a
- * call whose last wave needs more (its tiles x splits > 64) returns
- * ZIB_ERR_TOO_LARGE before launching.  The counters must start at zero: they do
- * (static initialisation), every completed call leaves them at zero, and
+/* zib_gemm_w8a8 for callers that must not allocate device memory: a host
+ * framework that owns the GPU's memory through its own pool and budget (a
+ * cudaMalloc behind its back fragments the pool, escapes its accounting and
+ * can fail when the pool already holds the free memory), code recording a CUDA
+ * stream capture (which refuses cudaMalloc), and latency-bound loops (cudaMalloc
+ * and cudaFree synchronise the device).  Its split-K tail uses a static device
+ * scratch area instead of the workspace that zib_gemm_w8a8 allocates on first
+ * use; the call allocates and frees nothing.  `splits` (1-4) is the number of
+ * K-slices each tile of a short last wave runs as (2-CTA tiles, M > 128;
+ * 1 = no split; launches without a short last wave run unsplit).  Limit: the
+ * scratch holds 64 units of 256 KB (16 MB of device memory on every GPU that
+ * loads this library, held until the process exits) and 128 arrival counters;
+ * a call whose last wave needs more (its tiles x splits > 64) returns
+ * ZIB_ERR_TOO_LARGE before launching.  The counters must start at zero: they
+ * do (static initialisation), every completed call leaves them at zero, and
  * zib_device_error_read_clear() re-zeroes them after a device error.  The
  * first call on each device looks up the scratch address with
- * cudaGetSymbolAddress and belongs before any stream capture.  Calls that
- * overlap in time on one device (any streams) share the scratch and race.
- * No counterpart in the reference. */
+ * cudaGetSymbolAddress (with that device current) and should come before any
+ * stream capture.  Every call shares the scratch: calls that overlap on the GPU
+ * (any streams of one device) race.  No counterpart in the reference. */
 ZIB_API int zib_gemm_w8a8_static_scratch(const void* q, int64_t ldq, const void* wq, int64_t ldw,
                                const void* sx, const void* sw, const void* bias, void* y,
                                int64_t ldy, int64_t M, int64_t N, int64_t K, int splits,

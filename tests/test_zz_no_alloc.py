@@ -1,5 +1,9 @@
-"""zib_gemm_w8a8_static_scratch (split-K scratch in a static device array, no allocation)
-against zib_gemm_w8a8, through the C ABI (needs a B200).
+"""zib_gemm_w8a8_static_scratch against zib_gemm_w8a8, through the C ABI (needs a B200).
+
+The static-scratch GEMM is for callers that must not allocate device memory (a framework
+that budgets the GPU's memory through its own pool, a stream capture in progress, a
+latency-bound loop where cudaMalloc would synchronise): its split-K partials live in a fixed
+16 MB static device area instead of a workspace allocated on first use.
 
 Kept in its own file so that it is collected last: it must pass alone and after the rest
 of the suite, with whatever the earlier tests left in the static scratch.
