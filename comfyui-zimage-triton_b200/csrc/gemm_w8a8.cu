@@ -688,6 +688,89 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mb, 
   }
 }
 
+// Skinny GEMM for M <= 8 rows (the stacked adaLN linear: 2 rows x 460800
+// columns x K = 256): a 128-row tensor-core tile would be 94% padding and the
+// launch is a stream over the weights, so each half-warp takes one weight row
+// (column of the output) at a time, forms the MR int32 dot products with dp4a
+// (exact, like the int32 accumulators of the tcgen05 path) and runs the same
+// dequant (+bias) arithmetic as that path's epilogue.  The A rows sit in
+// shared memory; each lane keeps four weight loads in flight.
+constexpr int kSkinnyMaxM = 8;
+constexpr int kSkinnyMaxK = 4096;
+
+template <int EPI, int MR>
+__global__ void __launch_bounds__(256) gemm_w8a8_skinny_kernel(const int8_t* __restrict__ q, int64_t ldq,
+                                                               const int8_t* __restrict__ w, int64_t ldw,
+                                                               const Params p) {
+  extern __shared__ uint4 a_s[];  // [MR][K / 16]
+  const int kc = p.K / 16;
+  for (int i = threadIdx.x; i < MR * kc; i += blockDim.x) {
+    const int m = i / kc, c = i % kc;
+    a_s[i] = m < p.M ? __ldg(reinterpret_cast<const uint4*>(q + (int64_t)m * ldq) + c) : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, half = lane >> 4, sub = lane & 15;
+  const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  float sxf[MR];
+#pragma unroll
+  for (int m = 0; m < MR; ++m) sxf[m] = (EPI == EPI_BF16 && m < p.M) ? bf16_bits_to_float(p.sx[m]) : 0.0f;
+  // a warp covers 8 columns per step: column 8 * step + 2 j + half, j = 0..3 (warp-uniform loop)
+  for (int64_t base = warp * 8; base < p.N; base += nwarps * 8) {
+    int32_t acc[4][MR];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int m = 0; m < MR; ++m) acc[j][m] = 0;
+    for (int c = sub; c < kc; c += 16) {
+      uint4 wv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t n = base + 2 * j + half;
+        wv[j] = n < p.N ? __ldg(reinterpret_cast<const uint4*>(w + n * ldw) + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+        const uint4 a = a_s[m * kc + c];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int t = acc[j][m];
+          t = __dp4a((int)wv[j].x, (int)a.x, t);
+          t = __dp4a((int)wv[j].y, (int)a.y, t);
+          t = __dp4a((int)wv[j].z, (int)a.z, t);
+          t = __dp4a((int)wv[j].w, (int)a.w, t);
+          acc[j][m] = t;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int m = 0; m < MR; ++m) {
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) acc[j][m] += __shfl_xor_sync(0xFFFFFFFFu, acc[j][m], o);
+      }
+      const int64_t n = base + 2 * j + half;
+      if (sub != 0 || n >= p.N) continue;
+      if (EPI == EPI_I32) {
+#pragma unroll
+        for (int m = 0; m < MR; ++m)
+          if (m < p.M) p.acc[(int64_t)m * p.ldacc + n] = acc[j][m];
+      } else {
+        const float swf = bf16_bits_to_float(p.sw[n]);
+        const float bf = p.bias ? bf16_bits_to_float(p.bias[n]) : 0.0f;
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+          if (m >= p.M) continue;
+          float v = dequant((uint32_t)acc[j][m], sxf[m], swf);
+          if (p.bias) v = bf16_rne_alu(__fadd_rn(v, bf));
+          p.y[(int64_t)m * p.ldy + n] = (uint16_t)(__float_as_uint(v) >> 16);
+        }
+      }
+    }
+  }
+}
+
 // Work unit u -> tile, K-block range and split index (-1: the whole tile).
 struct Unit {
   int tile, kb0, kb1, split;
@@ -1209,6 +1292,28 @@ static void plan_split(Params& p, int clusters, cudaStream_t st) {
   p.counters = w->ctr;
 }
 
+// M <= 8 rows: the skinny kernel (one launch, CTAs sized for four per SM).
+template <int EPI>
+static int launch_skinny(const void* q, int64_t ldq, const void* w, int64_t ldw, const Params& p, void* stream,
+                         const char* what) {
+  const int mr = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
+  const size_t smem = (size_t)mr * p.K;
+  const int64_t steps = ((int64_t)p.N + 7) / 8;  // warp steps of 8 columns
+  int64_t grid = (steps + 7) / 8;                 // 8 warps per CTA
+  const int64_t cap = (int64_t)num_sms_for_current_device() * 4;
+  if (grid > cap) grid = cap;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int8_t* qa = (const int8_t*)q;
+  const int8_t* wa = (const int8_t*)w;
+  switch (mr) {
+    case 1: gemm_w8a8_skinny_kernel<EPI, 1><<<(unsigned)grid, 256, smem, st>>>(qa, ldq, wa, ldw, p); break;
+    case 2: gemm_w8a8_skinny_kernel<EPI, 2><<<(unsigned)grid, 256, smem, st>>>(qa, ldq, wa, ldw, p); break;
+    case 4: gemm_w8a8_skinny_kernel<EPI, 4><<<(unsigned)grid, 256, smem, st>>>(qa, ldq, wa, ldw, p); break;
+    default: gemm_w8a8_skinny_kernel<EPI, 8><<<(unsigned)grid, 256, smem, st>>>(qa, ldq, wa, ldw, p); break;
+  }
+  return zib_check_launch(what);
+}
+
 // Common checks + tensor maps + launch.  w2 is the second B operand (SWIGLU: w3).
 template <int EPI>
 static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int64_t ldw, int64_t w_rows, Params p,
@@ -1222,6 +1327,10 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
   ZIB_HOST_CHECK(aligned16(q) && aligned16(w) && (!w2 || aligned16(w2)), ZIB_ERR_ALIGNMENT,
                  "%s: q/w must be 16-byte aligned", what);
   if (M == 0) return ZIB_OK;
+  if constexpr (EPI == EPI_BF16 || EPI == EPI_I32) {
+    if (g_gemm_variant == 0 && M <= kSkinnyMaxM && K <= kSkinnyMaxK)
+      return launch_skinny<EPI>(q, ldq, w, ldw, p, stream, what);
+  }
   CUtensorMap ta, tb, tb2;
   const uint32_t b_box = EPI == EPI_SWIGLU ? (uint32_t)SW_BOX_ROWS : 128u;
   int st = make_map(&ta, q, K, M, ldq, 128u);

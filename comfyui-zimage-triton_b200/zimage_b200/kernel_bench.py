@@ -215,6 +215,7 @@ CASES = {
     "qknorm_rope": (lambda: case_qknorm_rope(), "hbm"),
     "weight_prep": (lambda: case_weight_prep(), "hbm"),
     "gemm_cfg1_qkv_m1024": (lambda: case_gemm(1024, 3 * D, D), "int8"),
+    "gemm_adaln_stack": (lambda: case_gemm(2, 30 * 4 * D, 256), "int8"),
     "gemm_qkv": (lambda: case_gemm(M_TOK, 3 * D, D), "int8"),
     "gemm_out": (lambda: case_gemm(M_TOK, D, D), "int8"),
     "gemm_w13": (lambda: case_gemm(M_TOK, 2 * F, D), "int8"),

@@ -122,9 +122,11 @@ ZIB_API int zib_gemm_w8a8_qk_norm_rope(const void* q, int64_t ldq, const void* w
                                int64_t seq, int64_t heads, void* stream);
 
 /* Selects the GEMM tiling for subsequent zib_gemm_w8a8* calls on this process:
- * 0 = automatic (2-CTA 256x256 tiles with cta_group::2 when M > 128, else
- * 1-CTA 128x256 tiles), 1 = always 1-CTA, 2 = always 2-CTA.  Results are
- * bit-identical across variants.  No reference counterpart (tuning knob). */
+ * 0 = automatic (2-CTA 256x256 tiles with cta_group::2 when M > 128, 1-CTA
+ * 128x256 tiles for 9-128 rows, and for the plain and int32 entry points a
+ * dp4a kernel that streams the weights when M <= 8 and K <= 4096), 1 = always
+ * 1-CTA, 2 = always 2-CTA.  Results are bit-identical across variants.  No
+ * reference counterpart (tuning knob). */
 ZIB_API int zib_gemm_set_variant(int variant);
 
 /* Split-K tail for zib_gemm_w8a8 and zib_gemm_w8a8_acc_i32 with 2-CTA tiles

@@ -138,6 +138,44 @@ def test_gemm_dequant_epilogue_bitexact(cuda, gemm_variant, M, N, K, bias):
     assert torch.equal(y[:, :N].cpu(), want)
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 256, 128), (2, 46080, 256), (3, 1000, 4096), (5, 300, 160), (8, 4100, 512),
+                                   (2, 8, 16)])
+def test_gemm_skinny_rows_equal_tensor_core_path(cuda, M, N, K):
+    """M <= 8 rows run on the dp4a kernel (automatic variant): bit-identical int32 sums and
+    dequant + bias to the tcgen05 path and the oracle."""
+    lib = _lib.load()
+    q = _rand_i8((M, K), 21)
+    w = _rand_i8((N, K), 22)
+    g = torch.Generator().manual_seed(23)
+    sx = (torch.rand(M, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
+    sw = (torch.rand(N, generator=g) * 0.02 + 0.001).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.5).to(torch.bfloat16)
+    qd, wd, sxd, swd, bd = q.cuda(), w.cuda(), sx.cuda(), sw.cuda(), b.cuda()
+    st = _lib.stream_of(qd)
+
+    def run(variant, bias):
+        assert lib.zib_gemm_set_variant(variant) == 0
+        acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+        y = torch.empty(M, N + (-N) % 8, dtype=torch.bfloat16, device="cuda")
+        _lib.call("zib_gemm_w8a8_acc_i32", qd.data_ptr(), K, wd.data_ptr(), K, acc.data_ptr(), N, M, N, K, st)
+        _lib.call("zib_gemm_w8a8", qd.data_ptr(), K, wd.data_ptr(), K, sxd.data_ptr(), swd.data_ptr(),
+                  bd.data_ptr() if bias else None, y.data_ptr(), y.stride(0), M, N, K, st)
+        torch.cuda.synchronize()
+        assert _lib.device_error_read_clear() == 0
+        return acc.cpu(), y[:, :N].cpu()
+
+    try:
+        for bias in (False, True):
+            a0, y0 = run(0, bias)
+            a1, y1 = run(1, bias)
+            assert torch.equal(a0, a1) and torch.equal(y0, y1)
+            want = ops.gemm_acc_i32(q, w)
+            assert torch.equal(a0, want)
+            assert torch.equal(y0, ops.dequant_epilogue(want, sx, sw, b if bias else None))
+    finally:
+        lib.zib_gemm_set_variant(0)
+
+
 @pytest.mark.parametrize("M,N,K,check_oracle", [(2560, 2048, 6144, True), (1024, 11520, 10240, False),
                                                 (9216, 3840, 10240, False)])
 def test_gemm_split_tail_equals_unsplit(cuda, M, N, K, check_oracle):
