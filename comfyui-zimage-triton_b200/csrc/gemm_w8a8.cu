@@ -1145,55 +1145,34 @@ static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 // A launch of T tiles on C persistent CTA pairs runs ceil(T / C) waves; when the
 // last wave is short (R = T mod C tiles), those R tiles are split along K into
 // S = min(C / R, 4) units so that the last wave is ~1/S as long.  The partial
-// int32 tiles meet in a per-device workspace (one slot per unit and CTA of the
-// pair, 128 KB each) with one arrival counter per tail tile and CTA; the last
-// arrival resets its counter.  The workspace is allocated on first use outside
-// stream capture (sized for one unit per CTA pair) and kept; launches of split
-// GEMMs that overlap on different streams of one device would share it, so
-// such callers turn splitting off (zib_gemm_set_split(0)).
+// int32 tiles meet in a workspace (one 128 KB slot per unit and CTA of the
+// pair) with one arrival counter per tail tile and CTA; the last arrival
+// resets its counter.  The caller owns the workspace: it allocates it,
+// zero-fills the counters and registers it per device with
+// zib_gemm_set_split_workspace (the Python layer does this with torch on first
+// use); the library never allocates.  Without a registered workspace, or with
+// one too small for the tail, a launch runs unsplit (or with fewer splits).
+// Launches that use one workspace must not overlap on the GPU.
 static bool g_split_enabled = true;
 constexpr int kSplitMinKBlocks = 48;  // K >= 6144
+constexpr int64_t kSplitUnitBytes = 2 * 128 * 256 * sizeof(int32_t);  // both CTAs' partial tiles
 struct SplitWs {
   int32_t* ws = nullptr;
   int* ctr = nullptr;
-  int units = 0;
+  int units = 0;     // partial-tile pairs the workspace holds
+  int tails = 0;     // tail tiles its counters cover
 };
 static std::mutex g_split_mu;
 static SplitWs g_split_ws[64];
 
-static const SplitWs* split_workspace(int units, cudaStream_t st) {
+static SplitWs split_workspace() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     cudaGetLastError();
-    return nullptr;
+    return SplitWs{};
   }
   std::lock_guard<std::mutex> lk(g_split_mu);
-  SplitWs& w = g_split_ws[dev];
-  if (w.units >= units) return &w;
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return nullptr;  // no allocation inside a capture: this launch runs unsplit
-  }
-  int32_t* ws = nullptr;
-  int* ctr = nullptr;
-  if (cudaMalloc(&ws, (size_t)units * 2 * 128 * 256 * sizeof(int32_t)) != cudaSuccess ||
-      cudaMalloc(&ctr, (size_t)units * 2 * sizeof(int)) != cudaSuccess ||
-      cudaMemset(ctr, 0, (size_t)units * 2 * sizeof(int)) != cudaSuccess) {
-    cudaGetLastError();
-    if (ws) cudaFree(ws);
-    if (ctr) cudaFree(ctr);
-    return nullptr;
-  }
-  if (w.ws) {  // a larger replacement: the old buffers may still be in use by queued launches
-    cudaDeviceSynchronize();
-    cudaFree(w.ws);
-    cudaFree(w.ctr);
-  }
-  w.ws = ws;
-  w.ctr = ctr;
-  w.units = units;
-  return &w;
+  return g_split_ws[dev];
 }
 
 // The allocation-free variant (zib_gemm_w8a8_static_scratch), for callers that
@@ -1270,7 +1249,7 @@ static int plan_split_static(Params& p, int clusters, int splits, const char* wh
 }
 
 // Decide the split of the last wave (pair kernel, plain and int32 epilogues).
-static void plan_split(Params& p, int clusters, cudaStream_t st) {
+static void plan_split(Params& p, int clusters) {
   p.num_units = p.num_tiles;
   p.tail_start = p.num_tiles;
   p.splits = 1;
@@ -1282,14 +1261,15 @@ static void plan_split(Params& p, int clusters, cudaStream_t st) {
   int S = C / R;
   if (S > 4) S = 4;
   if (S > p.num_kb / 2) S = p.num_kb / 2;  // at least two K-blocks per split
+  const SplitWs w = split_workspace();
+  if (!w.ws || R > w.tails) return;
+  if (R * S > w.units) S = w.units / R;  // as many splits as the registered workspace holds
   if (S < 2) return;
-  const SplitWs* w = split_workspace(C, st);
-  if (!w) return;
   p.tail_start = T - R;
   p.splits = S;
   p.num_units = p.tail_start + R * S;
-  p.ws = w->ws;
-  p.counters = w->ctr;
+  p.ws = w.ws;
+  p.counters = w.ctr;
 }
 
 // M <= 8 rows: the skinny kernel (one launch, CTAs sized for four per SM).
@@ -1378,7 +1358,7 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
         const int st = plan_split_static(p, clusters, static_splits, what);
         if (st) return st;
       } else {
-        plan_split(p, clusters, (cudaStream_t)stream);
+        plan_split(p, clusters);
       }
     }
     gemm_w8a8_pair_kernel<EPI><<<2 * clusters, Cfg<EPI>::THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
@@ -1530,6 +1510,27 @@ extern "C" int zib_selftest_bounded_wait(void* stream) {
   return zib_check_launch("selftest_bounded_wait");
 }
 
+extern "C" int zib_gemm_set_split_workspace(int device, void* ws, int64_t ws_bytes, void* counters,
+                                            int64_t n_counters) {
+  ZIB_HOST_CHECK(device >= 0 && device < 64, ZIB_ERR_INVALID_ARG, "gemm_set_split_workspace: bad device %d",
+                 device);
+  ZIB_HOST_CHECK((ws == nullptr) == (counters == nullptr), ZIB_ERR_INVALID_ARG,
+                 "gemm_set_split_workspace: register both buffers or neither");
+  ZIB_HOST_CHECK(!ws || (ws_bytes >= zib::gemm::kSplitUnitBytes && n_counters >= 2), ZIB_ERR_INVALID_ARG,
+                 "gemm_set_split_workspace: needs at least %lld bytes and 2 counters",
+                 (long long)zib::gemm::kSplitUnitBytes);
+  ZIB_HOST_CHECK(!ws || (((uintptr_t)ws & 15) == 0 && ((uintptr_t)counters & 3) == 0), ZIB_ERR_ALIGNMENT,
+                 "gemm_set_split_workspace: the workspace must be 16-byte aligned");
+  std::lock_guard<std::mutex> lk(zib::gemm::g_split_mu);
+  zib::gemm::SplitWs& w = zib::gemm::g_split_ws[device];
+  w.ws = static_cast<int32_t*>(ws);
+  w.ctr = static_cast<int*>(counters);
+  const int64_t units = ws ? ws_bytes / zib::gemm::kSplitUnitBytes : 0;
+  w.units = (int)(units < (1 << 20) ? units : (1 << 20));
+  w.tails = ws ? (int)((n_counters / 2) < (1 << 20) ? n_counters / 2 : (1 << 20)) : 0;
+  return ZIB_OK;
+}
+
 extern "C" int zib_gemm_set_split(int enable) {
   zib::gemm::g_split_enabled = enable != 0;
   return ZIB_OK;
@@ -1545,7 +1546,7 @@ void zib_gemm_split_reset() {
     zib::gemm::StaticScratch& sc = zib::gemm::g_static_scratch[d];
     if (!w.ctr && !sc.ctr) continue;
     cudaSetDevice(d);
-    if (w.ctr) cudaMemset(w.ctr, 0, (size_t)w.units * 2 * sizeof(int));
+    if (w.ctr) cudaMemset(w.ctr, 0, (size_t)w.tails * 2 * sizeof(int));
     if (sc.ctr) cudaMemset(sc.ctr, 0, sizeof(zib::gemm::g_static_split_ctr));
   }
   cudaSetDevice(dev);

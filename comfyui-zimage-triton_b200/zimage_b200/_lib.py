@@ -44,6 +44,7 @@ SIGNATURES: dict[str, list] = {
                                    _F32, _F32, _VP, _VP, _I64, _I64, _I64, _VP],
     "zib_gemm_set_variant": [_I32],
     "zib_gemm_set_split": [_I32],
+    "zib_gemm_set_split_workspace": [_I32, _VP, _I64, _VP, _I64],
     "zib_gemm_w8a8_static_scratch": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _I32, _VP],
     "zib_weight_prep": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _VP],
     "zib_rms_norm": [_VP, _I64, _VP, _VP, _I64, _I64, _I64, _F32, _VP],
@@ -124,9 +125,31 @@ def stream_of(t: torch.Tensor) -> int:
 LAUNCHES = 0
 
 
+# Split-K workspaces of the plain GEMM entry points, one per device: allocated here with torch
+# (so the memory is the framework's, and the library itself never allocates) and registered
+# with zib_gemm_set_split_workspace on a device's first such GEMM.  256 KB of partial tiles per
+# CTA pair (one per two SMs) plus two zeroed arrival counters per tail tile.
+_SPLIT_WS: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+_SPLIT_GEMMS = ("zib_gemm_w8a8", "zib_gemm_w8a8_acc_i32")
+
+
+def ensure_split_workspace(dev: int | None = None) -> None:
+    dev = torch.cuda.current_device() if dev is None else dev
+    if dev in _SPLIT_WS:
+        return
+    pairs = max(1, torch.cuda.get_device_properties(dev).multi_processor_count // 2)
+    ws = torch.empty(pairs * 2 * 128 * 256, dtype=torch.int32, device=f"cuda:{dev}")
+    ctr = torch.zeros(pairs * 2, dtype=torch.int32, device=f"cuda:{dev}")
+    check(load().zib_gemm_set_split_workspace(dev, ws.data_ptr(), ws.numel() * 4, ctr.data_ptr(), ctr.numel()),
+          "zib_gemm_set_split_workspace")
+    _SPLIT_WS[dev] = (ws, ctr)
+
+
 def call(name: str, *args) -> None:
     """Invoke ``name`` and raise on a non-zero status."""
     global LAUNCHES
+    if name in _SPLIT_GEMMS:
+        ensure_split_workspace()
     LAUNCHES += 1
     check(getattr(load(), name)(*args), name)
 

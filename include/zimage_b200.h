@@ -132,11 +132,21 @@ ZIB_API int zib_gemm_set_variant(int variant);
 /* Split-K tail for zib_gemm_w8a8 and zib_gemm_w8a8_acc_i32 with 2-CTA tiles
  * (on by default): when the last wave of tiles is short and K >= 6144, its
  * tiles run as 2-4 units over slices of K whose int32 partials are summed by
- * the last unit to finish (bit-identical results).  Uses a per-device workspace of 256 KB
- * per CTA pair (~19 MB on B200), allocated on first use outside stream capture;
- * launches that overlap on different streams of one device must turn it off.
- * No reference counterpart (tuning knob). */
+ * the last unit to finish (bit-identical results).  It needs the workspace
+ * that the caller registers with zib_gemm_set_split_workspace; without one
+ * the GEMM runs unsplit.  No reference counterpart (tuning knob). */
 ZIB_API int zib_gemm_set_split(int enable);
+
+/* Registers the caller's split-K workspace for `device` (NULL, NULL
+ * unregisters): `ws` (16-byte aligned) holds ws_bytes / 256 KB partial-tile
+ * pairs, `counters` n_counters int32 that must be zero when registered (each
+ * completed GEMM leaves them at zero; zib_device_error_read_clear() re-zeroes
+ * them after a device error).  The caller keeps both alive while GEMMs may use
+ * them, and GEMMs on that device that use them must not overlap on the GPU.
+ * One 256 KB pair per two SMs and two counters per pair cover every launch
+ * (~19 MB on B200).  No reference counterpart (the caller owns all workspaces). */
+ZIB_API int zib_gemm_set_split_workspace(int device, void* ws, int64_t ws_bytes, void* counters,
+                               int64_t n_counters);
 
 /* zib_gemm_w8a8 for callers that must not allocate device memory: a host
  * framework that owns the GPU's memory through its own pool and budget (a

@@ -59,6 +59,13 @@ def test_host_validation_before_launch():
     # misaligned output of the SwiGLU epilogue
     assert lib.zib_gemm_w8a8_swiglu_had(16, 128, 16, 16, 128, 16, 16, 16, 18, 128, 8, 128, 128, None) == \
         _lib.ZIB_ERR_ALIGNMENT
+    # split-K workspace registration: both buffers or neither, at least one partial-tile pair, aligned
+    pair = 2 * 128 * 256 * 4
+    assert lib.zib_gemm_set_split_workspace(0, 4096, pair, None, 2) == _lib.ZIB_ERR_INVALID_ARG
+    assert lib.zib_gemm_set_split_workspace(0, 4096, pair - 16, 8192, 2) == _lib.ZIB_ERR_INVALID_ARG
+    assert lib.zib_gemm_set_split_workspace(0, 4100, pair, 8192, 2) == _lib.ZIB_ERR_ALIGNMENT
+    assert lib.zib_gemm_set_split_workspace(64, 4096, pair, 8192, 2) == _lib.ZIB_ERR_INVALID_ARG
+    assert lib.zib_gemm_set_split_workspace(0, None, 0, None, 0) == _lib.ZIB_OK  # nothing registered
     with pytest.raises(ValueError):
         _lib.check(_lib.ZIB_ERR_INVALID_ARG, "x")
     with pytest.raises(RuntimeError):

@@ -206,9 +206,20 @@ def test_gemm_split_tail_equals_unsplit(cuda, M, N, K, check_oracle):
         a1, y1 = run(1)
         a2, y2 = run(1)
         a0, y0 = run(0)
+        # no registered workspace: the launch runs unsplit
+        dev = torch.cuda.current_device()
+        assert lib.zib_gemm_set_split_workspace(dev, None, 0, None, 0) == 0
+        acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+        assert lib.zib_gemm_set_split(1) == 0
+        lib.zib_gemm_w8a8_acc_i32(qd.data_ptr(), K, wd.data_ptr(), K, acc.data_ptr(), N, M, N, K, st)
+        torch.cuda.synchronize()
+        a3 = acc.cpu()
     finally:
         lib.zib_gemm_set_split(1)
-    assert torch.equal(a1, a0) and torch.equal(a2, a0)
+        ws, ctr = _lib._SPLIT_WS[torch.cuda.current_device()]
+        lib.zib_gemm_set_split_workspace(torch.cuda.current_device(), ws.data_ptr(), ws.numel() * 4,
+                                         ctr.data_ptr(), ctr.numel())
+    assert torch.equal(a1, a0) and torch.equal(a2, a0) and torch.equal(a3, a0)
     assert torch.equal(y1, y0) and torch.equal(y2, y0)
     if check_oracle:
         want = ops.gemm_acc_i32(q, w)
