@@ -154,8 +154,9 @@ ZIB_API int zib_gemm_set_split_workspace(int device, void* ws, int64_t ws_bytes,
  * can fail when the pool already holds the free memory), code recording a CUDA
  * stream capture (which refuses cudaMalloc), and latency-bound loops (cudaMalloc
  * and cudaFree synchronise the device).  Its split-K tail uses a static device
- * scratch area instead of the workspace that zib_gemm_w8a8 allocates on first
- * use; the call allocates and frees nothing.  `splits` (1-4) is the number of
+ * scratch area instead of a workspace that the caller would have to allocate
+ * and register (zib_gemm_set_split_workspace); the call allocates and frees
+ * nothing.  `splits` (1-4) is the number of
  * K-slices each tile of a short last wave runs as (2-CTA tiles, M > 128;
  * 1 = no split; launches without a short last wave run unsplit).  Limit: the
  * scratch holds 64 units of 256 KB (16 MB of device memory on every GPU that

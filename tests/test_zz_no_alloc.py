@@ -3,7 +3,7 @@
 The static-scratch GEMM is for callers that must not allocate device memory (a framework
 that budgets the GPU's memory through its own pool, a stream capture in progress, a
 latency-bound loop where cudaMalloc would synchronise): its split-K partials live in a fixed
-16 MB static device area instead of a workspace allocated on first use.
+16 MB static device area instead of a workspace that the caller allocates and registers.
 
 Kept in its own file so that it is collected last: it must pass alone and after the rest
 of the suite, with whatever the earlier tests left in the static scratch.
