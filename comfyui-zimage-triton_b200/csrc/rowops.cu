@@ -312,57 +312,60 @@ __global__ void __launch_bounds__(256, 3) qknorm_rope_kernel(
     const float* __restrict__ w, int64_t S, int64_t H, int64_t total_rows, float eps) {
   // 16 lanes per (token, head) row, 8 values (4 pairs) per lane; each half-warp
   // handles R rows spaced 16 apart so the block's loads stay contiguous and
-  // every thread has R independent loads in flight.
+  // every thread has R independent loads in flight.  Row indices are split
+  // with 32-bit divisions (the host checks that they fit).
   const int lane = threadIdx.x & 31;
   const int sub = lane & 15;
   const int hw = threadIdx.x >> 4;
-  const int64_t base = (int64_t)blockIdx.x * (16 * R);
-  float v[R][8];
+  const uint32_t base = blockIdx.x * (16u * R);
+  const uint32_t H32 = (uint32_t)H, S32 = (uint32_t)S;
+  uint4 xv[R];
   float4 c4[R], s4[R];
   int64_t oo[R];
   bool ok[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const int64_t rowg = base + r * 16 + hw;
-    ok[r] = rowg < total_rows;
-    const int64_t rr = ok[r] ? rowg : 0;
-    const int64_t h = rr % H;
-    const int64_t t = rr / H;
-    const int64_t s = t % S;
-    const int64_t b = t / S;
-    load_bf16x8(x + b * x_sb + s * x_ss + h * x_sh + sub * 8, v[r]);
+    const uint32_t rowg = base + r * 16u + (uint32_t)hw;
+    ok[r] = rowg < (uint64_t)total_rows;
+    const uint32_t rr = ok[r] ? rowg : 0u;
+    const uint32_t t = rr / H32, h = rr - t * H32;
+    const uint32_t b = t / S32, s = t - b * S32;
+    xv[r] = *reinterpret_cast<const uint4*>(x + b * x_sb + s * x_ss + h * x_sh + sub * 8);
     c4[r] = __ldg(reinterpret_cast<const float4*>(cosp + b * cs_b + s * 64 + sub * 4));
     s4[r] = __ldg(reinterpret_cast<const float4*>(sinp + b * cs_b + s * 64 + sub * 4));
     oo[r] = b * o_sb + s * o_ss + h * o_sh + sub * 8;
   }
-  float wv[8];
+  float4 wa = make_float4(0.f, 0.f, 0.f, 0.f), wb = wa;
   if (NORM) {
-    const float4 wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
-    const float4 wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
-    wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
-    wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
+    wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
+    wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
+    uint4 v = xv[r];
     if (NORM) {
-      double ss = 0.0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += (double)(v[r][j] * v[r][j]);
+      // exact sum of squares (fp64), then bf16(bf16(x * rstd) * w) two lanes per instruction
+      double a = 0.0, bsum = 0.0;
+      px::sumsq_acc(v.x, a, bsum);
+      px::sumsq_acc(v.y, a, bsum);
+      px::sumsq_acc(v.z, a, bsum);
+      px::sumsq_acc(v.w, a, bsum);
+      double ss = a + bsum;
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-      const float rstd = rstd_from_sum(ss, 128, eps);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[r][j] = bf16_round(__fmul_rn(bf16_round(__fmul_rn(v[r][j], rstd)), wv[j]));
+      v = px::norm_w(v, rstd_from_sum(ss, 128, eps), wa, wb);
     }
     const float cv[4] = {c4[r].x, c4[r].y, c4[r].z, c4[r].w};
     const float sv[4] = {s4[r].x, s4[r].y, s4[r].z, s4[r].w};
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float a = v[r][2 * k], bb = v[r][2 * k + 1];
-      v[r][2 * k] = bf16_round(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(bb, sv[k])));
-      v[r][2 * k + 1] = bf16_round(__fadd_rn(__fmul_rn(bb, cv[k]), __fmul_rn(a, sv[k])));
+    for (int k = 0; k < 4; ++k) {  // pair rotation: products and sums scalar, each rounded once
+      const float a = __uint_as_float(wv[k] << 16), bb = __uint_as_float(wv[k] & 0xFFFF0000u);
+      o[k] = px::to_bf16x2(px::mk(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(bb, sv[k])),
+                                  __fadd_rn(__fmul_rn(bb, cv[k]), __fmul_rn(a, sv[k]))));
     }
-    if (ok[r]) store_bf16x8(out + oo[r], v[r]);
+    if (ok[r]) *reinterpret_cast<uint4*>(out + oo[r]) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -1361,6 +1364,7 @@ extern "C" int zib_qknorm_rope(const void* x, int64_t x_sb, int64_t x_ss, int64_
                  ZIB_ERR_ALIGNMENT, "qknorm_rope: operands must be 16-byte aligned");
   const int64_t rows = B * S * H;
   if (rows == 0) return ZIB_OK;
+  ZIB_HOST_CHECK(rows < (1ll << 31), ZIB_ERR_TOO_LARGE, "qknorm_rope: more than 2^31 rows");
   constexpr int R = 4;
   const int rows_per_block = 16 * R;  // 256 threads, 4 rows per half-warp
   const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
