@@ -1318,6 +1318,13 @@ extern "C" int zib_swiglu(const void* gate, int64_t ldg, const void* up, int64_t
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (vec)
+    launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+      constexpr int R = decltype(Rc)::value;
+      auto k = wr::swiglu_wr<R, false, false>;
+      k<<<wr::grid_for(k, R, cpl, 0, rows), 32 * wr::kWarps, 0, st>>>(
+          (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, (uint16_t*)out, ldo, nullptr, 0, nullptr, cpl, rows);
+    });
+  if (vec && !launched)
     ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_PIPE_TRY((pipe::swiglu_pipe<W, false, false>), 1, rows, n,
         (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, (uint16_t*)out, ldo, nullptr, 0, nullptr, n));
   if (!launched)
@@ -1339,7 +1346,14 @@ extern "C" int zib_swiglu_quant(const void* gate, int64_t ldg, const void* up, i
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "swiglu_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = false;
+  bool launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+    constexpr int R = decltype(Rc)::value;
+    auto k = hadamard ? wr::swiglu_wr<R, true, true> : wr::swiglu_wr<R, true, false>;
+    wr::set_smem(k, wr::smem_for(cpl, 1));
+    k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+        (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, cpl, rows);
+  });
+  if (!launched)
   ZIB_DISPATCH_W(pipe::pipe_warps(n), ZIB_DISPATCH_BOOL(hadamard, HAD,
       ZIB_PIPE_TRY((pipe::swiglu_pipe<W, true, HAD>), 1, rows, n,
           (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, n)));

@@ -357,6 +357,49 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
   }
 }
 
+// out = bf16(bf16(silu(g)) * u) (swiglu.py:51-58); QUANT: then rotate (HAD) and
+// quantise the row (int8_linear.py:119-130) instead of storing it.  silu and the
+// product are the packed forms of the SwiGLU GEMM epilogue (same roundings as
+// the scalar fp32 ones: the product of two bf16 values is exact in fp32).
+template <int R, bool QUANT, bool HAD>
+__global__ void __launch_bounds__(32 * kWarps) swiglu_wr(
+    const uint16_t* __restrict__ g, int64_t ldg, const uint16_t* __restrict__ u, int64_t ldu,
+    uint16_t* __restrict__ out, int64_t ldo, int8_t* __restrict__ q, int64_t ldq, uint16_t* __restrict__ sx,
+    int cpl, int64_t rows) {
+  __shared__ uint32_t redu[kWarps];
+  const Team<R> t;
+  const int64_t f0 = t.first(cpl);
+  uint4* sl = QUANT ? warp_slice(cpl, 1) : nullptr;
+  const int64_t step = (int64_t)gridDim.x * (kWarps / R);
+  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows; row += step) {
+    const uint16_t* gr = g + row * ldg + f0;
+    const uint16_t* ur = u + row * ldu + f0;
+    px::AbsMax m;
+#pragma unroll 4
+    for (int k = 0; k < cpl; ++k) {
+      const uint4 gv = ld_nc(gr + 256 * k), uv = ld_nc(ur + 256 * k);
+      const uint4 v = make_uint4(hmul2(px::silu_bf16x2(gv.x), uv.x), hmul2(px::silu_bf16x2(gv.y), uv.y),
+                                 hmul2(px::silu_bf16x2(gv.z), uv.z), hmul2(px::silu_bf16x2(gv.w), uv.w));
+      if (!QUANT) {
+        *reinterpret_cast<uint4*>(out + row * ldo + f0 + 256 * k) = v;
+      } else {
+        sl[32 * k] = v;
+        if (!HAD) m.add(v);
+      }
+    }
+    if (QUANT) {
+      if (HAD) {
+        uint4* base = sl - t.lane;
+        __syncwarp();  // chunks written by other lanes
+        rotate_pairs(base, cpl, t.lane, m, [&](int c) { return base[c]; }, NoSink{});
+        __syncwarp();
+      }
+      quant_row<R>(t, sl, cpl, m.packed(), redu, row, q, ldq, sx);
+      __syncwarp();
+    }
+  }
+}
+
 // --- host side ---------------------------------------------------------------------------
 
 // Team size and chunks per lane for a row of n bf16: n % 256 == 0 and at most
