@@ -1113,8 +1113,8 @@ extern "C" int zib_act_quant(const void* x, int64_t ldx, void* q, int64_t ldq, v
   bool launched = wr::dispatch(K, [&](auto Rc, int cpl) {
     constexpr int R = decltype(Rc)::value;
     auto k = hadamard ? wr::act_quant_wr<R, true> : wr::act_quant_wr<R, false>;
-    wr::set_smem(k, wr::smem_for(cpl, 1));
-    k<<<wr::grid_for(k, R, cpl, 1, M), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+    wr::set_smem(k, wr::smem_for(R, cpl, 1));
+    k<<<wr::grid_for(k, R, cpl, 1, M), 32 * wr::warps_of(R), wr::smem_for(R, cpl, 1), st>>>(
         (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, cpl, M);
   });
   if (!launched && !x_rot)
@@ -1143,8 +1143,8 @@ extern "C" int zib_rms_norm(const void* x, int64_t ldx, const float* w, void* y,
     launched = wr::dispatch(n, [&](auto Rc, int cpl) {
       constexpr int R = decltype(Rc)::value;
       auto k = wr::rmsnorm_wr<R, 0, false>;
-      wr::set_smem(k, wr::smem_for(cpl, 1));
-      k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+      wr::set_smem(k, wr::smem_for(R, cpl, 1));
+      k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::warps_of(R), wr::smem_for(R, cpl, 1), st>>>(
           (const uint16_t*)x, ldx, w, nullptr, nullptr, 0, 1, (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps, cpl,
           rows);
     });
@@ -1175,8 +1175,8 @@ extern "C" int zib_rmsnorm_mod(const void* x, int64_t ldx, const float* w, const
     launched = wr::dispatch(n, [&](auto Rc, int cpl) {
       constexpr int R = decltype(Rc)::value;
       auto k = wr::rmsnorm_wr<R, 1, false>;
-      wr::set_smem(k, wr::smem_for(cpl, 1));
-      k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+      wr::set_smem(k, wr::smem_for(R, cpl, 1));
+      k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::warps_of(R), wr::smem_for(R, cpl, 1), st>>>(
           (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
           (uint16_t*)y, ldy, nullptr, 0, nullptr, n, eps, cpl, rows);
     });
@@ -1209,8 +1209,8 @@ extern "C" int zib_rmsnorm_mod_quant(const void* x, int64_t ldx, const float* w,
   bool launched = wr::dispatch(n, [&](auto Rc, int cpl) {
     constexpr int R = decltype(Rc)::value;
     auto k = hadamard ? wr::rmsnorm_wr<R, 2, true> : wr::rmsnorm_wr<R, 2, false>;
-    wr::set_smem(k, wr::smem_for(cpl, 1));
-    k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+    wr::set_smem(k, wr::smem_for(R, cpl, 1));
+    k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::warps_of(R), wr::smem_for(R, cpl, 1), st>>>(
         (const uint16_t*)x, ldx, w, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, rows_per_batch,
         nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, n, eps, cpl, rows);
   });
@@ -1242,11 +1242,12 @@ extern "C" int zib_norm_gate_residual(const void* x, int64_t ldx, const void* r,
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (vec)
-    launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+    launched = wr::dispatch<true>(n, [&](auto Rc, int cpl) {
       constexpr int R = decltype(Rc)::value;
+      constexpr int nb = wr::ngr_buffers(R);
       auto k = wr::ngr_wr<R, false, false>;
-      wr::set_smem(k, wr::smem_for(cpl, 1));
-      k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+      wr::set_smem(k, wr::smem_for(R, cpl, nb));
+      k<<<wr::grid_for(k, R, cpl, nb, rows), 32 * wr::warps_of(R), wr::smem_for(R, cpl, nb), st>>>(
           (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
           (uint16_t*)y, ldy, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, n, eps, eps, cpl, rows);
     });
@@ -1281,11 +1282,12 @@ extern "C" int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, cons
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "norm_gate_residual_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+  bool launched = wr::dispatch<true>(n, [&](auto Rc, int cpl) {
     constexpr int R = decltype(Rc)::value;
+    constexpr int nb = wr::ngr_buffers(R);
     auto k = hadamard ? wr::ngr_wr<R, true, true> : wr::ngr_wr<R, true, false>;
-    wr::set_smem(k, wr::smem_for(cpl, 1));
-    k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+    wr::set_smem(k, wr::smem_for(R, cpl, nb));
+    k<<<wr::grid_for(k, R, cpl, nb, rows), 32 * wr::warps_of(R), wr::smem_for(R, cpl, nb), st>>>(
         (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
         (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
         (uint16_t*)sx, n, eps, eps2, cpl, rows);
@@ -1321,7 +1323,7 @@ extern "C" int zib_swiglu(const void* gate, int64_t ldg, const void* up, int64_t
     launched = wr::dispatch(n, [&](auto Rc, int cpl) {
       constexpr int R = decltype(Rc)::value;
       auto k = wr::swiglu_wr<R, false, false>;
-      k<<<wr::grid_for(k, R, cpl, 0, rows), 32 * wr::kWarps, 0, st>>>(
+      k<<<wr::grid_for(k, R, cpl, 0, rows), 32 * wr::warps_of(R), 0, st>>>(
           (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, (uint16_t*)out, ldo, nullptr, 0, nullptr, cpl, rows);
     });
   if (vec && !launched)
@@ -1349,8 +1351,8 @@ extern "C" int zib_swiglu_quant(const void* gate, int64_t ldg, const void* up, i
   bool launched = wr::dispatch(n, [&](auto Rc, int cpl) {
     constexpr int R = decltype(Rc)::value;
     auto k = hadamard ? wr::swiglu_wr<R, true, true> : wr::swiglu_wr<R, true, false>;
-    wr::set_smem(k, wr::smem_for(cpl, 1));
-    k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::kWarps, wr::smem_for(cpl, 1), st>>>(
+    wr::set_smem(k, wr::smem_for(R, cpl, 1));
+    k<<<wr::grid_for(k, R, cpl, 1, rows), 32 * wr::warps_of(R), wr::smem_for(R, cpl, 1), st>>>(
         (const uint16_t*)gate, ldg, (const uint16_t*)up, ldu, nullptr, 0, (int8_t*)q, ldq, (uint16_t*)sx, cpl, rows);
   });
   if (!launched)

@@ -1,5 +1,6 @@
 // Warp-per-row kernels: R warps per row (R = 1 for 3840 columns, 4 for
-// 10240), one read of every input and one write of every output.
+// 10240; the fused norm kernels take teams of 3 for 3840), one read of every
+// input and one write of every output.
 //
 // Lane l of warp r in a row's team owns the 16-byte chunks (8 bf16)
 //   c = 32 * cpl * r + l + 32 * k,   k = 0 .. cpl-1,
@@ -24,7 +25,10 @@
 
 namespace wr {
 
-constexpr int kWarps = 4;  // warps per CTA; a CTA runs kWarps / R rows at a time
+constexpr int kWarps = 4;  // warps per CTA when R divides it; a CTA runs kWarps / R rows at a time
+
+// warps per CTA for teams of R warps: kWarps when R divides it, else one team
+__host__ __device__ constexpr int warps_of(int R) { return kWarps % R == 0 ? kWarps : R; }
 
 // --- packed bf16x2 helpers --------------------------------------------------------
 
@@ -70,7 +74,8 @@ struct Team {
     grp = w / R;
   }
   __device__ __forceinline__ void sync() const {
-    if (R > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "r"(R * 32) : "memory");
+    // barrier 1 + team (a constant when the CTA is one team)
+    if (R > 1) asm volatile("bar.sync %0, %1;" ::"r"(warps_of(R) == R ? 1 : 1 + grp), "r"(R * 32) : "memory");
   }
   // exact in practice: every partial is an exact fp64 sum of exact fp32 squares
   __device__ __forceinline__ double sum(double v, double* red) const {
@@ -212,16 +217,16 @@ __device__ __forceinline__ void quant_row(const Team<R>& t, const uint4* sl, int
 }
 
 template <int R, bool HAD>
-__global__ void __launch_bounds__(32 * kWarps) act_quant_wr(const uint16_t* __restrict__ x, int64_t ldx,
+__global__ void __launch_bounds__(32 * warps_of(R)) act_quant_wr(const uint16_t* __restrict__ x, int64_t ldx,
                                                             int8_t* __restrict__ q, int64_t ldq,
                                                             uint16_t* __restrict__ sx, uint16_t* __restrict__ xr,
                                                             int cpl, int64_t rows) {
-  __shared__ uint32_t redu[kWarps];
+  __shared__ uint32_t redu[warps_of(R)];
   const Team<R> t;
   const int64_t f0 = t.first(cpl);
   uint4* sl = warp_slice(cpl, 1);
-  const int64_t step = (int64_t)gridDim.x * (kWarps / R);
-  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows; row += step) {
+  const int64_t step = (int64_t)gridDim.x * (warps_of(R) / R);
+  for (int64_t row = (int64_t)blockIdx.x * (warps_of(R) / R) + t.grp; row < rows; row += step) {
     // this warp's next row into L2 (measured: helps the plain quantiser, slows the rotating kernels)
     if (!HAD && row + step < rows) prefetch_row(t, x + (row + step) * ldx, cpl);
     copy_row(x + row * ldx + f0, sl, cpl);
@@ -251,19 +256,19 @@ __global__ void __launch_bounds__(32 * kWarps) act_quant_wr(const uint16_t* __re
 
 // MODE 0: rmsnorm -> bf16; 1: rmsnorm * (1+s) (+shift) -> bf16; 2: MODE 1 -> rotate / quant
 template <int R, int MODE, bool HAD>
-__global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
+__global__ void __launch_bounds__(32 * warps_of(R)) rmsnorm_wr(
     const uint16_t* __restrict__ x, int64_t ldx, const float* __restrict__ w, const uint16_t* __restrict__ scale,
     const uint16_t* __restrict__ shift, int64_t ld_mod, int64_t rows_per_batch, uint16_t* __restrict__ y,
     int64_t ldy, int8_t* __restrict__ q, int64_t ldq, uint16_t* __restrict__ sx, int64_t n, float eps, int cpl,
     int64_t rows) {
-  __shared__ double redd[kWarps];
-  __shared__ uint32_t redu[kWarps];
+  __shared__ double redd[warps_of(R)];
+  __shared__ uint32_t redu[warps_of(R)];
   const Team<R> t;
   const int64_t f0 = t.first(cpl);
   const float* wl = w + f0;
   uint4* sl = warp_slice(cpl, 1);
-  const int64_t step = (int64_t)gridDim.x * (kWarps / R);
-  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows; row += step) {
+  const int64_t step = (int64_t)gridDim.x * (warps_of(R) / R);
+  for (int64_t row = (int64_t)blockIdx.x * (warps_of(R) / R) + t.grp; row < rows; row += step) {
     copy_row(x + row * ldx + f0, sl, cpl);
     copies_done();
     const float rstd = rstd_from_sum(t.sum(row_sumsq(sl, cpl), redd), (int)n, eps);
@@ -300,33 +305,52 @@ __global__ void __launch_bounds__(32 * kWarps) rmsnorm_wr(
   }
 }
 
-// y = r + g * rmsnorm(x); FUSE: then rmsnorm(y; w2) * (1+s) (+shift) -> rotate / quant
+// row buffers per warp of ngr_wr: the residual row is staged for teams of three
+__host__ __device__ constexpr int ngr_buffers(int R) { return R == 3 ? 2 : 1; }
+
+// y = r + g * rmsnorm(x); FUSE: then rmsnorm(y; w2) * (1+s) (+shift) -> rotate / quant.
+// Teams of three warps (R = 3, picked for 3840 features) copy the residual row
+// into a second row buffer together with x, so that both rows are in flight at
+// once; otherwise the residual is loaded chunk by chunk after the first norm's
+// reduction.  Measured at [9216, 3840] on B200: one warp per row 94 us; teams
+// of three 86 us (a row's latency split three ways, with a third of a row's
+// buffer per warp); the staged residual 86 us fused, 47 -> 45 us unfused; with
+// one warp per row the doubled buffer halves the resident warps and costs 22 us.
 template <int R, bool FUSE, bool HAD>
-__global__ void __launch_bounds__(32 * kWarps) ngr_wr(
+__global__ void __launch_bounds__(32 * warps_of(R)) ngr_wr(
     const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ r, int64_t ldr,
     const uint16_t* __restrict__ gate, int64_t ld_gate, int64_t rows_per_batch, const float* __restrict__ w,
     uint16_t* __restrict__ y, int64_t ldy, const float* __restrict__ w2, const uint16_t* __restrict__ scale,
     const uint16_t* __restrict__ shift, int64_t ld_mod, int8_t* __restrict__ q, int64_t ldq,
     uint16_t* __restrict__ sx, int64_t n, float eps, float eps2, int cpl, int64_t rows) {
-  __shared__ double redd[kWarps];
-  __shared__ uint32_t redu[kWarps];
+  __shared__ double redd[warps_of(R)];
+  __shared__ uint32_t redu[warps_of(R)];
   const Team<R> t;
   const int64_t f0 = t.first(cpl);
   const float* wl = w + f0;
-  uint4* sl = warp_slice(cpl, 1);  // x, then y
-  const int64_t step = (int64_t)gridDim.x * (kWarps / R);
-  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows; row += step) {
+  constexpr bool STAGE = R == 3;
+  uint4* sl = warp_slice(cpl, ngr_buffers(R));  // x, then y
+  uint4* se = sl + 32 * cpl;                    // STAGE: the residual row
+  const int64_t step = (int64_t)gridDim.x * (warps_of(R) / R);
+  for (int64_t row = (int64_t)blockIdx.x * (warps_of(R) / R) + t.grp; row < rows; row += step) {
     const uint16_t* rr = r + row * ldr + f0;
     copy_row(x + row * ldx + f0, sl, cpl);
-    copies_done();
+    if (STAGE) {
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      copy_row(rr, se, cpl);
+      asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 1;" ::: "memory");  // x has landed
+    } else {
+      copies_done();
+    }
     const float rstd = rstd_from_sum(t.sum(row_sumsq(sl, cpl), redd), (int)n, eps);
     const int64_t b = batch_of(row, rows_per_batch);
     const uint16_t* gl = gate + b * ld_gate + f0;
     uint16_t* yr = y + row * ldy + f0;
     double ss2 = 0.0;
+    if (STAGE) asm volatile("cp.async.wait_group 0;" ::: "memory");  // the residual row has landed
 #pragma unroll 4
     for (int k = 0; k < cpl; ++k) {
-      const uint4 e = __ldcs(reinterpret_cast<const uint4*>(rr + 256 * k));
+      const uint4 e = STAGE ? se[32 * k] : __ldcs(reinterpret_cast<const uint4*>(rr + 256 * k));
       const uint4 a = px::norm_w(sl[32 * k], rstd, wl + 256 * k);
       const uint4 g = ld_nc(gl + 256 * k);
       // bf16(r + bf16(g * a)), fused_norm_residual.py:69-73
@@ -362,16 +386,16 @@ __global__ void __launch_bounds__(32 * kWarps) ngr_wr(
 // product are the packed forms of the SwiGLU GEMM epilogue (same roundings as
 // the scalar fp32 ones: the product of two bf16 values is exact in fp32).
 template <int R, bool QUANT, bool HAD>
-__global__ void __launch_bounds__(32 * kWarps) swiglu_wr(
+__global__ void __launch_bounds__(32 * warps_of(R)) swiglu_wr(
     const uint16_t* __restrict__ g, int64_t ldg, const uint16_t* __restrict__ u, int64_t ldu,
     uint16_t* __restrict__ out, int64_t ldo, int8_t* __restrict__ q, int64_t ldq, uint16_t* __restrict__ sx,
     int cpl, int64_t rows) {
-  __shared__ uint32_t redu[kWarps];
+  __shared__ uint32_t redu[warps_of(R)];
   const Team<R> t;
   const int64_t f0 = t.first(cpl);
   uint4* sl = QUANT ? warp_slice(cpl, 1) : nullptr;
-  const int64_t step = (int64_t)gridDim.x * (kWarps / R);
-  for (int64_t row = (int64_t)blockIdx.x * (kWarps / R) + t.grp; row < rows; row += step) {
+  const int64_t step = (int64_t)gridDim.x * (warps_of(R) / R);
+  for (int64_t row = (int64_t)blockIdx.x * (warps_of(R) / R) + t.grp; row < rows; row += step) {
     const uint16_t* gr = g + row * ldg + f0;
     const uint16_t* ur = u + row * ldu + f0;
     px::AbsMax m;
@@ -403,11 +427,16 @@ __global__ void __launch_bounds__(32 * kWarps) swiglu_wr(
 // --- host side ---------------------------------------------------------------------------
 
 // Team size and chunks per lane for a row of n bf16: n % 256 == 0 and at most
-// 16 chunks (8 KB of shared memory per row buffer) per warp; false -> the
-// caller uses another kernel.
-static inline bool pick(int64_t n, int* R, int* cpl) {
+// 16 chunks (8 KB of shared memory per row buffer) per warp; `three` asks for
+// teams of three warps where they fit; false -> the caller uses another kernel.
+static inline bool pick(int64_t n, bool three, int* R, int* cpl) {
   if (n <= 0 || n % 256) return false;
   const int64_t t = n / 256;
+  if (three && t % 3 == 0 && t / 3 <= 16) {
+    *R = 3;
+    *cpl = (int)(t / 3);
+    return true;
+  }
   for (int r = 1; r <= 4; r *= 2) {
     if (t % r == 0 && t / r <= 16) {
       *R = r;
@@ -418,19 +447,20 @@ static inline bool pick(int64_t n, int* R, int* cpl) {
   return false;
 }
 
-// dynamic shared memory of a CTA: kWarps slices of nbuf row buffers of cpl * 32 chunks
-static inline size_t smem_for(int cpl, int nbuf) { return (size_t)kWarps * nbuf * cpl * 32 * 16; }
+// dynamic shared memory of a CTA: warps_of(R) slices of nbuf row buffers of cpl * 32 chunks
+static inline size_t smem_for(int R, int cpl, int nbuf) { return (size_t)warps_of(R) * nbuf * cpl * 32 * 16; }
 
 template <class K>
 static int grid_for(K kernel, int R, int cpl, int nbuf, int64_t rows) {
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32 * kWarps, smem_for(cpl, nbuf)) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32 * warps_of(R), smem_for(R, cpl, nbuf)) !=
           cudaSuccess ||
       per_sm < 1) {
     cudaGetLastError();
     per_sm = 1;
   }
-  const int64_t need = (rows + (kWarps / R) - 1) / (kWarps / R);
+  const int64_t per_cta = warps_of(R) / R;
+  const int64_t need = (rows + per_cta - 1) / per_cta;
   const int64_t g = (int64_t)per_sm * pipe::num_sms();
   return (int)(need < g ? need : g);
 }
@@ -440,13 +470,19 @@ static void set_smem(K kernel, size_t bytes) {
   if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-// Calls f(integral_constant<R>, cpl) for the team size picked for n; false when
-// n has no warp-row shape.
-template <class F>
+// Calls f(integral_constant<R>, cpl) for the team size picked for n (THREE:
+// teams of three warps where they fit); false when n has no warp-row shape.
+template <bool THREE = false, class F>
 static bool dispatch(int64_t n, F&& f) {
   int R, cpl;
-  if (!pick(n, &R, &cpl)) return false;
+  if (!pick(n, THREE, &R, &cpl)) return false;
   using std::integral_constant;
+  if constexpr (THREE) {
+    if (R == 3) {
+      f(integral_constant<int, 3>{}, cpl);
+      return true;
+    }
+  }
   if (R == 1) f(integral_constant<int, 1>{}, cpl);
   else if (R == 2) f(integral_constant<int, 2>{}, cpl);
   else f(integral_constant<int, 4>{}, cpl);
