@@ -43,7 +43,8 @@ INT8_DATASHEET_TOPS = 4500.0  # B200 dense INT8, datasheet (the measured peaks h
 HBM_FALLBACK_GBS = 6650.0  # STREAM-style copy measured earlier on this hardware, used without MEASURED_PEAKS.json
 # DRAM bytes (read + write) per launch of each GEMM entry point at the step shapes, from
 # one ncu capture (profiles/gemm_w8a8_epilogues_9216rows.md)
-NCU_TRAFFIC = {"zib_gemm_w8a8_swiglu_had": 290857216, "zib_gemm_w8a8_qk_norm_rope": 287255040}
+NCU_TRAFFIC = {"zib_gemm_w8a8_swiglu_had": 290857216, "zib_gemm_w8a8_swiglu_had_w13": 290541312,
+               "zib_gemm_w8a8_qk_norm_rope": 287255040}
 NCU_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/gemm_w8a8_epilogues_9216rows.md"
 WORKLOAD = ("30-layer S3-DiT step at 1024x1024 (4096 image + 512 text tokens), CFG pair B=2, "
             "all linears W8A8+Hadamard128, bf16 SDPA")

@@ -91,6 +91,7 @@ struct Params {
   const uint16_t* sx;
   const uint16_t* sw;   // per weight row (SWIGLU: w1 scales)
   const uint16_t* sw2;  // SWIGLU: w3 scales
+  int w13;              // SWIGLU: B is one [2F, K] tensor of alternating 32-row w1 / w3 blocks
   const uint16_t* bias;
   uint16_t* y;
   int64_t ldy;
@@ -655,8 +656,9 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const EpiCtx& c, 
 // weight rows.  SWIGLU tiles: twice 32 rows of w1 then the same 32 rows of w3.
 template <int EPI>
 __device__ __forceinline__ void load_b_part(uint8_t* dst, const CUtensorMap* b0, const CUtensorMap* b1, int nb,
-                                            int part, int kx, uint64_t* bar, uint32_t pair_bar, bool pair) {
-  if (EPI == EPI_SWIGLU) {
+                                            int part, int kx, uint64_t* bar, uint32_t pair_bar, bool pair,
+                                            bool w13) {
+  if (EPI == EPI_SWIGLU && !w13) {
 #pragma unroll
     for (int jj = 0; jj < 2; ++jj) {
       const int f = nb * 128 + part * 64 + jj * SW_BOX_ROWS;
@@ -842,8 +844,8 @@ __global__ void __launch_bounds__(Cfg<EPI>::THREADS, 1)
           uint8_t* st = smem + stage * S_STAGE_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], S_STAGE_BYTES);
           tma_load_2d(st, &tmap_a, &full_bar[stage], kb * BK, mb * 128);
-          load_b_part<EPI>(st + HALF_BYTES, &tmap_b, &tmap_b2, nb, 0, kb * BK, &full_bar[stage], 0, false);
-          load_b_part<EPI>(st + 2 * HALF_BYTES, &tmap_b, &tmap_b2, nb, 1, kb * BK, &full_bar[stage], 0, false);
+          load_b_part<EPI>(st + HALF_BYTES, &tmap_b, &tmap_b2, nb, 0, kb * BK, &full_bar[stage], 0, false, p.w13);
+          load_b_part<EPI>(st + 2 * HALF_BYTES, &tmap_b, &tmap_b2, nb, 1, kb * BK, &full_bar[stage], 0, false, p.w13);
           pend_mask |= 1u << stage;
           pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -985,7 +987,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
           const uint32_t fb_leader = leader ? fb : mapa_rank(fb, 0);
           uint8_t* st = smem + stage * P_STAGE_BYTES;
           tma_load_2d_pair(st, &tmap_a, fb_leader, kb * BK, mb * 256 + (int)rank * 128);
-          load_b_part<EPI>(st + HALF_BYTES, &tmap_b, &tmap_b2, nb, (int)rank, kb * BK, nullptr, fb_leader, true);
+          load_b_part<EPI>(st + HALF_BYTES, &tmap_b, &tmap_b2, nb, (int)rank, kb * BK, nullptr, fb_leader, true,
+                           p.w13);
           pend_mask |= 1u << stage;
           pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -1299,7 +1302,7 @@ template <int EPI>
 static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int64_t ldw, int64_t w_rows, Params p,
                   void* stream, const char* what, int static_splits = 0) {
   const int64_t M = p.M, K = p.K;
-  ZIB_HOST_CHECK(q && w && (EPI != EPI_SWIGLU || w2), ZIB_ERR_INVALID_ARG, "%s: null operand", what);
+  ZIB_HOST_CHECK(q && w && (EPI != EPI_SWIGLU || w2 || p.w13), ZIB_ERR_INVALID_ARG, "%s: null operand", what);
   ZIB_HOST_CHECK(M >= 0 && p.N > 0 && K > 0, ZIB_ERR_INVALID_ARG, "%s: bad shape M=%d N=%d K=%d", what, p.M, p.N,
                  p.K);
   ZIB_HOST_CHECK(K % 16 == 0 && ldq >= K && ldw >= K && ldq % 16 == 0 && ldw % 16 == 0, ZIB_ERR_ALIGNMENT,
@@ -1312,12 +1315,16 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
       return launch_skinny<EPI>(q, ldq, w, ldw, p, stream, what);
   }
   CUtensorMap ta, tb, tb2;
-  const uint32_t b_box = EPI == EPI_SWIGLU ? (uint32_t)SW_BOX_ROWS : 128u;
+  // SWIGLU with separate w1 / w3: 32-row boxes from each; with the interleaved
+  // [2F, K] tensor: one 128-row box per CTA part, as for the plain GEMM
+  const bool two_b = EPI == EPI_SWIGLU && !p.w13;
+  const uint32_t b_box = two_b ? (uint32_t)SW_BOX_ROWS : 128u;
+  const int64_t b_rows = EPI == EPI_SWIGLU && p.w13 ? 2 * w_rows : w_rows;
   int st = make_map(&ta, q, K, M, ldq, 128u);
   if (st) return st;
-  st = make_map(&tb, w, K, w_rows, ldw, b_box);
+  st = make_map(&tb, w, K, b_rows, ldw, b_box);
   if (st) return st;
-  st = make_map(&tb2, EPI == EPI_SWIGLU ? w2 : w, K, w_rows, ldw, b_box);
+  st = make_map(&tb2, two_b ? w2 : w, K, b_rows, ldw, b_box);
   if (st) return st;
 
   const int cols_per_tile = EPI == EPI_SWIGLU ? 128 : BN;  // output columns per tile
@@ -1453,6 +1460,65 @@ extern "C" int zib_gemm_w8a8_swiglu_had(const void* q, int64_t ldq, const void* 
   p.y = (uint16_t*)x_rot;
   p.ldy = ldo;
   return zib::gemm::launch<zib::gemm::EPI_SWIGLU>(q, ldq, w1, w3, ldw, F, p, stream, "gemm_w8a8_swiglu_had");
+}
+
+namespace zib {
+namespace gemm {
+
+// One [2F, K] int8 weight of alternating 32-row blocks (w1 rows 32g..32g+31,
+// then w3 rows 32g..32g+31, g = 0 .. F/32-1) from w1 and w3 [F, K] (row
+// stride ldw): each thread moves 16 bytes.
+__global__ void w13_interleave_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w3, int64_t ldw,
+                                      uint8_t* __restrict__ w13, int64_t F, int64_t K) {
+  const int64_t cpr = K / 16;  // 16-byte chunks per row
+  const int64_t total = 2 * F * cpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cpr, c = i % cpr;
+    const int64_t src_row = (r / 64) * 32 + (r % 32);
+    const uint8_t* src = (r % 64) < 32 ? w1 : w3;
+    *reinterpret_cast<uint4*>(w13 + r * K + c * 16) =
+        __ldg(reinterpret_cast<const uint4*>(src + src_row * ldw + c * 16));
+  }
+}
+
+}  // namespace gemm
+}  // namespace zib
+
+extern "C" int zib_w13_interleave(const void* w1, const void* w3, int64_t ldw, void* w13, int64_t F, int64_t K,
+                                  void* stream) {
+  ZIB_HOST_CHECK(w1 && w3 && w13, ZIB_ERR_INVALID_ARG, "w13_interleave: null operand");
+  ZIB_HOST_CHECK(F > 0 && F % 32 == 0 && K > 0 && ldw >= K, ZIB_ERR_INVALID_ARG,
+                 "w13_interleave: bad shape F=%lld K=%lld (F must be a multiple of 32)", (long long)F, (long long)K);
+  ZIB_HOST_CHECK(K % 16 == 0 && ldw % 16 == 0 && aligned16(w1) && aligned16(w3) && aligned16(w13), ZIB_ERR_ALIGNMENT,
+                 "w13_interleave: rows must be 16-byte aligned");
+  const int64_t total = 2 * F * (K / 16);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  zib::gemm::w13_interleave_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)w1, (const uint8_t*)w3, ldw, (uint8_t*)w13, F, K);
+  return zib_check_launch("w13_interleave");
+}
+
+extern "C" int zib_gemm_w8a8_swiglu_had_w13(const void* q, int64_t ldq, const void* w13, int64_t ldw,
+                                            const void* sx, const void* sw1, const void* sw3, void* x_rot,
+                                            int64_t ldo, int64_t M, int64_t F, int64_t K, void* stream) {
+  ZIB_HOST_CHECK(M < (1ll << 31) && F < (1ll << 30) && K < (1ll << 31), ZIB_ERR_TOO_LARGE,
+                 "gemm_w8a8_swiglu_had_w13: too large");
+  ZIB_HOST_CHECK(F > 0 && F % 128 == 0, ZIB_ERR_INVALID_ARG,
+                 "gemm_w8a8_swiglu_had_w13: features %lld not divisible by group_size 128", (long long)F);
+  ZIB_HOST_CHECK(sx && sw1 && sw3 && x_rot && ldo >= F, ZIB_ERR_INVALID_ARG,
+                 "gemm_w8a8_swiglu_had_w13: bad operands");
+  ZIB_HOST_CHECK(ldo % 8 == 0 && aligned16(x_rot) && aligned16(sw1) && aligned16(sw3), ZIB_ERR_ALIGNMENT,
+                 "gemm_w8a8_swiglu_had_w13: outputs/scales must be 16-byte aligned");
+  zib::gemm::Params p = zib::gemm::base_params(M, F, K);
+  p.sx = (const uint16_t*)sx;
+  p.sw = (const uint16_t*)sw1;
+  p.sw2 = (const uint16_t*)sw3;
+  p.y = (uint16_t*)x_rot;
+  p.ldy = ldo;
+  p.w13 = 1;
+  return zib::gemm::launch<zib::gemm::EPI_SWIGLU>(q, ldq, w13, nullptr, ldw, F, p, stream,
+                                                   "gemm_w8a8_swiglu_had_w13");
 }
 
 extern "C" int zib_gemm_w8a8_qk_norm_rope(const void* q, int64_t ldq, const void* wq, int64_t ldw, const void* sx,

@@ -163,6 +163,21 @@ def case_gemm_swiglu(M, F_, K):
     return run, 2 * M * 2 * F_ * K, f"{M}x(2x{F_})x{K} int8 -> SwiGLU -> rot128 bf16"
 
 
+def case_gemm_swiglu_w13(M, F_, K):
+    q, w1, w3 = _i8(M, K), _i8(F_, K, seed=1), _i8(F_, K, seed=3)
+    sx, s1, s3 = _bf16(M).abs() * 1e-2, _bf16(F_, seed=2).abs() * 1e-3, _bf16(F_, seed=4).abs() * 1e-3
+    w13 = torch.empty(2 * F_, K, dtype=torch.int8, device="cuda")
+    st = _lib.stream_of(q)
+    _lib.call("zib_w13_interleave", w1.data_ptr(), w3.data_ptr(), K, w13.data_ptr(), F_, K, st)
+    y = _empty(M, F_)
+
+    def run():
+        _lib.call("zib_gemm_w8a8_swiglu_had_w13", q.data_ptr(), K, w13.data_ptr(), K, sx.data_ptr(),
+                  s1.data_ptr(), s3.data_ptr(), y.data_ptr(), F_, M, F_, K, st)
+
+    return run, 2 * M * 2 * F_ * K, f"{M}x(2x{F_})x{K} int8 (w1/w3 interleaved) -> SwiGLU -> rot128 bf16"
+
+
 def case_gemm_qk_rope(M, K):
     N = 3 * H * HD
     q, w = _i8(M, K), _i8(N, K, seed=1)
@@ -222,6 +237,7 @@ CASES = {
     "gemm_w2": (lambda: case_gemm(M_TOK, D, F), "int8"),
     "gemm_qkv_qk_rope": (lambda: case_gemm_qk_rope(M_TOK, D), "int8"),
     "gemm_w13_swiglu_had": (lambda: case_gemm_swiglu(M_TOK, F, D), "int8"),
+    "gemm_w13_swiglu_had_w13": (lambda: case_gemm_swiglu_w13(M_TOK, F, D), "int8"),
     "sdpa_torch": (lambda: case_sdpa(), "bf16"),
 }
 

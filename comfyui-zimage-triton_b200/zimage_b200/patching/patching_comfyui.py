@@ -254,7 +254,7 @@ def _block_cache(block: nn.Module):
     if not all(getattr(n, "weight", None) is not None for n in norms):
         return None
     key = tuple((n.weight.data_ptr(), n.weight._version) for n in norms) + tuple(
-        (l._w_int8.data_ptr(), l._w_scale.data_ptr()) for l in lins)
+        (l._w_int8.data_ptr(), l._w_int8._version, l._w_scale.data_ptr()) for l in lins)
     c = block.__dict__.get("_zib_cache")
     if c is not None and c["key"] == key:
         return c
@@ -265,10 +265,24 @@ def _block_cache(block: nn.Module):
         "eps_an1": _eps(block.attention_norm1), "eps_an2": _eps(block.attention_norm2),
         "eps_fn1": _eps(block.ffn_norm1), "eps_fn2": _eps(block.ffn_norm2),
         "eps_q": _eps(attn.q_norm), "eps_k": _eps(attn.k_norm),
-        "F": F_, "key": key,
+        "F": F_, "w13": _w13_interleaved(ff.w1._w_int8, ff.w3._w_int8), "key": key,
     }
     block.__dict__["_zib_cache"] = c
     return c
+
+
+def _w13_interleaved(w1: torch.Tensor, w3: torch.Tensor) -> torch.Tensor | None:
+    """w1 and w3 as one int8 [2F, K] tensor of alternating 32-row blocks, the weight
+    layout of zib_gemm_w8a8_swiglu_had_w13 (one TMA copy per CTA and k-block instead
+    of four); None when the two weights do not share a 16-byte-aligned row layout."""
+    F_, K_ = w1.shape
+    if (w1.stride(1) != 1 or w3.stride(1) != 1 or w1.stride(0) != w3.stride(0) or K_ % 16
+            or w1.stride(0) % 16 or w1.data_ptr() % 16 or w3.data_ptr() % 16 or F_ % 32):
+        return None
+    w13 = torch.empty(2 * F_, K_, dtype=torch.int8, device=w1.device)
+    _lib.call("zib_w13_interleave", w1.data_ptr(), w3.data_ptr(), w1.stride(0), w13.data_ptr(), F_, K_,
+              _lib.stream_of(w1))
+    return w13
 
 
 # Cross-block fusion: a fused block whose successor in the same layer list is also
@@ -368,9 +382,15 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
               float(c["eps_an2"]), float(c["eps_fn1"]), 1, stream)
     # w1 and w3 GEMMs + SwiGLU + w2-input rotation in one launch, then quantise   (swiglu.py:51-58)
     x_rot = torch.empty(M, F_, dtype=bf, device=dev)
-    _timed_call("zib_gemm_w8a8_swiglu_had", 2 * M * 2 * F_ * D, q8f.data_ptr(), D, ff.w1._w_int8.data_ptr(),
-                ff.w3._w_int8.data_ptr(), D, sxf.data_ptr(), ff.w1._w_scale.data_ptr(), ff.w3._w_scale.data_ptr(),
-                x_rot.data_ptr(), F_, M, F_, D, stream)
+    w13 = c.get("w13")
+    if w13 is not None:
+        _timed_call("zib_gemm_w8a8_swiglu_had_w13", 2 * M * 2 * F_ * D, q8f.data_ptr(), D, w13.data_ptr(),
+                    w13.stride(0), sxf.data_ptr(), ff.w1._w_scale.data_ptr(), ff.w3._w_scale.data_ptr(),
+                    x_rot.data_ptr(), F_, M, F_, D, stream)
+    else:
+        _timed_call("zib_gemm_w8a8_swiglu_had", 2 * M * 2 * F_ * D, q8f.data_ptr(), D, ff.w1._w_int8.data_ptr(),
+                    ff.w3._w_int8.data_ptr(), D, sxf.data_ptr(), ff.w1._w_scale.data_ptr(),
+                    ff.w3._w_scale.data_ptr(), x_rot.data_ptr(), F_, M, F_, D, stream)
     q8h = torch.empty(M, F_, dtype=i8, device=dev)
     sxh = torch.empty(M, dtype=bf, device=dev)
     _lib.call("zib_act_quant", x_rot.data_ptr(), F_, q8h.data_ptr(), F_, sxh.data_ptr(), None, M, F_, 0, stream)

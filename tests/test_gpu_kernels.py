@@ -279,6 +279,31 @@ def test_gemm_swiglu_matches_composed_kernels(cuda):
     assert torch.equal(q_f, q_ref) and torch.equal(s_f, s_ref)
 
 
+@pytest.mark.parametrize("M,F,K", [(48, 128, 384), (129, 384, 256), (1100, 1280, 3840), (2300, 10240, 3840)])
+def test_gemm_swiglu_interleaved_weights_bitexact(cuda, gemm_variant, M, F, K):
+    """The interleaved-[w1|w3] form equals the two-weight form bit for bit (same tiles, same epilogue)."""
+    q, sx, _ = ops.act_quant_had128(seeded_x(M, K, seed=41))
+    w1q, sw1, _ = ops.weight_prep(seeded_w(F, K, seed=42))
+    w3q, sw3, _ = ops.weight_prep(seeded_w(F, K, seed=43))
+    qd, w1d, w3d, sxd, s1d, s3d = (t.cuda() for t in (q, w1q, w3q, sx.flatten(), sw1, sw3))
+    st = _lib.stream_of(qd)
+    w13 = torch.empty(2 * F, K, dtype=torch.int8, device="cuda")
+    _lib.call("zib_w13_interleave", w1d.data_ptr(), w3d.data_ptr(), K, w13.data_ptr(), F, K, st)
+    want_w13 = torch.stack([w1q.reshape(F // 32, 32, K), w3q.reshape(F // 32, 32, K)], dim=1).reshape(2 * F, K)
+    ref = torch.empty(M, F, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_gemm_w8a8_swiglu_had", qd.data_ptr(), K, w1d.data_ptr(), w3d.data_ptr(), K, sxd.data_ptr(),
+              s1d.data_ptr(), s3d.data_ptr(), ref.data_ptr(), F, M, F, K, st)
+    got = torch.empty(M, F, dtype=torch.bfloat16, device="cuda")
+    for _ in range(2):
+        got.fill_(0)
+        _lib.call("zib_gemm_w8a8_swiglu_had_w13", qd.data_ptr(), K, w13.data_ptr(), K, sxd.data_ptr(),
+                  s1d.data_ptr(), s3d.data_ptr(), got.data_ptr(), F, M, F, K, st)
+        torch.cuda.synchronize()
+        assert _lib.device_error_read_clear() == 0
+        assert torch.equal(w13.cpu(), want_w13)
+        assert torch.equal(got, ref)
+
+
 def test_gemm_swiglu_rejects_ragged_features(cuda):
     q = torch.zeros(8, 128, dtype=torch.int8, device="cuda")
     w = torch.zeros(200, 128, dtype=torch.int8, device="cuda")
