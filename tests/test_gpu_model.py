@@ -112,11 +112,35 @@ def test_block_fused_equals_composed_and_matches_oracle(cuda):
         finally:
             pc.ENABLE_FUSED_BLOCK = True
     assert "_zib_cache" in m.layers[0].__dict__
+    assert m.layers[0].__dict__["_zib_cache"]["w13"] is not None  # interleaved [w1|w3] FFN weight in use
     assert torch.equal(y_fused, y_comp)
     # oracle with its own weight prep and fp32 attention: within the attention-numerics band
     p = omodel.prep_layer(params[0], quant_adaln=True)
     want = omodel.block_forward(p, x, fc, t, n_heads=heads)
     assert rel_l2(y_fused.cpu(), want) <= 1.5e-2
+
+
+def test_fused_block_follows_in_place_weight_updates(cuda):
+    """The fused path's interleaved [w1|w3] copy is rebuilt when w1 or w3 change in place."""
+    from zimage_b200.patching import patching_comfyui as pc
+
+    dim, heads, ffn = 1024, 8, 2816
+    m, _ = _small_model(1, dim, heads, ffn, seed=9)
+    _patch(m)
+    x, t, fm, _ = _inputs(2, 8, 8, 16, dim, seed=6)
+    ff = m.layers[0].feed_forward
+    with torch.no_grad():
+        y0 = m(x.cuda(), t.cuda(), fm.cuda())
+        ff.w1._w_int8[:64].neg_()
+        ff.w3._w_int8[-32:].zero_()
+        y_fused = m(x.cuda(), t.cuda(), fm.cuda())
+        pc.ENABLE_FUSED_BLOCK = False
+        try:
+            y_comp = m(x.cuda(), t.cuda(), fm.cuda())
+        finally:
+            pc.ENABLE_FUSED_BLOCK = True
+    assert not torch.equal(y_fused, y0)
+    assert torch.equal(y_fused, y_comp)
 
 
 def _record_attention():
