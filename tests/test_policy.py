@@ -101,3 +101,16 @@ def test_registration_names():
     spec.loader.exec_module(mod)
     assert list(mod.NODE_CLASS_MAPPINGS) == ["ZImageTritonApply"]
     assert mod.NODE_DISPLAY_NAME_MAPPINGS == {"ZImageTritonApply": "ZImage Triton Accelerate"}
+
+
+def test_interleaved_ffn_weight_needs_a_shared_aligned_row_layout():
+    """The fused block path keeps the two-weight SwiGLU GEMM when w1 and w3 cannot be
+    interleaved in 32-row blocks (checked on the host, before any device call)."""
+    from zimage_b200.patching.patching_comfyui import _w13_interleaved
+
+    w = torch.zeros(96, 128, dtype=torch.int8)
+    assert _w13_interleaved(w[:48], w[48:]) is None                        # F not a multiple of 32
+    assert _w13_interleaved(w[:, :120], w[:, 8:]) is None                  # K not a multiple of 16
+    wide = torch.zeros(64, 160, dtype=torch.int8)
+    assert _w13_interleaved(w[:64], wide[:, :128]) is None                 # different row strides
+    assert _w13_interleaved(w[:32, ::2].contiguous(), w[:32].t()[:64, :32].t()) is None  # column-strided
