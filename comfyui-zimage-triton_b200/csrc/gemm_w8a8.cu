@@ -630,13 +630,13 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      // bf16(bf16(x * rstd) * w), then the pair rotation, each rounded to bf16 (the
-      // rotation's products and sums stay scalar: packed, they may be contracted)
+      // bf16(bf16(x * rstd) * w), then the pair rotation fma(a, c, -(b s)),
+      // fma(b, c, a s) as the reference's compiler contracts it (fused_qknorm_rope.py:140-141);
+      // scalar intrinsics, so that no other contraction can change a rounding
       const uint32_t n2 = px::to_bf16x2(px::mul(px::from_bf16x2(xw[k]), RS));
       const uint32_t m2 = px::to_bf16x2(px::mul(px::from_bf16x2(n2), W[k]));
       const float a = lo_f32(m2), b = hi_f32(m2);
-      o[k] = cvt_bf16x2(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(b, sv[k])),
-                        __fadd_rn(__fmul_rn(b, cv[k]), __fmul_rn(a, sv[k])));
+      o[k] = cvt_bf16x2(__fmaf_rn(a, cv[k], -__fmul_rn(b, sv[k])), __fmaf_rn(b, cv[k], __fmul_rn(a, sv[k])));
     }
     if (grow < p.M)
       *reinterpret_cast<uint4*>(p.y + (int64_t)grow * p.ldy + (nb * 2 + hh) * 128 + sub * 8) =
@@ -1612,8 +1612,10 @@ void zib_gemm_split_reset() {
     zib::gemm::StaticScratch& sc = zib::gemm::g_static_scratch[d];
     if (!w.ctr && !sc.ctr) continue;
     cudaSetDevice(d);
+    cudaDeviceSynchronize();  // no GEMM of this device is still counting on any stream
     if (w.ctr) cudaMemset(w.ctr, 0, (size_t)w.tails * 2 * sizeof(int));
     if (sc.ctr) cudaMemset(sc.ctr, 0, sizeof(zib::gemm::g_static_split_ctr));
+    cudaDeviceSynchronize();
   }
   cudaSetDevice(dev);
   cudaGetLastError();

@@ -134,13 +134,16 @@ __device__ __forceinline__ f2 exp_pair(f2 x) {
 }
 
 // bf16(g * sigmoid(g)) of the bf16 pair g2 (swiglu.py:51-55), sigmoid = the
-// correctly rounded reciprocal of 1 + exp(-g)
+// correctly rounded reciprocal of 1 + exp(-g), 0 where exp(-g) overflows fp32
 __device__ __forceinline__ uint32_t silu_bf16x2(uint32_t g2) {
   const f2 g = from_bf16x2(g2);
   const f2 e = exp_pair(mul(g, mk(-1.0f, -1.0f)));
-  float d0, d1;
+  float d0, d1, g0, g1;
   split(add(mk(1.0f, 1.0f), e), d0, d1);
-  return to_bf16x2(mul(g, mk(__frcp_rn(d0), __frcp_rn(d1))));
+  split(g, g0, g1);
+  const float s0 = -g0 > kExpOverflow ? 0.0f : __frcp_rn(d0);
+  const float s1 = -g1 > kExpOverflow ? 0.0f : __frcp_rn(d1);
+  return to_bf16x2(mul(g, mk(s0, s1)));
 }
 
 // (a + b, a - b) for the bf16 pair w = (a low, b high), each rounded once to fp32

@@ -233,8 +233,7 @@ __global__ void __launch_bounds__(1024) norm_gate_residual_kernel(
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         float xs = bf16_round(__fmul_rn(bf16_round(__fmul_rn(v[i][j], rstd)), wv[j]));
-        float t = bf16_round(__fmul_rn(gv[j], xs));
-        v[i][j] = bf16_round(__fadd_rn(rv[j], t));
+        v[i][j] = bf16_fma(gv[j], xs, rv[j]);  // RN_bf16(r + g * xs), one rounding
         if (FUSE) ss2 += (double)(v[i][j] * v[i][j]);
       }
       st_chunk<VEC>(y + row * ldy, c, n, v[i]);
@@ -360,10 +359,10 @@ __global__ void __launch_bounds__(256, 3) qknorm_rope_kernel(
     const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
     uint32_t o[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {  // pair rotation: products and sums scalar, each rounded once
+    for (int k = 0; k < 4; ++k) {  // pair rotation: fma(a, c, -(b s)), fma(b, c, a s)
       const float a = __uint_as_float(wv[k] << 16), bb = __uint_as_float(wv[k] & 0xFFFF0000u);
-      o[k] = px::to_bf16x2(px::mk(__fsub_rn(__fmul_rn(a, cv[k]), __fmul_rn(bb, sv[k])),
-                                  __fadd_rn(__fmul_rn(bb, cv[k]), __fmul_rn(a, sv[k]))));
+      o[k] = px::to_bf16x2(px::mk(__fmaf_rn(a, cv[k], -__fmul_rn(bb, sv[k])),
+                                  __fmaf_rn(bb, cv[k], __fmul_rn(a, sv[k]))));
     }
     if (ok[r]) *reinterpret_cast<uint4*>(out + oo[r]) = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -900,12 +899,8 @@ __global__ void __launch_bounds__(128) ngr_pipe(
         a0 = __fmul_rn(a0, wv[j]);
         a1 = __fmul_rn(a1, wv[j + 1]);
         bf16_round2(a0, a1);
-        a0 = __fmul_rn(gv[j], a0);
-        a1 = __fmul_rn(gv[j + 1], a1);
-        bf16_round2(a0, a1);
-        a0 = __fadd_rn(rv[j], a0);
-        a1 = __fadd_rn(rv[j + 1], a1);
-        bf16_round2(a0, a1);
+        a0 = bf16_fma(gv[j], a0, rv[j]);  // RN_bf16(r + g * xs), one rounding
+        a1 = bf16_fma(gv[j + 1], a1, rv[j + 1]);
         v[j] = a0;
         v[j + 1] = a1;
         if (FUSE) ss2 += (double)(a0 * a0) + (double)(a1 * a1);

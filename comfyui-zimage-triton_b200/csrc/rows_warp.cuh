@@ -49,6 +49,12 @@ __device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
   asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
+// RN_bf16(a * b + c) per lane, one rounding
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
 __device__ __forceinline__ void unpack8(const uint4& d, float v[8]) {
   v[0] = lo_f(d.x); v[1] = hi_f(d.x); v[2] = lo_f(d.y); v[3] = hi_f(d.y);
   v[4] = lo_f(d.z); v[5] = hi_f(d.z); v[6] = lo_f(d.w); v[7] = hi_f(d.w);
@@ -353,9 +359,10 @@ __global__ void __launch_bounds__(32 * warps_of(R)) ngr_wr(
       const uint4 e = STAGE ? se[32 * k] : __ldcs(reinterpret_cast<const uint4*>(rr + 256 * k));
       const uint4 a = px::norm_w(sl[32 * k], rstd, wl + 256 * k);
       const uint4 g = ld_nc(gl + 256 * k);
-      // bf16(r + bf16(g * a)), fused_norm_residual.py:69-73
-      const uint4 v = make_uint4(hadd2(e.x, hmul2(g.x, a.x)), hadd2(e.y, hmul2(g.y, a.y)),
-                                 hadd2(e.z, hmul2(g.z, a.z)), hadd2(e.w, hmul2(g.w, a.w)));
+      // RN_bf16(r + g * a), one rounding: the reference's compiler contracts the bf16
+      // multiply-add of fused_norm_residual.py:72 into a fused multiply-add
+      const uint4 v = make_uint4(hfma2(g.x, a.x, e.x), hfma2(g.y, a.y, e.y),
+                                 hfma2(g.z, a.z, e.z), hfma2(g.w, a.w, e.w));
       *reinterpret_cast<uint4*>(yr + 256 * k) = v;
       if (FUSE) {
         sl[32 * k] = v;

@@ -46,6 +46,10 @@ void zib_gemm_split_reset();
 int zib_err_read_clear_rows();
 
 extern "C" int zib_device_error_read_clear(void) {
+  // every stream of the device, non-blocking ones included, has finished before the
+  // word is read (and before any counter is re-zeroed below)
+  cudaDeviceSynchronize();
+  cudaGetLastError();
   int a = zib_err_read_clear_gemm();
   int b = zib_err_read_clear_rows();
   if (a) zib_gemm_split_reset();  // a stopped GEMM may have left split-K counters mid-count

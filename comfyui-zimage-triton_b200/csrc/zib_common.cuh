@@ -34,6 +34,18 @@ __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// RN_bf16(a * b + c) with one rounding (fma.rn.bf16) of bf16-representable a, b, c:
+// the bf16 multiply-add that the reference's Triton kernels contract
+// (fused_norm_residual.py:69-73)
+__device__ __forceinline__ float bf16_fma(float a, float b, float c) {
+  const unsigned short ha = (unsigned short)(__float_as_uint(a) >> 16);
+  const unsigned short hb = (unsigned short)(__float_as_uint(b) >> 16);
+  const unsigned short hc = (unsigned short)(__float_as_uint(c) >> 16);
+  unsigned short hd;
+  asm("fma.rn.bf16 %0, %1, %2, %3;" : "=h"(hd) : "h"(ha), "h"(hb), "h"(hc));
+  return __uint_as_float((uint32_t)hd << 16);
+}
+
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
   return __uint_as_float(((uint32_t)b) << 16);
 }
@@ -117,9 +129,14 @@ __device__ __forceinline__ float zib_expf(float x) {
   return __uint_as_float(__float_as_uint(p) + ((uint32_t)ki << 23));
 }
 
-// sigmoid(g) = 1 / (1 + exp(-g)), the correctly rounded reciprocal
+// exp(x) overflows fp32 for x above this (ln of the largest finite fp32, rounded down)
+constexpr float kExpOverflow = 88.72283935546875f;
+
+// sigmoid(g) = 1 / (1 + exp(-g)), the correctly rounded reciprocal; exactly 0 where
+// exp(-g) overflows to inf in fp32 (the reference's fp32 sigmoid, swiglu.py:55)
 __device__ __forceinline__ float zib_sigmoidf(float g) {
-  return __frcp_rn(__fadd_rn(1.0f, zib_expf(-g)));
+  const float s = __frcp_rn(__fadd_rn(1.0f, zib_expf(-g)));
+  return -g > kExpOverflow ? 0.0f : s;
 }
 
 // tanh: odd Taylor polynomial (to x^11) for |x| < 0.25, else (1 - e^-2|x|) / (1 + e^-2|x|)

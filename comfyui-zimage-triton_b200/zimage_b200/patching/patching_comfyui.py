@@ -106,25 +106,31 @@ def _convert_rope_matrix_to_complex(freqs_cis: torch.Tensor) -> torch.Tensor:
 
 
 _TABLE_CACHE: dict = {}
+_TABLE_CACHE_SIZE = 8
 
 
 def _cos_sin(freqs_cis: torch.Tensor, batch: int):
     """(cos, sin, batch_stride) fp32 tables from the 2x2-matrix or complex64 form.
 
-    The 30 blocks of one step receive the same ``freqs_cis``; the conversion is
-    cached on (pointer, shape, version) so it runs once per step.
+    The blocks of one step receive the same few ``freqs_cis`` tensors (the joint
+    sequence, and the image and caption parts for the refiners); each conversion is
+    cached on (pointer, shape, version), keeping the last few, so it runs once per step.
+    The cached value holds the tensor it was built from, so its memory cannot be
+    reused by another tensor with the same key while the entry lives.
     """
-    key = (freqs_cis.data_ptr(), tuple(freqs_cis.shape), freqs_cis._version, freqs_cis.dtype, batch)
-    hit = _TABLE_CACHE.get("k")
-    if hit == key:
-        return _TABLE_CACHE["v"]
+    key = (freqs_cis.data_ptr(), tuple(freqs_cis.shape), freqs_cis._version, freqs_cis.dtype, batch,
+           freqs_cis.device)
+    hit = _TABLE_CACHE.get(key)
+    if hit is not None:
+        return hit[0]
     if freqs_cis.is_complex():
         fc = freqs_cis
     else:
         fc = _convert_rope_matrix_to_complex(freqs_cis)
     val = rope_tables(fc, batch)
-    _TABLE_CACHE["k"] = key
-    _TABLE_CACHE["v"] = val
+    if len(_TABLE_CACHE) >= _TABLE_CACHE_SIZE:
+        _TABLE_CACHE.pop(next(iter(_TABLE_CACHE)))
+    _TABLE_CACHE[key] = (val, freqs_cis)
     return val
 
 

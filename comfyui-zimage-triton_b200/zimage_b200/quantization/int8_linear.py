@@ -28,7 +28,6 @@ import types
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from .. import _lib
 
@@ -139,17 +138,6 @@ def _make_w8a8_forward(module: nn.Linear, hadamard: bool):
     return types.MethodType(_forward, module)
 
 
-def _make_w8a16_forward(module: nn.Linear):
-    """Weight-only INT8 (int8_linear.py:143-151); not selected by the node, plain torch ops."""
-    bias = module.bias
-
-    def _forward(self, x: torch.Tensor) -> torch.Tensor:
-        w_deq = self._w_int8.to(x.dtype) * self._w_scale.unsqueeze(1).to(x.dtype)
-        return F.linear(x, w_deq, bias)
-
-    return types.MethodType(_forward, module)
-
-
 def _int8_state_dict_hook(module, state_dict, prefix, local_metadata) -> None:
     """Hide the CPU weight from state_dict (int8_linear.py:154-170)."""
     key = prefix + "weight"
@@ -176,16 +164,46 @@ def _int8_apply(self, fn, recurse=True):
 
 
 _VALID_MODES = ("w8a8", "w8a8_hadamard", "w8a16")
+_B200_MODES = ("w8a8", "w8a8_hadamard")
+
+# Layer-selection policies:
+#   "reference"   - the reference's (int8_linear.py:44-56): sensitive names, layers.0 and the
+#                   last two blocks stay in the source dtype;
+#   "all_linears" - every nn.Linear with in/out >= min_dim;
+#   "main_layers" - every nn.Linear of the main block list ``layers.N.`` (adaLN included, first
+#                   and last blocks included); embedders, refiners and the final layer stay in
+#                   the source dtype as the reference keeps them.
+_POLICIES = ("reference", "all_linears", "main_layers")
+_MAIN_LAYER_RE = re.compile(r"^(?:.*\.)?layers\.\d+\.")
+
+
+def _policy_skips(policy: str, name: str, n_blocks: int) -> bool:
+    if policy == "reference":
+        return _is_sensitive_layer(name, n_blocks)
+    if policy == "main_layers":
+        return _MAIN_LAYER_RE.match(name) is None
+    return False
 
 
 def select_layers(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
-                  skip_sensitive: bool = True):
+                  skip_sensitive: bool = True, policy: str | None = None):
     """Layer-selection policy of apply_int8_quantization (int8_linear.py:242-271), no side effects.
 
+    ``policy`` (one of "reference", "all_linears", "main_layers") overrides
+    ``skip_sensitive`` (True = "reference", False = "all_linears").
     Returns ([(name, module, use_hadamard), ...], stats).
     """
     if mode not in _VALID_MODES:
         raise ValueError(f"Unknown mode: {mode!r}. Use one of {_VALID_MODES}")
+    if mode not in _B200_MODES:
+        # the reference's weight-only mode (int8_linear.py:143-151) dequantises the whole weight
+        # and calls F.linear in eager torch on every forward; the node never selects it
+        raise ValueError(f"mode {mode!r} (weight-only INT8 through a dequantised bf16 F.linear) is not "
+                         f"provided on the sm_100a path; use one of {_B200_MODES}")
+    if policy is None:
+        policy = "reference" if skip_sensitive else "all_linears"
+    if policy not in _POLICIES:
+        raise ValueError(f"Unknown policy: {policy!r}. Use one of {_POLICIES}")
     use_hadamard = mode == "w8a8_hadamard"
     n_blocks = _count_blocks(model)
     stats = {"quantized": 0, "skipped": 0, "sensitive": 0, "had_skipped": 0}
@@ -197,10 +215,10 @@ def select_layers(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
         if in_f < min_dim or out_f < min_dim:
             stats["skipped"] += 1
             continue
-        if skip_sensitive and _is_sensitive_layer(name, n_blocks):
+        if _policy_skips(policy, name, n_blocks):
             stats["sensitive"] += 1
             continue
-        if mode != "w8a16" and in_f % 16 != 0:
+        if in_f % 16 != 0:
             # the tcgen05 GEMM streams K in 16-byte TMA rows
             stats["skipped"] += 1
             logger.debug("INT8 skip %s: in=%d not a multiple of 16", name, in_f)
@@ -215,14 +233,15 @@ def select_layers(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
 
 
 def apply_int8_quantization(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
-                            skip_sensitive: bool = True) -> dict[str, int]:
+                            skip_sensitive: bool = True, policy: str | None = None) -> dict[str, int]:
     """Quantise qualifying nn.Linear layers in place (int8_linear.py:209-321).
 
     ``skip_sensitive=False`` quantises every linear with in/out >= ``min_dim``
-    (the all-linears policy); the default reproduces the reference policy.
+    (the all-linears policy); the default reproduces the reference policy;
+    ``policy`` selects one of "reference", "all_linears", "main_layers" by name.
     Returns {"quantized", "skipped", "sensitive", "had_skipped"}.
     """
-    plan, stats = select_layers(model, min_dim, mode, skip_sensitive)
+    plan, stats = select_layers(model, min_dim, mode, skip_sensitive, policy)
     for name, module, had in plan:
         in_f, out_f = module.in_features, module.out_features
         w_int8, w_scale = quantize_weight(module.weight.data, had)
@@ -231,11 +250,7 @@ def apply_int8_quantization(model: nn.Module, min_dim: int = _MIN_DIM, mode: str
         module.register_buffer("_w_scale", w_scale.to(device=target, dtype=module.weight.dtype))
         module.weight.data = module.weight.data.to(device="cpu")
 
-        if mode == "w8a16":
-            fwd = _make_w8a16_forward(module)
-        else:
-            fwd = _make_w8a8_forward(module, had)
-        module.forward = fwd
+        module.forward = _make_w8a8_forward(module, had)
         module._int8_quantized = True
         module._int8_use_hadamard = had
         module._int8_layer_name = name

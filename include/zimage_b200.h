@@ -51,8 +51,10 @@ ZIB_API const char* zib_last_error(void);
 /* 0 if device `dev` is an sm_100 part this library can run on, else a zib_status. */
 ZIB_API int zib_device_check(int dev);
 /* Reads and clears the device-side error word of the current device (set by a
- * kernel whose bounded wait expired: ZIB_ERR_TIMEOUT).  Synchronising; not for
- * the hot path.  Returns 0 when no kernel reported an error. */
+ * kernel whose bounded wait expired: ZIB_ERR_TIMEOUT).  Synchronises the current
+ * device first (every stream, non-blocking ones included) and, after a GEMM
+ * error, each device whose split-K counters it re-zeroes; not for the hot path
+ * nor inside a stream capture.  Returns 0 when no kernel reported an error. */
 ZIB_API int zib_device_error_read_clear(void);
 /* Launches one thread that waits on a barrier nothing arrives at: the bounded
  * wait of the GEMM and row kernels expires (2 s), the device error word reads
@@ -175,9 +177,10 @@ ZIB_API int zib_gemm_set_split_workspace(int device, void* ws, int64_t ws_bytes,
  * and cudaFree synchronise the device).  Its split-K tail uses a static device
  * scratch area instead of a workspace that the caller would have to allocate
  * and register (zib_gemm_set_split_workspace); the call allocates and frees
- * nothing.  `splits` (1-4) is the number of
- * K-slices each tile of a short last wave runs as (2-CTA tiles, M > 128;
- * 1 = no split; launches without a short last wave run unsplit).  Limit: the
+ * nothing.  `splits` (1-4, and at most ceil(K / 128), the number of 128-wide
+ * K-blocks) is the number of K-slices each tile of a short last wave runs as
+ * (2-CTA tiles, M > 128; 1 = no split; launches without a short last wave run
+ * unsplit); more splits than K-blocks returns ZIB_ERR_INVALID_ARG.  Limit: the
  * scratch holds 64 units of 256 KB (16 MB of device memory on every GPU that
  * loads this library, held until the process exits) and 128 arrival counters;
  * a call whose last wave needs more (its tiles x splits > 64) returns

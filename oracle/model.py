@@ -104,6 +104,38 @@ def block_forward(p: dict, x: torch.Tensor, freqs_cis: torch.Tensor, adaln_input
     return x
 
 
+def block_forward_rows(p: dict, x: torch.Tensor, bidx: torch.Tensor, sidx: torch.Tensor,
+                       freqs_cis: torch.Tensor, adaln_input: torch.Tensor, attn, eps: float = 1e-5,
+                       qk_eps: float = 1e-5, n_heads=N_HEADS, head_dim=HEAD_DIM) -> torch.Tensor:
+    """``block_forward`` on a subset of token rows (patching_comfyui.py:340-415).
+
+    Every op of the block except attention works row by row, so a row subset is
+    exact given the attention output of those rows.  x [R, D] bf16 are the rows;
+    bidx / sidx [R] their batch index (adaLN row) and sequence position (RoPE
+    row); ``attn(q, k, v)`` takes the rows' [R, H, d] Q, K, V and returns their
+    [R, H*d] attention output.
+    """
+    R, D = x.shape
+    raw = linear(p, "adaln_w", adaln_input, p["adaln_b"])
+    s_msa, g_msa, s_mlp, g_mlp = ops.adaln_chunks(raw, D)
+    x3 = x.unsqueeze(1)                                                   # [R, 1, D]
+    attn_in = ops.modulate(ops.rms_norm(x3, p["attention_norm1"], eps), s_msa[bidx])
+    qkv = linear(p, "qkv", attn_in.reshape(R, D))
+    hd = n_heads * head_dim
+    fc = freqs_cis.reshape(-1, freqs_cis.shape[-2], freqs_cis.shape[-1])
+    fc = fc[bidx if fc.shape[0] > 1 else torch.zeros_like(bidx), sidx].unsqueeze(1)   # [R, 1, d/2]
+    xq = ops.fused_qknorm_rope(qkv[:, :hd].reshape(R, 1, n_heads, head_dim), p["q_norm"], fc, qk_eps)
+    xk = ops.fused_qknorm_rope(qkv[:, hd:2 * hd].reshape(R, 1, n_heads, head_dim), p["k_norm"], fc, qk_eps)
+    xv = qkv[:, 2 * hd:].reshape(R, n_heads, head_dim)
+    o = attn(xq.reshape(R, n_heads, head_dim), xk.reshape(R, n_heads, head_dim), xv)
+    attn_out = linear(p, "out", o.reshape(R, hd)).reshape(R, 1, D)
+    x3 = ops.norm_gate_residual(attn_out, x3, g_msa[bidx], p["attention_norm2"], eps)
+    ffn_in = ops.modulate(ops.rms_norm(x3, p["ffn_norm1"], eps), s_mlp[bidx]).reshape(R, D)
+    h = ops.swiglu(linear(p, "w1", ffn_in), linear(p, "w3", ffn_in))
+    ffn_out = linear(p, "w2", h).reshape(R, 1, D)
+    return ops.norm_gate_residual(ffn_out, x3, g_mlp[bidx], p["ffn_norm2"], eps).reshape(R, D)
+
+
 def step_forward(layers: list, x, freqs_cis, adaln_input, eps=1e-5, qk_eps=1e-5, **kw):
     for p in layers:
         x = block_forward(p, x, freqs_cis, adaln_input, eps, qk_eps, **kw)
