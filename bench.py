@@ -1,23 +1,36 @@
-"""Benchmark: Z-Image S3-DiT DiT step on B200 through the sm_100a W8A8 path.
+"""Benchmark: Z-Image S3-DiT sampling on B200 through the sm_100a W8A8 path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One step = one forward of the 30-layer S3-DiT block stack (dim 3840, 30 heads
-x 128, SwiGLU 10240, adaLN from a 256-d timestep embedding) over one image's
-CFG pair at 1024x1024: B=2 rows x (4096 image tokens + 512 text tokens), every
-block linear W8A8 + block-Hadamard-128 (the all-linears policy), SDPA over 4608
-tokens in bf16.  Random-init weights, seeded N(0,1) synthetic inputs (no
-checkpoints or datasets exist offline).  The weights (5.4 GB int8) are far
-larger than L2, so each step streams them from HBM; no L2 flush is needed.
+Workload (the 30-layer ~6B S3-DiT at 1024x1024, random-init weights, seeded
+synthetic inputs - no checkpoints or datasets exist offline): a batch of 16
+images, each a 16 x 128 x 128 latent (4096 image tokens after 2x2 patches)
+with 512 caption tokens of 2560-d text-encoder features, sampled by flow-
+matching Euler steps with classifier-free guidance 4.0 (Base: 30 steps, each
+image's conditional and unconditional rows in one batch) and the AuraFlow
+time shift 3.0.  Every linear of the 30 main blocks (adaLN included) is
+W8A8 + block-Hadamard-128; the embedders, refiners and final layer stay bf16 as
+the reference keeps them; attention is torch SDPA in bf16.
 
-With N GPUs (torchrun, one process per GPU, NCCL) each rank runs its own
-image (weak scaling) and the final hidden states' latent slice is gathered to
-every rank with one NCCL all_gather inside the timed region.
+One bench step = one denoising step of the whole batch: the batch is sharded
+by image across N GPUs (one process per GPU, torchrun, NCCL), each rank runs
+its images in micro-batches of two images (model batch 4 with guidance), each
+micro-batch step one CUDA-graph replay; the final latents are all-gathered
+with one NCCL collective at the end of the timed region.  Strong scaling: the
+16-image batch is fixed, per-GPU work shrinks as N grows.
 
-`value` is the whole-job time per DiT step: max-over-ranks elapsed / (K * N).
+`value` is the whole-job DiT step time per image, ms: (max-over-ranks time of K
+batch steps) / (K * 16).  `e2e` is the same through the sampler's public call
+with each step's latents and caption features copied in from pinned host memory
+and the new latents copied back, inside the timed region.  `images_per_s`
+gives the Base rate (16 images x 30 steps at the measured step time) and a
+timed full 4-step Turbo generation (no guidance, model batch 2).
+
 `--impl reference` times the CPU restatement of the reference path (the
-oracle: reference W8A8 arithmetic incl. its bf16-matmul rotation, torch._int_mm
-on CPU, CPU SDPA) on a bounded sample and extrapolates to the same unit.
+oracle: the reference's W8A8 arithmetic with its bf16-matmul rotation,
+torch._int_mm, the Triton kernels' arithmetic, CPU SDPA) on the host cores;
+each bench step is one main block over a slice of one image's CFG pair (all
+4608 keys), and `value` scales it to the same unit.
 """
 
 from __future__ import annotations
@@ -37,21 +50,25 @@ sys.path.insert(0, str(ROOT / "comfyui-zimage-triton_b200"))
 
 METRIC = "DiT step ms at 1024² (6B, W8A8); INT8 GEMM TOPS and % of peak"
 DIM, HEADS, FFN, LAYERS, ADALN = 3840, 30, 10240, 30, 256
-GRID, N_TXT, B_CFG = 64, 512, 2
+LAT_C, LAT_HW, GRID, N_TXT, CAP_DIM = 16, 128, 64, 512, 2560
 SEQ = GRID * GRID + N_TXT
+N_IMAGES, MICRO = 16, 2
+BASE_STEPS, BASE_CFG, TURBO_STEPS, SHIFT = 30, 4.0, 4, 3.0
 INT8_DATASHEET_TOPS = 4500.0  # B200 dense INT8, datasheet (the measured peaks hold bf16 and HBM only)
 HBM_FALLBACK_GBS = 6650.0  # STREAM-style copy measured earlier on this hardware, used without MEASURED_PEAKS.json
-# DRAM bytes (read + write) per launch of each GEMM entry point at the step shapes, from
-# one ncu capture (profiles/gemm_w8a8_epilogues_9216rows.md)
-NCU_TRAFFIC = {"zib_gemm_w8a8_swiglu_had": 290857216, "zib_gemm_w8a8_swiglu_had_w13": 290541312,
-               "zib_gemm_w8a8_qk_norm_rope": 287255040}
-NCU_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/gemm_w8a8_epilogues_9216rows.md"
-WORKLOAD = ("30-layer S3-DiT step at 1024x1024 (4096 image + 512 text tokens), CFG pair B=2, "
-            "all linears W8A8+Hadamard128, bf16 SDPA")
+# DRAM bytes (read + write) of one launch of the dominant GEMM, measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum) at the given row count M
+NCU_TRAFFIC = {("zib_gemm_w8a8_swiglu_had_w13", 9216): 290541312}
+WORKLOAD = (f"Z-Image 30-layer S3-DiT (dim 3840, 30 heads, FFN 10240, 2+2 refiner blocks), 1024x1024, "
+            f"{N_IMAGES}-image batch sharded by image, Base: {BASE_STEPS}-step Euler, CFG {BASE_CFG}, shift {SHIFT}, "
+            f"micro-batches of {MICRO} images; main-block linears W8A8+Hadamard128, bf16 SDPA")
+CONFIG = {"workload": WORKLOAD, "global_batch": N_IMAGES, "seq_len": SEQ, "cfg_rows_per_image": 2,
+          "l2": "no flush: 5.4 GB int8 weights streamed per micro-batch step >> 126 MB L2"}
 
 
-def _int_ops_per_step(B=B_CFG, S=SEQ):
-    M = B * S
+def _int_ops_per_image_step(S=SEQ):
+    """Int8 ops of the 30 main blocks for one image's CFG pair (2 x S token rows)."""
+    M = 2 * S
     per_block = 2 * M * (DIM * 3 * DIM + DIM * DIM + DIM * 2 * FFN + FFN * DIM)
     return per_block * LAYERS
 
@@ -113,39 +130,41 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# reference arm / CPU baseline: the oracle on host cores
+# reference arm / CPU baselines: the oracle (and the installed reference) on host cores
 # ---------------------------------------------------------------------------
 
-def cpu_sample_ms_per_step(rows: int = 64, reps: int = 3) -> tuple[float, dict]:
-    """Time one block of the reference's CPU path on `rows` of the B*S token rows and
-    extrapolate to a 30-layer step: t * (B*S/rows) * 30.
+def make_cpu_block(rows: int):
+    """A callable that runs one main block of the reference's CPU path on `rows` of one image's
+    2 x 4608 CFG token rows (attention: those queries against all 4608 keys of the image),
+    and the number of host threads it uses.  Inputs and weights are made once.
 
     Linears use the reference arithmetic (bf16-matmul Hadamard rotation, per-token
     quantisation, torch._int_mm, bf16 dequant epilogue; int8_linear.py:114-138) with
-    random int8 weights (timing does not depend on their values); row ops follow
-    the Triton kernels' restatement; attention is fp32 CPU SDPA of `rows` queries
-    against all 4608 keys per head.
+    random int8 weights (timing does not depend on their values); row ops follow the
+    Triton kernels' arithmetic; attention is fp32 CPU SDPA.
     """
     import torch
 
     sys.path.insert(0, str(ROOT))
     from oracle import ops
+    from zimage_b200.nextdit import rope_freqs_complex, zimage_positions
 
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
     R = rows
+    per_img = R // 2
 
     def rw(n, k):
         return torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8), \
             (torch.rand(n, generator=g) * 1e-3).to(torch.bfloat16)
 
     W = {"qkv": rw(3 * DIM, DIM), "out": rw(DIM, DIM), "w1": rw(FFN, DIM), "w3": rw(FFN, DIM), "w2": rw(DIM, FFN)}
-    x = torch.randn(B_CFG, R // B_CFG, DIM, generator=g).to(torch.bfloat16)
+    x = torch.randn(2, per_img, DIM, generator=g).to(torch.bfloat16)
     nw = (1 + 0.1 * torch.randn(DIM, generator=g)).to(torch.bfloat16)
     qn = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
-    mod = (0.1 * torch.randn(B_CFG, DIM, generator=g)).to(torch.bfloat16)
-    kv = torch.randn(B_CFG, HEADS, SEQ, 128, generator=g)
-    fc = ops.rope_freqs_complex(ops.zimage_positions(GRID, GRID, N_TXT))[: R // B_CFG].unsqueeze(0)
+    mod = (0.1 * torch.randn(2, DIM, generator=g)).to(torch.bfloat16)
+    kv = torch.randn(2, HEADS, SEQ, 128, generator=g)
+    fc = rope_freqs_complex(zimage_positions(GRID, GRID, N_TXT))[:per_img].unsqueeze(0)
 
     def lin(key, a):
         wq, sw = W[key]
@@ -154,54 +173,107 @@ def cpu_sample_ms_per_step(rows: int = 64, reps: int = 3) -> tuple[float, dict]:
 
     def block():
         a = ops.modulate(ops.rms_norm(x, nw), mod).reshape(R, DIM)
-        qkv = lin("qkv", a).reshape(B_CFG, R // B_CFG, 3, HEADS, 128)
+        qkv = lin("qkv", a).reshape(2, per_img, 3, HEADS, 128)
         q = ops.fused_qknorm_rope(qkv[:, :, 0], qn, fc)
         ops.fused_qknorm_rope(qkv[:, :, 1], qn, fc)
         o = torch.nn.functional.scaled_dot_product_attention(q.float().transpose(1, 2), kv, kv)
         o = o.transpose(1, 2).reshape(R, DIM).to(torch.bfloat16)
-        ao = lin("out", o).reshape(B_CFG, R // B_CFG, DIM)
+        ao = lin("out", o).reshape(2, per_img, DIM)
         x1 = ops.norm_gate_residual(ao, x, mod, nw)
         f = ops.modulate(ops.rms_norm(x1, nw), mod).reshape(R, DIM)
         h = ops.swiglu(lin("w1", f), lin("w3", f))
-        fo = lin("w2", h).reshape(B_CFG, R // B_CFG, DIM)
+        fo = lin("w2", h).reshape(2, per_img, DIM)
         return ops.norm_gate_residual(fo, x1, mod, nw)
 
-    block()
+    return block, torch.get_num_threads()
+
+
+def cpu_reference_cfg1() -> dict | None:
+    """Config 1 on the host cores through the reference's own code when it is installed next to
+    this repository (``apply_int8_quantization(..., "w8a8_hadamard")`` then ``lin(x)``,
+    int8_linear.py:209-321 and :114-138), else through the oracle's restatement of it."""
+    import torch
+    import torch.nn as nn
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    # x bf16 [1024, 3840] ~ N(0,1) with a seeded 1% of channels x20; W bf16 [11520, 3840] ~ N(0, 0.02); zero bias
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1024, DIM, generator=g)
+    x[:, torch.randperm(DIM, generator=g)[:38]] *= 20.0
+    x = x.to(torch.bfloat16)
+    w = (torch.randn(3 * DIM, DIM, generator=torch.Generator().manual_seed(1)) * 0.02).to(torch.bfloat16)
+    b = torch.zeros(3 * DIM, dtype=torch.bfloat16)
+    kind = "reference"
+    try:
+        sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+        from zimage_triton.quantization import apply_int8_quantization
+
+        holder = nn.Module()
+        holder.proj = nn.Linear(DIM, 3 * DIM, bias=True, dtype=torch.bfloat16)
+        with torch.no_grad():
+            holder.proj.weight.copy_(w)
+            holder.proj.bias.copy_(b)
+        apply_int8_quantization(holder, min_dim=0, mode="w8a8_hadamard")
+        fn = holder.proj
+    except ImportError:
+        kind = "port"
+        sys.path.insert(0, str(ROOT))
+        from oracle import ops
+
+        wq, sw, _ = ops.weight_prep(w)
+
+        def fn(a):
+            q, sx, _ = ops.act_quant_had128_matmul(a)
+            return ops.dequant_epilogue(ops.gemm_acc_i32(q, wq), sx, sw, b)
     ts = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        block()
-        ts.append(time.perf_counter() - t0)
-    t = min(ts)
-    ms_step = t * 1e3 * (B_CFG * SEQ / R) * LAYERS
-    info = {"sample": f"one block on {R} of {B_CFG * SEQ} token rows (attention: {R} queries x {SEQ} keys), "
-                      f"best of {reps}, x{B_CFG * SEQ // R} rows x{LAYERS} layers",
-            "cores": torch.get_num_threads(), "block_sample_s": round(t, 4)}
-    return ms_step, info
+    with torch.no_grad():
+        for i in range(7):
+            t0 = time.perf_counter()
+            fn(x)
+            if i >= 2:
+                ts.append(time.perf_counter() - t0)
+    ms = statistics.median(ts) * 1e3
+    ops_ = 2 * 1024 * 3 * DIM * DIM
+    return {"value": round(ms, 3), "unit": "ms", "tops": round(ops_ / (ms * 1e-3) / 1e12, 3),
+            "cores": torch.get_num_threads(), "kind": kind,
+            "sample": "W8A8+Hadamard QKV linear [1024, 3840] -> 11520, median of 5 after 2 warm-up"}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    vals = []
-    info = {}
-    for _ in range(max(1, args.warmup // 3)):
-        cpu_sample_ms_per_step(rows=64, reps=1)
+    rows = 1152  # 1/8 of one image's 2 x 4608 CFG rows, all 4608 keys: a few s of CPU work per step
+    block, cores = make_cpu_block(rows)
+    for _ in range(max(0, args.warmup)):
+        block()
+    t0 = time.perf_counter()
+    ts = []
     for _ in range(args.steps):
-        v, info = cpu_sample_ms_per_step(rows=64, reps=1)
-        vals.append(v)
-    value = statistics.median(vals)
+        t1 = time.perf_counter()
+        block()
+        ts.append(time.perf_counter() - t1)
+    wall = time.perf_counter() - t0
+    per_step_s = wall / max(1, args.steps)
+    block_s = statistics.median(ts)
+    # one image step = 30 main blocks over the full 2 x 4608 rows
+    value_ms = block_s * (2 * SEQ / rows) * LAYERS * 1e3
     n = max(1, args.gpus)
+    sample = (f"one main block over {rows} of one image's {2 * SEQ} CFG token rows (attention against all "
+              f"{SEQ} keys), scaled x{2 * SEQ // rows} rows x{LAYERS} layers; embedders, refiners and final "
+              f"layer not included")
     print(json.dumps({
-        "metric": METRIC, "impl": "reference", "value": round(value / n, 3), "unit": "ms",
-        "n_gpus": n, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "int8/bf16",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": B_CFG * n, "seq_len": SEQ,
-                                        "parallelism": f"cpu, {info.get('cores')} threads"},
-        "cpu_baseline": {"value": round(value / n, 3), "unit": "ms", "cores": info.get("cores"), "kind": "port",
-                         "sample": info.get("sample")},
-        "e2e": {"value": round(value / n, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "metric": METRIC, "impl": "reference", "value": round(value_ms / n, 3), "unit": "ms",
+        "n_gpus": n, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_s * 1e3, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int8/bf16",
+        "data": "synthetic (seeded N(0,1) latents and caption features, random-init weights)",
+        "config": dict(CONFIG, parallelism=f"dp{n} (images)"),
+        "step_definition": "one bench step = one timed CPU sample (ms_per_step is its wall time); value "
+                           "scales the sample to the GPU arm's unit",
+        "rows_factor": 2 * SEQ / rows, "layer_factor": LAYERS,
+        "cpu_baseline": {"value": round(value_ms / n, 3), "unit": "ms", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value_ms / n, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
@@ -234,17 +306,23 @@ def measure_int_mm_tops(dev) -> float | None:
 
 
 def build_model(dev, seed=0):
+    """Random-init full Z-Image DiT on `dev`, patched by the node (main-layer linears W8A8).
+
+    Returns (model, seconds to build + init, seconds of the node's apply_triton)."""
     import torch
 
     import nodes
-    from zimage_b200.nextdit import NextDiT, random_init_
+    from zimage_b200.nextdit import ZImageDiT, random_init_
 
+    t0 = time.time()
     torch.manual_seed(seed)
-    m = NextDiT(n_layers=LAYERS, dim=DIM, n_heads=HEADS, ffn_dim=FFN, adaln_dim=ADALN, device=dev)
+    m = ZImageDiT(n_layers=LAYERS, dim=DIM, n_heads=HEADS, ffn_dim=FFN, cap_feat_dim=CAP_DIM, device=dev)
     random_init_(m, seed=seed)
+    torch.cuda.synchronize()
+    t1 = time.time()
     node = nodes.ZImageTritonApply()
-    node.int8_min_dim = 0            # all-linears policy (adaLN 256->15360 included)
-    node.int8_skip_sensitive = False
+    node.int8_min_dim = 0
+    node.int8_policy = "main_layers"
 
     class _MP:
         pass
@@ -253,7 +331,39 @@ def build_model(dev, seed=0):
     mp.model = _MP()
     mp.model.diffusion_model = m
     node.apply_triton(mp, enable_int8=True)
-    return m
+    torch.cuda.synchronize()
+    return m, t1 - t0, time.time() - t1
+
+
+def image_inputs(lo: int, hi: int):
+    """Seeded per-image latents [n, 16, 128, 128] fp32 and caption features (cond, uncond) [n, 512, 2560]
+    bf16 on the CPU for images lo..hi-1 (independent of the sharding)."""
+    import torch
+
+    lat, cond, unc = [], [], []
+    for i in range(lo, hi):
+        lat.append(torch.randn(LAT_C, LAT_HW, LAT_HW, generator=torch.Generator().manual_seed(1000 + i)))
+        cond.append(torch.randn(N_TXT, CAP_DIM, generator=torch.Generator().manual_seed(2000 + i)))
+        unc.append(torch.randn(N_TXT, CAP_DIM, generator=torch.Generator().manual_seed(3000 + i)))
+    bf = torch.bfloat16
+    return torch.stack(lat), torch.stack(cond).to(bf), torch.stack(unc).to(bf)
+
+
+def config_figures(dev) -> dict:
+    """Configs 1-3 on this GPU (kernel microbenchmarks, L2 flushed before each launch)."""
+    import torch
+
+    from zimage_b200 import kernel_bench as kb
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    out = {}
+    for key, name in (("cfg1_act_quant", "act_quant_m1024"), ("cfg1_gemm", "gemm_cfg1_qkv_m1024"),
+                      ("cfg2_qknorm_rope", "qknorm_rope"), ("cfg3_ffn_block", "cfg3_ffn_block"),
+                      ("cfg3_swiglu_quant", "swiglu_quant_s4608")):
+        r = kb.run_case(name, 10, flush)
+        out[key] = {k: r[k] for k in ("shape", "ms_median", "gbs", "tops", "frac", "peak_source") if k in r}
+    del flush
+    return out
 
 
 def run_ours(args) -> None:
@@ -265,131 +375,109 @@ def run_ours(args) -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if N_IMAGES % (world * MICRO):
+        raise SystemExit(f"{N_IMAGES} images do not shard into micro-batches of {MICRO} on {world} GPUs")
     if world > 1:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    from oracle import ops as _ops  # seeded RoPE table only (positions -> cos/sin)
     from zimage_b200 import _lib
     from zimage_b200.patching import patching_comfyui as pc
+    from zimage_b200.sampler import FlowSampler
+    from zimage_b200.shard import gather_images, shard_range
 
     int_mm_tops = measure_int_mm_tops(dev) if rank == 0 else None
-    t_setup = time.time()
-    model = build_model(dev)
-    setup_s = time.time() - t_setup
+    model, init_s, apply_s = build_model(dev)
 
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    x = torch.randn(B_CFG, SEQ, DIM, generator=g, device=dev).to(torch.bfloat16)
-    t_emb = torch.randn(B_CFG, ADALN, generator=g, device=dev).to(torch.bfloat16)
-    freqs = _ops.rope_freqs_matrix(_ops.zimage_positions(GRID, GRID, N_TXT)).unsqueeze(0).to(dev)
+    lo, hi = shard_range(N_IMAGES, world, rank)
+    n_loc = hi - lo
+    lat_h, cond_h, unc_h = image_inputs(lo, hi)
+    lat0 = lat_h.to(dev)
+    caps = [torch.cat([cond_h[j:j + MICRO], unc_h[j:j + MICRO]], 0).to(dev) for j in range(0, n_loc, MICRO)]
+    n_mb = len(caps)
 
-    def step(inp):
-        with torch.no_grad():
-            return model(inp, t_emb, freqs)
+    t_cap = time.time()
+    base = FlowSampler(model, (LAT_C, LAT_HW, LAT_HW), (N_TXT, CAP_DIM), micro_batch=MICRO, cfg=BASE_CFG,
+                       steps=BASE_STEPS, shift=SHIFT, device=dev)
+    capture_s = time.time() - t_cap
+    lat = lat0.clone()
 
-    from zimage_b200.shard import gather_images
+    def batch_step(i: int) -> None:
+        """Step i of the schedule over this rank's micro-batches (one graph replay each)."""
+        for k in range(n_mb):
+            sl = slice(k * MICRO, (k + 1) * MICRO)
+            lat[sl].copy_(base.step(lat[sl], caps[k], i % BASE_STEPS))
 
-    def gather(out):
-        # this rank's image (its CFG pair) -> latent-sized slice; one NCCL all_gather of all images
-        lat = out[:, : GRID * GRID, :64].unsqueeze(0).contiguous()
-        return gather_images(lat, world)
-
-    for _ in range(args.warmup):
-        y = step(x)
-    gather(y)
-    torch.cuda.synchronize()
+    # launches of this library per micro-batch step, counted on an eager step
     launches0 = _lib.LAUNCHES
-    step(x)
-    launches_per_step = _lib.LAUNCHES - launches0  # kernel-launching calls of this library per step
+    with torch.no_grad():
+        base._step(lat[:MICRO].clone(), caps[0], base._sigmas_dev[0:2])
+    launches_per_mb = _lib.LAUNCHES - launches0
     torch.cuda.synchronize()
 
-    cap = None
-    if not args.no_graph:
-        from zimage_b200.graph import CapturedStep
-
-        # the whole step as one CUDA graph: same kernels, no per-launch host work or gaps
-        cap = CapturedStep(lambda xi, ti: model(xi, ti, freqs), x, t_emb)
-        eager_step = step
-
-        def step(inp):  # noqa: F811
-            return cap(inp, t_emb)
-
-        for _ in range(args.warmup):
-            y = step(x)
-        torch.cuda.synchronize()
+    for i in range(args.warmup):
+        batch_step(i)
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-
     clk = ClockSampler(local)
     clk.start()
     time.sleep(0.3)
-    gemm_steps = args.steps
-    if cap is None:
-        pc.GEMM_EVENTS = []
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        y = step(x)
-    gather(y)
+    for i in range(args.steps):
+        batch_step(args.warmup + i)
+    final = gather_images(lat, N_IMAGES)
     e1.record()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     elapsed = e0.elapsed_time(e1)
-    launches = launches_per_step * args.steps
     clocks = clk.stop()
-    if cap is not None:
-        # GEMM launch times for the roofline: the same kernels in eager steps right after
-        pc.GEMM_EVENTS = []
-        gemm_steps = max(1, min(args.steps, 3))
-        for _ in range(gemm_steps):
-            eager_step(x)
-        torch.cuda.synchronize()
+    if world > 1:
+        t = torch.tensor([elapsed], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+
+    # GEMM launch times for the roofline: the same kernels in eager micro-batch steps right after
+    pc.GEMM_EVENTS = []
+    gemm_steps = max(1, min(args.steps, 3))
+    xs = lat[:MICRO].clone()
+    with torch.no_grad():
+        for i in range(gemm_steps):
+            base._step(xs, caps[0], base._sigmas_dev[i:i + 2])
+    torch.cuda.synchronize()
     gem = pc.GEMM_EVENTS
     pc.GEMM_EVENTS = None
-    gemm_ms = sum(a.elapsed_time(b) for a, b, _, _ in gem)
-    gemm_ops = sum(o for _, _, o, _ in gem)
     per_kernel = {}
     for a_, b_, o_, name_ in gem:
         k = per_kernel.setdefault(name_, {"launches": 0, "ms": 0.0, "ops": 0})
         k["launches"] += 1
         k["ms"] += a_.elapsed_time(b_)
         k["ops"] += o_
+    gemm_ms = sum(v["ms"] for v in per_kernel.values())
+    gemm_ops = sum(v["ops"] for v in per_kernel.values())
     dominant = max(per_kernel, key=lambda k: per_kernel[k]["ms"]) if per_kernel else None
-    if world > 1:
-        t = torch.tensor([elapsed], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = float(t.item())
 
-    # end to end through the public call with host buffers: H2D inputs, forward, D2H output
-    xh = x.cpu().pin_memory()
-    th = t_emb.cpu().pin_memory()
-    yh = torch.empty(B_CFG, SEQ, DIM, dtype=torch.bfloat16).pin_memory()
+    # end to end through the sampler's call with host buffers: every step copies each micro-batch's
+    # latents and caption features in from pinned host memory and the new latents back out
+    lat_pin = lat.cpu().pin_memory()
+    caps_pin = [c.cpu().pin_memory() for c in caps]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    yhs = [yh] + [torch.empty_like(yh).pin_memory() for _ in range(min(args.steps, 2) - 1)]
-    torch.cuda.synchronize()
     f0.record()
-    if cap is not None:
-        # host inputs in / outputs out on a copy stream, overlapped with the graph replays
-        from zimage_b200.graph import run_steps_overlapped
-
-        run_steps_overlapped(cap, [(xh, th)] * args.steps, [yhs[i % len(yhs)] for i in range(args.steps)])
-        yd = cap.static_out
-    else:
-        for _ in range(args.steps):
-            xd = xh.to(dev, non_blocking=True)
-            td = th.to(dev, non_blocking=True)
-            with torch.no_grad():
-                yd = model(xd, td, freqs)
-            yh.copy_(yd, non_blocking=True)
-    gather(yd)
+    for i in range(args.steps):
+        for k in range(n_mb):
+            sl = slice(k * MICRO, (k + 1) * MICRO)
+            y = base.graph(lat_pin[sl], caps_pin[k], base._sigmas_dev[(i % BASE_STEPS):(i % BASE_STEPS) + 2])
+            lat_pin[sl].copy_(y, non_blocking=True)
+    gather_images(lat_pin.to(dev, non_blocking=True), N_IMAGES)
     f1.record()
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1)
@@ -397,68 +485,118 @@ def run_ours(args) -> None:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
+    h2d = N_IMAGES * (LAT_C * LAT_HW * LAT_HW * 4 + 2 * N_TXT * CAP_DIM * 2)
+    d2h = N_IMAGES * LAT_C * LAT_HW * LAT_HW * 4
+
+    # Turbo: one full 4-step generation without guidance (after one untimed generation)
+    del base
+    turbo = FlowSampler(model, (LAT_C, LAT_HW, LAT_HW), (N_TXT, CAP_DIM), micro_batch=MICRO, cfg=1.0,
+                        steps=TURBO_STEPS, shift=SHIFT, device=dev)
+    tlat = lat0.clone()
+    cond_d = cond_h.to(dev)
+    turbo.sample(tlat, cond_d)
+    tlat.copy_(lat0)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    turbo.sample(tlat, cond_d)
+    gather_images(tlat, N_IMAGES)
+    g1.record()
+    torch.cuda.synchronize()
+    turbo_ms = g0.elapsed_time(g1)
+    if world > 1:
+        t = torch.tensor([turbo_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        turbo_ms = float(t.item())
+    del turbo
     err = _lib.device_error_read_clear()
 
-    cpu = None
+    cfgs = None
+    cpu = cpu1 = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, info = cpu_sample_ms_per_step(rows=64, reps=3)
-        cpu = {"value": round(v, 3), "unit": "ms", "cores": info["cores"], "kind": "port",
-               "sample": info["sample"]}
+        cfgs = config_figures(dev)
+        cpu1 = cpu_reference_cfg1()
+        block, cores = make_cpu_block(2 * SEQ)
+        t0 = time.perf_counter()
+        block()
+        t_blk = time.perf_counter() - t0
+        del block
+        cpu = {"value": round(t_blk * LAYERS * 1e3, 3), "unit": "ms", "cores": cores, "kind": "port",
+               "sample": f"one full main block over one image's CFG pair (2 x {SEQ} token rows, full "
+                         f"attention), {t_blk:.1f} s, x{LAYERS} layers; embedders, refiners and final layer "
+                         f"not included"}
 
-    if rank == 0:
-        ms_step = elapsed / args.steps
-        dk = per_kernel.get(dominant) if dominant else None
-        achieved = dk["ops"] / (dk["ms"] * 1e-3) / 1e12 if dk and dk["ms"] > 0 else None
-        gemm_tops = gemm_ops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
-        kernels = {k: {"launches": v["launches"], "avg_launch_us": round(v["ms"] * 1e3 / v["launches"], 2),
-                       "tops": round(v["ops"] / (v["ms"] * 1e-3) / 1e12, 1),
-                       "frac": round(v["ops"] / (v["ms"] * 1e-3) / 1e12 / INT8_DATASHEET_TOPS, 4)}
-                   for k, v in per_kernel.items()}
-        peaks = _peaks()
-        rec = {
-            "metric": METRIC, "value": round(ms_step / world, 3), "unit": "ms", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "int8/bf16",
-            "data": "synthetic (seeded N(0,1) latents/text tokens, random-init weights)",
-            "config": {"workload": WORKLOAD, "global_batch": B_CFG * world, "seq_len": SEQ,
-                       "parallelism": f"dp{world} (images)",
-                       "cuda_graph": cap is not None,
-                       "l2": "no flush: 5.4 GB int8 weights streamed per step >> 126 MB L2"},
-            "roofline": {"kernel": f"{dominant} (tcgen05 kind::i8)", "bound": "tensor",
-                         "achieved": None if achieved is None else round(achieved, 1),
-                         "peak": INT8_DATASHEET_TOPS, "unit": "TOPS",
-                         "frac": None if achieved is None else round(achieved / INT8_DATASHEET_TOPS, 4),
-                         "peak_source": "B200 datasheet dense INT8 (no measured INT8 peak: "
-                                        + ("MEASURED_PEAKS.json has bf16/HBM only)" if peaks
-                                           else "MEASURED_PEAKS.json absent)"),
-                         "int_mm_measured_tops": None if int_mm_tops is None else round(int_mm_tops, 1),
-                         "frac_of_int_mm": None if (achieved is None or not int_mm_tops)
-                         else round(achieved / int_mm_tops, 4),
-                         "launches": per_kernel[dominant]["launches"] if dominant else 0,
-                         "avg_launch_us": kernels[dominant]["avg_launch_us"] if dominant else None,
-                         "traffic": NCU_TRAFFIC.get(dominant),
-                         "traffic_source": NCU_TRAFFIC_SOURCE,
-                         "all_gemms_tops": None if gemm_tops is None else round(gemm_tops, 1),
-                         "gemm_share_of_step": round((gemm_ms / gemm_steps) / max(elapsed / args.steps, 1e-9), 4),
-                         "gemm_kernels": kernels,
-                         "timing": "CUDA events around each GEMM launch" + (
-                             "" if cap is None else " in eager steps right after the graph-timed region")},
-            "e2e": {"value": round(e2e_ms / args.steps / world, 3), "unit": "ms",
-                    "h2d_bytes_per_step": xh.numel() * 2 + th.numel() * 2,
-                    "d2h_bytes_per_step": yh.numel() * 2},
-            "gpu_launches": launches,
-            "clocks": clocks,
-            "int_ops_per_step": _int_ops_per_step(),
-            "setup_s": round(setup_s, 1),
-            "device_error": err,
-            "hbm_peak_gbs": peaks.get("hbm_gbs", HBM_FALLBACK_GBS),
-            "hbm_peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-        }
-        if cpu:
-            rec["cpu_baseline"] = cpu
-        print(json.dumps(rec), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    if rank != 0:
+        return
+    batch_step_ms = elapsed / args.steps
+    ms_img_step = batch_step_ms / N_IMAGES
+    dk = per_kernel.get(dominant) if dominant else None
+    achieved = dk["ops"] / (dk["ms"] * 1e-3) / 1e12 if dk and dk["ms"] > 0 else None
+    gemm_tops = gemm_ops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    kernels = {k: {"launches": v["launches"], "avg_launch_us": round(v["ms"] * 1e3 / v["launches"], 2),
+                   "tops": round(v["ops"] / (v["ms"] * 1e-3) / 1e12, 1),
+                   "frac": round(v["ops"] / (v["ms"] * 1e-3) / 1e12 / INT8_DATASHEET_TOPS, 4)}
+               for k, v in per_kernel.items()}
+    m_launch = 2 * MICRO * SEQ
+    traffic = NCU_TRAFFIC.get((dominant, m_launch))
+    peaks = _peaks()
+    rec = {
+        "metric": METRIC, "value": round(ms_img_step, 3), "unit": "ms", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(batch_step_ms, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "int8/bf16",
+        "data": "synthetic (seeded N(0,1) latents and caption features, random-init weights)",
+        "config": dict(CONFIG, parallelism=f"dp{world} (images)", cuda_graph=True, micro_batch_images=MICRO),
+        "step_definition": f"ms_per_step = one Euler step of the whole {N_IMAGES}-image batch (max over ranks); "
+                           f"value = ms_per_step / {N_IMAGES} images",
+        "images_per_s": {"base_30step_cfg4": round(N_IMAGES / (BASE_STEPS * batch_step_ms * 1e-3), 4),
+                         "base_basis": "measured batch step time x 30 steps",
+                         "turbo_4step": round(N_IMAGES / (turbo_ms * 1e-3), 4),
+                         "turbo_generation_ms": round(turbo_ms, 2),
+                         "turbo_basis": "one timed full 4-step generation of the batch incl. the latent gather"},
+        "roofline": {"kernel": f"{dominant} (tcgen05 kind::i8)", "bound": "tensor",
+                     "achieved": None if achieved is None else round(achieved, 1),
+                     "peak": INT8_DATASHEET_TOPS, "unit": "TOPS",
+                     "frac": None if achieved is None else round(achieved / INT8_DATASHEET_TOPS, 4),
+                     "peak_source": "B200 datasheet dense INT8 (no measured INT8 peak: "
+                                    + ("MEASURED_PEAKS.json has bf16/HBM only)" if peaks
+                                       else "MEASURED_PEAKS.json absent)"),
+                     "int_mm_measured_tops": None if int_mm_tops is None else round(int_mm_tops, 1),
+                     "frac_of_int_mm": None if (achieved is None or not int_mm_tops)
+                     else round(achieved / int_mm_tops, 4),
+                     "launches": per_kernel[dominant]["launches"] if dominant else 0,
+                     "avg_launch_us": kernels[dominant]["avg_launch_us"] if dominant else None,
+                     "rows_per_launch": m_launch,
+                     "traffic": traffic,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel at "
+                                        f"{m_launch} rows" if traffic else
+                                        f"no ncu capture at {m_launch} rows"),
+                     "all_gemms_tops": None if gemm_tops is None else round(gemm_tops, 1),
+                     "gemm_kernels": kernels,
+                     "timing": "CUDA events around each GEMM launch in eager micro-batch steps right after "
+                               "the graph-timed region"},
+        "e2e": {"value": round(e2e_ms / args.steps / N_IMAGES, 3), "unit": "ms",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_mb * n_mb * args.steps,
+        "clocks": clocks,
+        "int_ops_per_image_step": _int_ops_per_image_step(),
+        "setup_s": {"model_init": round(init_s, 2), "apply_triton": round(apply_s, 2),
+                    "graph_capture": round(capture_s, 2)},
+        "device_error": err,
+        "hbm_peak_gbs": peaks.get("hbm_gbs", HBM_FALLBACK_GBS),
+        "hbm_peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+        "latents_checksum": float(final.double().abs().sum().item()),
+    }
+    if cfgs:
+        rec["configs"] = cfgs
+    if cpu:
+        rec["cpu_baseline"] = cpu
+    if cpu1:
+        rec["cpu_baseline_cfg1"] = cpu1
+    print(json.dumps(rec), flush=True)
 
 
 def main() -> None:
@@ -468,7 +606,6 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels eagerly (no CUDA graph)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

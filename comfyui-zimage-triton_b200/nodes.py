@@ -99,6 +99,8 @@ class ZImageTritonApply:
     int8_min_dim = 1024
     int8_skip_sensitive = True
     int8_policy = None  # "reference" / "all_linears" / "main_layers"; None: from int8_skip_sensitive
+    # re-quantise INT8 layers whose bf16 weight a LoRA patch changed (the reference ignores LoRA there)
+    int8_lora_aware = False
 
     def apply_triton(self, model, enable_int8: bool = True):  # noqa: ANN001
         from zimage_b200.patching import apply_triton_kernels_comfyui
@@ -145,7 +147,8 @@ class ZImageTritonApply:
             from zimage_b200.quantization import apply_int8_quantization
 
             int8_stats = apply_int8_quantization(transformer, min_dim=self.int8_min_dim, mode="w8a8_hadamard",
-                                                 skip_sensitive=self.int8_skip_sensitive, policy=self.int8_policy)
+                                                 skip_sensitive=self.int8_skip_sensitive, policy=self.int8_policy,
+                                                 lora_aware=self.int8_lora_aware)
             transformer._int8_quantized = True
             transformer._int8_stats = int8_stats
             # ComfyUI VRAM accounting: recompute the model size (nodes.py:217-223)

@@ -206,6 +206,28 @@ def case_weight_prep(N=3 * D, K=D):
     return run, N * K * 2 + N * K + N * 2, f"[{N},{K}] bf16 -> int8 (offline)"
 
 
+def case_cfg3_ffn_block(M=S, Dm=D, Fm=F):
+    """The SwiGLU FFN block at 4608 rows as the fused block path runs it: RMSNorm * (1 + scale)
+    -> rotate -> int8; w1/w3 GEMM + SwiGLU + rotation (interleaved weight); int8 quantise; w2 GEMM."""
+    x, w, raw = _bf16(M, Dm), torch.ones(Dm, device="cuda"), _bf16(1, 4 * Dm, seed=1) * 0.1
+    w13, w2 = _i8(2 * Fm, Dm, seed=2), _i8(Dm, Fm, seed=3)
+    s1, s3, s2 = (torch.rand(n, device="cuda").to(torch.bfloat16) * 1e-3 for n in (Fm, Fm, Dm))
+    q, sx = _empty(M, Dm, dtype=torch.int8), _empty(M)
+    xr, qh, sxh, out = _empty(M, Fm), _empty(M, Fm, dtype=torch.int8), _empty(M), _empty(M, Dm)
+    st = _lib.stream_of(x)
+
+    def run():
+        _lib.call("zib_rmsnorm_mod_quant", x.data_ptr(), Dm, w.data_ptr(), raw.data_ptr(), None, 4 * Dm, M,
+                  q.data_ptr(), Dm, sx.data_ptr(), M, Dm, 1e-5, 1, st)
+        _lib.call("zib_gemm_w8a8_swiglu_had_w13", q.data_ptr(), Dm, w13.data_ptr(), Dm, sx.data_ptr(),
+                  s1.data_ptr(), s3.data_ptr(), xr.data_ptr(), Fm, M, Fm, Dm, st)
+        _lib.call("zib_act_quant", xr.data_ptr(), Fm, qh.data_ptr(), Fm, sxh.data_ptr(), None, M, Fm, 0, st)
+        _lib.call("zib_gemm_w8a8", qh.data_ptr(), Fm, w2.data_ptr(), Fm, sxh.data_ptr(), s2.data_ptr(), None,
+                  out.data_ptr(), Dm, M, Dm, Fm, st)
+
+    return run, 2 * M * 2 * Fm * Dm + 2 * M * Fm * Dm, f"[{M},{Dm}] norm*mod->int8, w13+SwiGLU, int8, w2"
+
+
 def case_sdpa():
     """torch SDPA (library) at the block's shape, for the step's time budget."""
     q = _bf16(B, S, 3, H, HD)
@@ -227,6 +249,8 @@ CASES = {
     "norm_gate_residual": (lambda: case_norm_gate_residual(), "hbm"),
     "swiglu_quant": (lambda: case_swiglu_quant(), "hbm"),
     "swiglu": (lambda: case_swiglu(), "hbm"),
+    "swiglu_quant_s4608": (lambda: case_swiglu_quant(S, F), "hbm"),
+    "cfg3_ffn_block": (lambda: case_cfg3_ffn_block(), "int8"),
     "qknorm_rope": (lambda: case_qknorm_rope(), "hbm"),
     "weight_prep": (lambda: case_weight_prep(), "hbm"),
     "gemm_cfg1_qkv_m1024": (lambda: case_gemm(1024, 3 * D, D), "int8"),

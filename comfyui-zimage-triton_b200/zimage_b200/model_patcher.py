@@ -28,6 +28,25 @@ class ZImageTritonModelPatcher(ModelPatcher):
         return super().patch_weight_to_device(key, device_to=device_to, inplace_update=inplace_update,
                                               return_weight=return_weight)
 
+    def _refresh_int8(self) -> None:
+        dm = getattr(getattr(self.model, "diffusion_model", None), "_int8_lora_aware", False)
+        if dm:
+            from zimage_b200.quantization import refresh_int8_weights
+
+            refresh_int8_weights(self.model.diffusion_model)
+
+    def patch_model(self, *args, **kwargs):
+        # LoRA-aware INT8: the patches just written into the (CPU) source weights are
+        # re-quantised into the layers' int8 buffers
+        out = super().patch_model(*args, **kwargs)
+        self._refresh_int8()
+        return out
+
+    def unpatch_model(self, *args, **kwargs):
+        out = super().unpatch_model(*args, **kwargs)
+        self._refresh_int8()
+        return out
+
     def partially_unload(self, device_to, memory_to_free=0, force_patch_weights=False):
         saved = []
         for _n, m in self.model.named_modules():

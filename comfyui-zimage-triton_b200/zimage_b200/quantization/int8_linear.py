@@ -232,13 +232,27 @@ def select_layers(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
     return plan, stats
 
 
+def weight_fingerprint(w: torch.Tensor) -> tuple:
+    """(storage pointer, version counter, hash of 4096 values at fixed strided positions) of a
+    weight: a low-rank update such as a LoRA patch changes nearly every value of the weight, so
+    it changes the sampled values whether it replaces the tensor or writes into it."""
+    flat = w.detach().reshape(-1)
+    idx = torch.linspace(0, flat.numel() - 1, min(flat.numel(), 4096)).long().to(flat.device)
+    return (w.data_ptr(), w._version, hash(flat[idx].float().cpu().numpy().tobytes()))
+
+
 def apply_int8_quantization(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
-                            skip_sensitive: bool = True, policy: str | None = None) -> dict[str, int]:
+                            skip_sensitive: bool = True, policy: str | None = None,
+                            lora_aware: bool = False) -> dict[str, int]:
     """Quantise qualifying nn.Linear layers in place (int8_linear.py:209-321).
 
     ``skip_sensitive=False`` quantises every linear with in/out >= ``min_dim``
     (the all-linears policy); the default reproduces the reference policy;
     ``policy`` selects one of "reference", "all_linears", "main_layers" by name.
+    ``lora_aware=True`` marks the model so that ``refresh_int8_weights`` (which the
+    ComfyUI model patcher calls after applying or removing weight patches) re-quantises
+    every layer whose source weight changed; the reference keeps the INT8 weights of
+    the first load and ignores LoRA on quantised layers (README.md:127-131).
     Returns {"quantized", "skipped", "sensitive", "had_skipped"}.
     """
     plan, stats = select_layers(model, min_dim, mode, skip_sensitive, policy)
@@ -249,6 +263,7 @@ def apply_int8_quantization(model: nn.Module, min_dim: int = _MIN_DIM, mode: str
         module.register_buffer("_w_int8", w_int8.to(target))
         module.register_buffer("_w_scale", w_scale.to(device=target, dtype=module.weight.dtype))
         module.weight.data = module.weight.data.to(device="cpu")
+        module._int8_src = weight_fingerprint(module.weight)
 
         module.forward = _make_w8a8_forward(module, had)
         module._int8_quantized = True
@@ -258,9 +273,38 @@ def apply_int8_quantization(model: nn.Module, min_dim: int = _MIN_DIM, mode: str
         module._int8_sd_hook = module._register_state_dict_hook(_int8_state_dict_hook)
         logger.debug("INT8 [%s] %s (%d->%d)", mode, name, in_f, out_f)
 
+    if lora_aware:
+        model._int8_lora_aware = True
     logger.info("INT8 [%s]: %d quantized, %d skipped, %d sensitive, %d had_skip", mode,
                 stats["quantized"], stats["skipped"], stats["sensitive"], stats["had_skipped"])
     return stats
+
+
+def refresh_int8_weights(model: nn.Module) -> int:
+    """Re-quantise every INT8 layer whose source weight changed since it was quantised.
+
+    The source weight (on the CPU, as after apply_int8_quantization) may have been
+    replaced or written in place, e.g. by a LoRA patch or its removal.  The new
+    int8 weights and scales are written into the existing ``_w_int8`` / ``_w_scale``
+    buffers, so every view of them (the stacked adaLN weights) and every cache
+    keyed on their versions (the fused block's interleaved FFN weight) follows.
+    Returns the number of layers re-quantised.
+    """
+    n = 0
+    for _name, m in model.named_modules():
+        if not (isinstance(m, nn.Linear) and getattr(m, "_int8_quantized", False) and hasattr(m, "_w_int8")):
+            continue
+        fp = weight_fingerprint(m.weight)
+        if fp == getattr(m, "_int8_src", None):
+            continue
+        w_int8, w_scale = quantize_weight(m.weight.data, bool(m._int8_use_hadamard))
+        m._w_int8.copy_(w_int8)
+        m._w_scale.copy_(w_scale.to(m._w_scale.dtype))
+        m._int8_src = fp
+        n += 1
+    if n:
+        logger.info("INT8 refresh: %d layers re-quantised.", n)
+    return n
 
 
 def restore_int8_quantization(model: nn.Module) -> int:
@@ -278,10 +322,10 @@ def restore_int8_quantization(model: nn.Module) -> int:
         if hook is not None:
             hook.remove()
         for attr in ("forward", "_apply", "_int8_quantized", "_int8_use_hadamard", "_int8_layer_name",
-                     "_int8_sd_hook"):
+                     "_int8_sd_hook", "_int8_src"):
             module.__dict__.pop(attr, None)
         restored += 1
-    for attr in ("_int8_quantized", "_int8_stats"):
+    for attr in ("_int8_quantized", "_int8_stats", "_int8_lora_aware"):
         if hasattr(model, attr):
             delattr(model, attr)
     # fused block caches hold views of the removed buffers
