@@ -579,7 +579,7 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
     rel(c.lane);
     return;
   }
-  double ss0 = 0.0, ss1 = 0.0;
+  double ss = 0.0;
 #pragma unroll 1
   for (int cc = 0; cc < CW / 32; ++cc) {
     uint32_t r[32];
@@ -590,19 +590,17 @@ __device__ __forceinline__ void epi_qkrope(const Params& p, const EpiCtx& c, int
       const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
       uint32_t o[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        o[t] = dequant2(r[j + 2 * t], r[j + 2 * t + 1], sx2, wv[t]);
-        px::sumsq_acc(o[t], ss0, ss1);  // exact squares; the fp64 sums are exact in practice
-      }
-      *reinterpret_cast<uint4*>(c.xbuf + xoff_512(rt, (c.cq * CW + cc * 32 + j) / 8)) =
-          make_uint4(o[0], o[1], o[2], o[3]);
+      for (int t = 0; t < 4; ++t) o[t] = dequant2(r[j + 2 * t], r[j + 2 * t + 1], sx2, wv[t]);
+      const uint4 ch = make_uint4(o[0], o[1], o[2], o[3]);
+      ss += px::sumsq_chunk(ch);  // canonical chunk sums, added exactly
+      *reinterpret_cast<uint4*>(c.xbuf + xoff_512(rt, (c.cq * CW + cc * 32 + j) / 8)) = ch;
     }
   }
   rel(c.lane);
   // one warp per head: this thread's row of the head is complete, so its rstd is
   // formed here once and handed to phase 2's lanes by shuffle
   const float eps = kind == 0 ? p.q_eps : p.k_eps;
-  const float rs_own = rstd_from_sum(ss0 + ss1, 128, eps);
+  const float rs_own = rstd_from_sum(ss, 128, eps);
   // this row's offset in the cos/sin tables (batch bi, position si; 32-bit, checked on the host)
   const int gr_own = row_ok ? row : 0;
   const int tab_own = (gr_own / p.seq) * (int)p.cs_b + (gr_own % p.seq) * 64;

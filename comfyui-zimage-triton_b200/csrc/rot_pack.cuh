@@ -70,23 +70,27 @@ __device__ __forceinline__ f2 from_bf16x2(uint32_t w) {
   return mk(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
-// exact sum of squares of the chunk's 8 bf16 values in fp64 (each square has
-// at most 16 significant bits; the fp64 partial sums are exact in practice)
-__device__ __forceinline__ void sumsq_acc(uint32_t w, double& a, double& b) {  // one bf16 pair
-  double lo, hi;
-  asm("cvt.f64.bf16 %0, %1;" : "=d"(lo) : "h"((unsigned short)(w & 0xFFFFu)));
-  asm("cvt.f64.bf16 %0, %1;" : "=d"(hi) : "h"((unsigned short)(w >> 16)));
-  a = __fma_rn(lo, lo, a);
-  b = __fma_rn(hi, hi, b);
+// acc + v^2 for the bf16 value v, one rounding (mixed-precision fma: no unpacking)
+__device__ __forceinline__ float sq_acc(unsigned short v, float acc) {
+  asm("fma.rn.f32.bf16 %0, %1, %1, %0;" : "+f"(acc) : "h"(v));
+  return acc;
 }
-__device__ __forceinline__ double sumsq_chunk(const uint4& d) {
-  double a = 0.0, b = 0.0;
-  sumsq_acc(d.x, a, b);
-  sumsq_acc(d.y, a, b);
-  sumsq_acc(d.z, a, b);
-  sumsq_acc(d.w, a, b);
-  return a + b;
+// chunk_sumsq (zib_common.cuh) of the chunk's 8 packed bf16 values: even positions are the
+// low halves, odd positions the high halves
+__device__ __forceinline__ float sumsq_chunk_f32(const uint4& d) {
+  float e = 0.0f, o = 0.0f;
+  e = sq_acc((unsigned short)(d.x & 0xFFFFu), e);
+  o = sq_acc((unsigned short)(d.x >> 16), o);
+  e = sq_acc((unsigned short)(d.y & 0xFFFFu), e);
+  o = sq_acc((unsigned short)(d.y >> 16), o);
+  e = sq_acc((unsigned short)(d.z & 0xFFFFu), e);
+  o = sq_acc((unsigned short)(d.z >> 16), o);
+  e = sq_acc((unsigned short)(d.w & 0xFFFFu), e);
+  o = sq_acc((unsigned short)(d.w >> 16), o);
+  return __fadd_rn(e, o);
 }
+// the same chunk sum widened for the row's exact fp64 accumulation
+__device__ __forceinline__ double sumsq_chunk(const uint4& d) { return (double)sumsq_chunk_f32(d); }
 
 // bf16(bf16(v * rstd) * w) of the chunk's 8 bf16 values, w = the chunk's 8
 // fp32 weights (rms_norm.py:53-57)

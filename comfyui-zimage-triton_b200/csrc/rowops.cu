@@ -153,8 +153,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(
     const int64_t c = threadIdx.x + (int64_t)i * blockDim.x;
     if (c < nchunks) {
       ld_chunk<VEC>(xr, c, n, v[i]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += (double)(v[i][j] * v[i][j]);  // exact products
+      ss += (double)chunk_sumsq(v[i]);
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
@@ -212,8 +211,7 @@ __global__ void __launch_bounds__(1024) norm_gate_residual_kernel(
     const int64_t c = threadIdx.x + (int64_t)i * blockDim.x;
     if (c < nchunks) {
       ld_chunk<VEC>(x + row * ldx, c, n, v[i]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += (double)(v[i][j] * v[i][j]);
+      ss += (double)chunk_sumsq(v[i]);
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
@@ -234,8 +232,8 @@ __global__ void __launch_bounds__(1024) norm_gate_residual_kernel(
       for (int j = 0; j < 8; ++j) {
         float xs = bf16_round(__fmul_rn(bf16_round(__fmul_rn(v[i][j], rstd)), wv[j]));
         v[i][j] = bf16_fma(gv[j], xs, rv[j]);  // RN_bf16(r + g * xs), one rounding
-        if (FUSE) ss2 += (double)(v[i][j] * v[i][j]);
       }
+      if (FUSE) ss2 += (double)chunk_sumsq(v[i]);
       st_chunk<VEC>(y + row * ldy, c, n, v[i]);
     }
   }
@@ -343,13 +341,9 @@ __global__ void __launch_bounds__(256, 3) qknorm_rope_kernel(
   for (int r = 0; r < R; ++r) {
     uint4 v = xv[r];
     if (NORM) {
-      // exact sum of squares (fp64), then bf16(bf16(x * rstd) * w) two lanes per instruction
-      double a = 0.0, bsum = 0.0;
-      px::sumsq_acc(v.x, a, bsum);
-      px::sumsq_acc(v.y, a, bsum);
-      px::sumsq_acc(v.z, a, bsum);
-      px::sumsq_acc(v.w, a, bsum);
-      double ss = a + bsum;
+      // the row's canonical sum of squares (chunk sums added exactly across the 16 lanes),
+      // then bf16(bf16(x * rstd) * w) two lanes per instruction
+      double ss = px::sumsq_chunk(v);
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
       v = px::norm_w(v, rstd_from_sum(ss, 128, eps), wa, wb);
@@ -789,8 +783,7 @@ __global__ void __launch_bounds__(128) rmsnorm_pipe(const uint16_t* __restrict__
     for (int64_t c = threadIdx.x; c < nchunks; c += 32 * W) {
       float v[8];
       load_bf16x8(sr + c * 8, v);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += (double)(v[j] * v[j]);
+      ss += (double)chunk_sumsq(v);
     }
     ss = cta_sum<W>(ss, redd);
     const float rstd = rstd_from_sum(ss, (int)n, eps);
@@ -879,8 +872,7 @@ __global__ void __launch_bounds__(128) ngr_pipe(
     for (int64_t c = threadIdx.x; c < nchunks; c += 32 * W) {
       float v[8];
       load_bf16x8(sxr + c * 8, v);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += (double)(v[j] * v[j]);
+      ss += (double)chunk_sumsq(v);
     }
     ss = cta_sum<W>(ss, redd);
     const float rstd = rstd_from_sum(ss, (int)n, eps);
@@ -903,8 +895,8 @@ __global__ void __launch_bounds__(128) ngr_pipe(
         a1 = bf16_fma(gv[j + 1], a1, rv[j + 1]);
         v[j] = a0;
         v[j + 1] = a1;
-        if (FUSE) ss2 += (double)(a0 * a0) + (double)(a1 * a1);
       }
+      if (FUSE) ss2 += (double)chunk_sumsq(v);
       store_bf16x8(y + row * ldy + c * 8, v);
       if (FUSE) store_bf16x8(sxr + c * 8, v);
     }

@@ -83,7 +83,7 @@ struct Team {
     // barrier 1 + team (a constant when the CTA is one team)
     if (R > 1) asm volatile("bar.sync %0, %1;" ::"r"(warps_of(R) == R ? 1 : 1 + grp), "r"(R * 32) : "memory");
   }
-  // exact in practice: every partial is an exact fp64 sum of exact fp32 squares
+  // exact in practice: every partial is an exact fp64 sum of fp32 chunk sums
   __device__ __forceinline__ double sum(double v, double* red) const {
     v = warp_sum_f64(v);
     if (R == 1) return v;
@@ -199,7 +199,7 @@ __device__ __forceinline__ void copies_done() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-// exact partial sum of squares of this lane's chunks
+// this lane's part of the row's sum of squares: its chunks' canonical fp32 sums, added in fp64
 __device__ __forceinline__ double row_sumsq(const uint4* sl, int cpl) {
   double ss = 0.0;
 #pragma unroll 4

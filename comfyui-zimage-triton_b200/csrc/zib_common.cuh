@@ -46,6 +46,22 @@ __device__ __forceinline__ float bf16_fma(float a, float b, float c) {
   return __uint_as_float((uint32_t)hd << 16);
 }
 
+// Canonical sum of squares of one chunk of 8 consecutive row values (bf16-representable
+// floats): the even and the odd positions are summed in order in fp32 (each square is exact,
+// each addition rounds once) and the two sums added.  Rows add their chunk sums exactly (fp64,
+// exact while the chunk sums' exponents lie within 29 bits of each other) and round once, so
+// the result does not depend on how a kernel spreads the chunks over threads.
+__device__ __forceinline__ float chunk_sumsq(const float v[8]) {
+  float e = __fmul_rn(v[0], v[0]), o = __fmul_rn(v[1], v[1]);
+  e = __fmaf_rn(v[2], v[2], e);
+  o = __fmaf_rn(v[3], v[3], o);
+  e = __fmaf_rn(v[4], v[4], e);
+  o = __fmaf_rn(v[5], v[5], o);
+  e = __fmaf_rn(v[6], v[6], e);
+  o = __fmaf_rn(v[7], v[7], o);
+  return __fadd_rn(e, o);
+}
+
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
   return __uint_as_float(((uint32_t)b) << 16);
 }

@@ -237,7 +237,10 @@ def weight_fingerprint(w: torch.Tensor) -> tuple:
     weight: a low-rank update such as a LoRA patch changes nearly every value of the weight, so
     it changes the sampled values whether it replaces the tensor or writes into it."""
     flat = w.detach().reshape(-1)
-    idx = torch.linspace(0, flat.numel() - 1, min(flat.numel(), 4096)).long().to(flat.device)
+    n = flat.numel()
+    k = min(n, 4096)
+    idx = (torch.arange(k, dtype=torch.int64) * (n - 1)) // max(k - 1, 1)  # exact integer positions
+    idx = idx.to(flat.device)
     return (w.data_ptr(), w._version, hash(flat[idx].float().cpu().numpy().tobytes()))
 
 

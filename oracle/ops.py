@@ -7,10 +7,10 @@ reference file:line it restates (paths relative to the reference project).
 Rounding conventions (the reference's, made explicit):
 
 * torch elementwise ops on bf16 compute in fp32 and round once to bf16 (RNE).
-* Row reductions (sum of squares) are restated with an exactly-rounded fp32
-  sum (fp64 accumulation, then one rounding).  The reference's Triton
-  ``tl.sum`` uses an implementation-defined tree order, so no order is
-  canonical; the CUDA kernels use the same exactly-rounded convention.
+* Row reductions (sum of squares) follow one canonical order (``sumsq_rows``):
+  fp32 sums over chunks of 8 values, added exactly and rounded once.  The
+  reference's Triton ``tl.sum`` uses an implementation-defined tree order, so no
+  order is canonical; the CUDA kernels use this one.
 * ``rsqrt`` is restated as IEEE ``1 / sqrt(v)`` in fp32: the correctly
   rounded square root, then the correctly rounded reciprocal.  Both are
   formed in fp64 and rounded once to fp32, which is exact for sqrt and
@@ -220,10 +220,35 @@ def w8a8_linear(x: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
 # RMSNorm family (rms_norm.py:47-57, fused_norm_residual.py:58-73)
 # ---------------------------------------------------------------------------
 
-def rstd_rows(x: torch.Tensor, eps: float) -> torch.Tensor:
-    """rsqrt(mean(x^2) + eps) per row in fp32 (exactly-rounded sum, IEEE ops)."""
+def sumsq_rows(x: torch.Tensor) -> torch.Tensor:
+    """Row sums of squares of a bf16 tensor in the kernels' canonical order, fp32 [..., 1].
+
+    The row is cut into chunks of 8 consecutive values (zero-padded at the end).  Within a
+    chunk the even and the odd positions are summed separately in fp32, in order
+    (each square of a bf16 value is exact in fp32; every addition rounds once), and the two
+    sums are added: s_c = ((x0^2 + x2^2) + x4^2) + x6^2 + (((x1^2 + x3^2) + x5^2) + x7^2).
+    The chunk sums are added exactly (fp64; exact while their exponents lie within 29 bits of
+    each other) and rounded once to fp32, so the result does not depend on how a kernel
+    distributes the chunks over its threads.  The reference's Triton ``tl.sum`` is an fp32
+    tree whose order is a compiler detail.
+    """
     n = x.shape[-1]
-    ss = (x.double() ** 2).sum(-1, keepdim=True).float()
+    pad = (-n) % 8
+    v = x.float().numpy().astype(np.float32)
+    if pad:
+        v = np.concatenate([v, np.zeros(v.shape[:-1] + (pad,), np.float32)], -1)
+    v = v.reshape(*v.shape[:-1], -1, 8)
+    sq = v * v                                   # exact
+    e = ((sq[..., 0] + sq[..., 2]) + sq[..., 4]) + sq[..., 6]
+    o = ((sq[..., 1] + sq[..., 3]) + sq[..., 5]) + sq[..., 7]
+    s = (e + o).astype(np.float64).sum(-1, keepdims=True)
+    return torch.from_numpy(s.astype(np.float32))
+
+
+def rstd_rows(x: torch.Tensor, eps: float) -> torch.Tensor:
+    """rsqrt(mean(x^2) + eps) per row in fp32 (canonical chunked sum, IEEE ops)."""
+    n = x.shape[-1]
+    ss = sumsq_rows(x)
     ms = (ss.double() / n).float()
     sq = torch.sqrt((ms + np.float32(eps)).double()).float()
     return (1.0 / sq.double()).float()

@@ -158,6 +158,22 @@ MODEL = {
 }
 
 
+# fraction of input values moved by one bf16 ulp in the reference's self-sensitivity runs: the
+# fraction of a block's QKV input that differs between this package and the reference (the
+# reference's approximate rsqrt in its RMSNorm), measured on the B200 at 2 x 4608 tokens
+PERTURB_RATE = 6e-6
+
+
+def perturb_ulp(x: torch.Tensor, rate: float, seed: int) -> torch.Tensor:
+    """x (bf16) with a seeded `rate` of its values moved to the next bf16 value away from zero."""
+    g = torch.Generator().manual_seed(seed)
+    pick = torch.rand(x.shape, generator=g) < rate
+    bits = x.contiguous().view(torch.int16).clone()
+    nz = pick & (x != 0)
+    bits[nz] += 1
+    return bits.view(torch.bfloat16)
+
+
 def model_inputs(name: str):
     """(x [B=2, S, dim] bf16, adaln_input [2, 256] bf16, freqs [1, S, 64, 2, 2] fp32) on the CPU."""
     from zimage_b200.nextdit import rope_freqs_matrix, zimage_positions

@@ -204,20 +204,29 @@ def run_models(torch, cases, only):
         x, t, fm = cases.model_inputs(name)
         xd, td, fmd = x.cuda(), t.cuda(), fm.cuda()
         rows = cases.model_rows(name, x.shape[0] * x.shape[1])
-        kept = {}
-        with torch.no_grad():
-            h = xd
-            for i, layer in enumerate(m.layers):
-                h = layer(h, None, fmd, adaln_input=td)
-                if i in spec["keep_layers"]:
-                    kept[i] = h.reshape(-1, h.shape[-1])[rows.cuda()].cpu()
-        torch.cuda.synchronize()
+        def run(inp):
+            kept = {}
+            with torch.no_grad():
+                h = inp
+                for i, layer in enumerate(m.layers):
+                    h = layer(h, None, fmd, adaln_input=td)
+                    if i in spec["keep_layers"]:
+                        kept[i] = h.reshape(-1, h.shape[-1])[rows.cuda()].cpu()
+            torch.cuda.synchronize()
+            return kept
+
+        kept = run(xd)
+        # the same forward on an input moved by one bf16 ulp at a seeded PERTURB_RATE of its
+        # values: how far the reference drifts from itself under the smallest input change
+        xp = cases.perturb_ulp(x, cases.PERTURB_RATE, seed=spec["xseed"] + 1)
+        kept_p = run(xp.cuda())
         out[name] = {"in_sha": {"x": cases.sha(x), "t": cases.sha(t), "freqs": cases.sha(fm)},
-                     "rows": rows, "layers": kept, "patch_stats": pstats, "int8_stats": qstats,
+                     "rows": rows, "layers": kept, "layers_perturbed": kept_p,
+                     "perturbed_values": int((xp != x).sum()), "patch_stats": pstats, "int8_stats": qstats,
                      "quantized": quantized}
         print(f"model {name}: {len(m.layers)} layers, {len(quantized)} int8 linears, "
               f"{time.time() - t0:.1f}s", flush=True)
-        del m, h, xd
+        del m, xd
         torch.cuda.empty_cache()
     return out
 

@@ -114,3 +114,23 @@ def test_interleaved_ffn_weight_needs_a_shared_aligned_row_layout():
     wide = torch.zeros(64, 160, dtype=torch.int8)
     assert _w13_interleaved(w[:64], wide[:, :128]) is None                 # different row strides
     assert _w13_interleaved(w[:32, ::2].contiguous(), w[:32].t()[:64, :32].t()) is None  # column-strided
+
+
+def test_weight_fingerprint_sees_in_place_updates():
+    """The LoRA-aware refresh keys on (pointer, version, sampled values): an in-place
+    low-rank update through .data (no version bump) and a write to the last element both
+    change it; the sampled positions stay in range for any size."""
+    from zimage_b200.quantization.int8_linear import weight_fingerprint
+
+    for shape in [(11520, 3840), (3, 5), (4096, 1), (1, 1)]:
+        w = torch.zeros(shape, dtype=torch.bfloat16)
+        fp = weight_fingerprint(w)
+        w.data[-1, -1] = 1.0
+        assert weight_fingerprint(w) != fp and w._version == 0
+    w = torch.randn(1024, 512).to(torch.bfloat16)
+    fp = weight_fingerprint(w)
+    assert weight_fingerprint(w) == fp
+    g = torch.Generator().manual_seed(0)
+    w.data.copy_((w.float() + 0.05 * torch.randn(1024, 4, generator=g) @ torch.randn(4, 512, generator=g))
+                 .to(torch.bfloat16))
+    assert weight_fingerprint(w) != fp

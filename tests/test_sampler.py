@@ -54,7 +54,7 @@ def test_micro_batches_do_not_depend_on_the_world_size(n_images, micro):
 SMALL = dict(n_layers=2, n_refiner_layers=1, dim=1024, n_heads=8, ffn_dim=2816, cap_feat_dim=256)
 
 
-def _small_model(seed=0, int8=True, patch=True):
+def _small_model(seed=0, int8=True, patch=True, policy="main_layers"):
     import nodes
     from zimage_b200.nextdit import ZImageDiT, random_init_
 
@@ -69,7 +69,7 @@ def _small_model(seed=0, int8=True, patch=True):
         mp.model.diffusion_model = m
         node = nodes.ZImageTritonApply()
         node.int8_min_dim = 0
-        node.int8_policy = "main_layers"
+        node.int8_policy = policy
         node.apply_triton(mp, enable_int8=int8)
     return m
 
@@ -115,6 +115,34 @@ def test_patched_full_model_close_to_unpatched_forward(cuda):
         y = m(lat.cuda(), t, cond.cuda()).float().cpu()
         want = ref(lat.cuda(), t, cond.cuda()).float().cpu()
     assert rel_l2(y, want) <= 1e-2
+
+
+@pytest.mark.gpu
+def test_all_linears_full_model(cuda):
+    """Every linear W8A8 (patch embedder K = 64 without rotation, final layer N = 64, the
+    timestep MLP and adaLN on the skinny GEMM, refiners on the fused / composed paths): the
+    captured sampler step equals the eager one, and the velocity stays within the W8A8
+    quantisation band of the model with bf16 embedders, refiners and final layer."""
+    from helpers import rel_l2
+    from zimage_b200.sampler import FlowSampler
+
+    m = _small_model(seed=5, policy="all_linears")
+    lins = [n for n, mod in m.named_modules() if isinstance(mod, torch.nn.Linear)]
+    assert all(getattr(m.get_submodule(n), "_int8_quantized", False) for n in lins)
+    assert not m.x_embedder._int8_use_hadamard and m.cap_embedder[1]._int8_use_hadamard
+    lat, cond, unc = _inputs(2, seed=2)
+    t = torch.tensor([0.4, 0.9], device="cuda")
+    ref = _small_model(seed=5, policy="main_layers")
+    with torch.no_grad():
+        v = m(lat.cuda(), t, cond.cuda()).float().cpu()
+        v_ref = ref(lat.cuda(), t, cond.cuda()).float().cpu()
+    assert torch.isfinite(v).all() and rel_l2(v, v_ref) <= 5e-2
+    outs = []
+    for graph in (True, False):
+        s = FlowSampler(m, (16, 16, 16), (16, SMALL["cap_feat_dim"]), micro_batch=2, cfg=4.0, steps=2,
+                        device="cuda", use_graph=graph)
+        outs.append(s.sample(lat.cuda(), cond.cuda(), unc.cuda()).cpu())
+    assert torch.equal(outs[0], outs[1])
 
 
 def _shard_worker(rank, world, port, out_path):
