@@ -31,9 +31,9 @@
 //   each (the row kernels' layout): the 128-point Hadamard transform on
 //   shuffles (SWIGLU) or norm * w + RoPE with coalesced cos/sin (QKROPE), and
 //   coalesced 256-byte row stores.
-//   SWIGLU tiles interleave the two weights in 32-row blocks,
-//   [w1 f0..f0+31 | w3 f0..f0+31 | w1 f0+32..f0+63 | w3 f0+32..f0+63 | ...], so
-//   each column quarter holds gate and up for 32 features.
+//   SWIGLU tiles stage 64 rows of each weight per 128 tile columns,
+//   [w1 f0..f0+63 | w3 f0..f0+63 | w1 f0+64..f0+127 | w3 f0+64..f0+127], so
+//   each column quarter pairs 32 gate columns with the up columns 64 further on.
 // Every mbarrier wait is bounded (globaltimer); on expiry the CTA records
 // ZIB_ERR_TIMEOUT in a device error word, drains its in-flight TMA loads and
 // MMAs, frees TMEM and exits.
@@ -55,7 +55,7 @@ constexpr int BN = 256;  // accumulator columns per tile
 constexpr int UMMA_K = 32;
 constexpr int HALF_BYTES = 128 * BK;  // one 128-row operand box
 constexpr int TMEM_COLS = 512;
-constexpr int SW_BOX_ROWS = 32;                // SWIGLU B box: 32 weight rows
+constexpr int SW_BOX_ROWS = 64;                // SWIGLU B box: 64 weight rows of w1 or of w3
 constexpr int SW_BOX_BYTES = SW_BOX_ROWS * BK;
 constexpr int S_STAGE_BYTES = 3 * HALF_BYTES;  // 1-CTA: A 128x128 + B 256x128
 constexpr int P_STAGE_BYTES = 2 * HALF_BYTES;  // 2-CTA pair: A 128x128 + B 128x128 per CTA
@@ -91,7 +91,7 @@ struct Params {
   const uint16_t* sx;
   const uint16_t* sw;   // per weight row (SWIGLU: w1 scales)
   const uint16_t* sw2;  // SWIGLU: w3 scales
-  int w13;              // SWIGLU: B is one [2F, K] tensor of alternating 32-row w1 / w3 blocks
+  int w13;              // SWIGLU: B is one [2F, K] tensor, the F rows of w1 then the F rows of w3
   const uint16_t* bias;
   uint16_t* y;
   int64_t ldy;
@@ -129,6 +129,24 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
       "%4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+// 3-D box (x = k, y = row, z = which of the two stacked [F, K] halves)
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t mbar_cluster, int x,
+                                                 int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(mbar_cluster), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -479,8 +497,9 @@ __device__ __forceinline__ void epi_split(const Params& p, const EpiCtx& c, int 
   }
 }
 
-// SWIGLU.  Phase 1 (thread = row): column quarter cq holds gate (cols
-// 64cq..64cq+31) and up (64cq+32..64cq+63) of features 128*nb + 32*cq + [0, 32);
+// SWIGLU.  Phase 1 (thread = row): the tile's 256 accumulator columns are two
+// parts of [64 gate | 64 up] columns; column quarter cq holds gate (cols
+// 128*(cq/2) + 32*(cq%2) + [0, 32)) and up (those + 64) of features 128*nb + 32*cq + [0, 32);
 // the bf16 SwiGLU values go to the staging tile [128 rows][128 features].
 // Phase 2 (8 lanes per row, two chunks each): Walsh-Hadamard over the 128
 // features of a row (index bits 0..2 and 6 in-thread, 3..5 by xor shuffles,
@@ -494,13 +513,13 @@ __device__ __forceinline__ void epi_swiglu(const Params& p, const EpiCtx& c, int
   const uint32_t sxb = row < p.M ? (uint32_t)p.sx[row] : 0u;
   const uint32_t sx2 = sxb | (sxb << 16);
   const int fb = nb * 128 + c.cq * 32;
-  const uint32_t tc = c.t_row + (uint32_t)(c.cq * 64);
+  const uint32_t tc = c.t_row + (uint32_t)((c.cq >> 1) * 128 + (c.cq & 1) * 32);
 #pragma unroll 1
   for (int g = 0; g < 2; ++g) {
     uint32_t rg[16], ru[16];
     __syncwarp();
     tmem_ld16(tc + (uint32_t)(g * 16), rg);
-    tmem_ld16(tc + (uint32_t)(32 + g * 16), ru);
+    tmem_ld16(tc + (uint32_t)(SW_BOX_ROWS + g * 16), ru);
     tmem_wait_ld();
     const uint4 s1a = ldg_u4(p.sw + fb + g * 16), s1b = ldg_u4(p.sw + fb + g * 16 + 8);
     const uint4 s3a = ldg_u4(p.sw2 + fb + g * 16), s3b = ldg_u4(p.sw2 + fb + g * 16 + 8);
@@ -651,23 +670,23 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const EpiCtx& c, 
 
 // Stage the B rows of tile nb for this CTA (`part` 0/1 = which 128 tile
 // columns; the 1-CTA kernel stages both).  Standard tiles: 128 consecutive
-// weight rows.  SWIGLU tiles: twice 32 rows of w1 then the same 32 rows of w3.
+// weight rows.  SWIGLU tiles: 64 rows of w1, then the same 64 rows of w3 (two
+// boxes from two tensors; one 3-D box when w1 and w3 are the halves of one tensor).
 template <int EPI>
 __device__ __forceinline__ void load_b_part(uint8_t* dst, const CUtensorMap* b0, const CUtensorMap* b1, int nb,
                                             int part, int kx, uint64_t* bar, uint32_t pair_bar, bool pair,
                                             bool w13) {
-  if (EPI == EPI_SWIGLU && !w13) {
-#pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int f = nb * 128 + part * 64 + jj * SW_BOX_ROWS;
-      uint8_t* d = dst + jj * 2 * SW_BOX_BYTES;
-      if (pair) {
-        tma_load_2d_pair(d, b0, pair_bar, kx, f);
-        tma_load_2d_pair(d + SW_BOX_BYTES, b1, pair_bar, kx, f);
-      } else {
-        tma_load_2d(d, b0, bar, kx, f);
-        tma_load_2d(d + SW_BOX_BYTES, b1, bar, kx, f);
-      }
+  if (EPI == EPI_SWIGLU) {
+    const int f = nb * 128 + part * SW_BOX_ROWS;
+    if (w13) {
+      if (pair) tma_load_3d_pair(dst, b0, pair_bar, kx, f, 0);
+      else tma_load_3d(dst, b0, bar, kx, f, 0);
+    } else if (pair) {
+      tma_load_2d_pair(dst, b0, pair_bar, kx, f);
+      tma_load_2d_pair(dst + SW_BOX_BYTES, b1, pair_bar, kx, f);
+    } else {
+      tma_load_2d(dst, b0, bar, kx, f);
+      tma_load_2d(dst + SW_BOX_BYTES, b1, bar, kx, f);
     }
   } else {
     if (pair) tma_load_2d_pair(dst, b0, pair_bar, kx, nb * 256 + part * 128);
@@ -1102,6 +1121,29 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+// int8 [2, rows, inner]: two [rows, inner] halves stacked (row stride ld_bytes, the second
+// half rows * ld_bytes after the first), boxes of 128 bytes x box_rows x both halves, 128B swizzle
+static int make_map_halves(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t ld_bytes,
+                           uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) {
+    zib_set_error("gemm_w8a8: cuTensorMapEncodeTiled unavailable");
+    return ZIB_ERR_UNSUPPORTED;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)ld_bytes, (cuuint64_t)(ld_bytes * rows)};
+  cuuint32_t box[3] = {(cuuint32_t)BK, box_rows, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    zib_set_error("gemm_w8a8: cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+    return ZIB_ERR_INVALID_ARG;
+  }
+  return ZIB_OK;
+}
+
 // int8 [outer, inner] row-major with row stride ld_bytes, boxes of 128 bytes x box_rows, 128B swizzle
 static int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld_bytes,
                     uint32_t box_rows) {
@@ -1256,7 +1298,8 @@ static void plan_split(Params& p, int clusters) {
   p.splits = 1;
   const int T = p.num_tiles, C = clusters;
   // The last unit of a split tile re-reads every partial (S x 128 KB per CTA) before its
-  // epilogue; that only pays off for long tiles (measured: K = 10240 gains 5%, K = 3840 loses 4%).
+  // epilogue; that only pays off for long tiles (measured: K = 10240 gains 5%; K = 3840 loses
+  // 4% at 7 waves, and 9% at 2.4 waves, where the split last wave is a larger share of the time).
   if (!g_split_enabled || T <= C || T % C == 0 || p.num_kb < kSplitMinKBlocks) return;
   const int R = T % C;
   int S = C / R;
@@ -1313,17 +1356,22 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
       return launch_skinny<EPI>(q, ldq, w, ldw, p, stream, what);
   }
   CUtensorMap ta, tb, tb2;
-  // SWIGLU with separate w1 / w3: 32-row boxes from each; with the interleaved
-  // [2F, K] tensor: one 128-row box per CTA part, as for the plain GEMM
+  // SWIGLU with separate w1 / w3: a 64-row box from each per CTA part; with w1 and
+  // w3 as the two halves of one [2F, K] tensor: one 3-D box of 64 rows x both halves
   const bool two_b = EPI == EPI_SWIGLU && !p.w13;
-  const uint32_t b_box = two_b ? (uint32_t)SW_BOX_ROWS : 128u;
-  const int64_t b_rows = EPI == EPI_SWIGLU && p.w13 ? 2 * w_rows : w_rows;
+  const uint32_t b_box = EPI == EPI_SWIGLU ? (uint32_t)SW_BOX_ROWS : 128u;
   int st = make_map(&ta, q, K, M, ldq, 128u);
   if (st) return st;
-  st = make_map(&tb, w, K, b_rows, ldw, b_box);
-  if (st) return st;
-  st = make_map(&tb2, two_b ? w2 : w, K, b_rows, ldw, b_box);
-  if (st) return st;
+  if (EPI == EPI_SWIGLU && p.w13) {
+    st = make_map_halves(&tb, w, K, w_rows, ldw, b_box);
+    if (st) return st;
+    tb2 = tb;
+  } else {
+    st = make_map(&tb, w, K, w_rows, ldw, b_box);
+    if (st) return st;
+    st = make_map(&tb2, two_b ? w2 : w, K, w_rows, ldw, b_box);
+    if (st) return st;
+  }
 
   const int cols_per_tile = EPI == EPI_SWIGLU ? 128 : BN;  // output columns per tile
   p.num_nb = (p.N + cols_per_tile - 1) / cols_per_tile;
@@ -1466,36 +1514,8 @@ namespace gemm {
 // One [2F, K] int8 weight of alternating 32-row blocks (w1 rows 32g..32g+31,
 // then w3 rows 32g..32g+31, g = 0 .. F/32-1) from w1 and w3 [F, K] (row
 // stride ldw): each thread moves 16 bytes.
-__global__ void w13_interleave_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w3, int64_t ldw,
-                                      uint8_t* __restrict__ w13, int64_t F, int64_t K) {
-  const int64_t cpr = K / 16;  // 16-byte chunks per row
-  const int64_t total = 2 * F * cpr;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / cpr, c = i % cpr;
-    const int64_t src_row = (r / 64) * 32 + (r % 32);
-    const uint8_t* src = (r % 64) < 32 ? w1 : w3;
-    *reinterpret_cast<uint4*>(w13 + r * K + c * 16) =
-        __ldg(reinterpret_cast<const uint4*>(src + src_row * ldw + c * 16));
-  }
-}
-
 }  // namespace gemm
 }  // namespace zib
-
-extern "C" int zib_w13_interleave(const void* w1, const void* w3, int64_t ldw, void* w13, int64_t F, int64_t K,
-                                  void* stream) {
-  ZIB_HOST_CHECK(w1 && w3 && w13, ZIB_ERR_INVALID_ARG, "w13_interleave: null operand");
-  ZIB_HOST_CHECK(F > 0 && F % 32 == 0 && K > 0 && ldw >= K, ZIB_ERR_INVALID_ARG,
-                 "w13_interleave: bad shape F=%lld K=%lld (F must be a multiple of 32)", (long long)F, (long long)K);
-  ZIB_HOST_CHECK(K % 16 == 0 && ldw % 16 == 0 && aligned16(w1) && aligned16(w3) && aligned16(w13), ZIB_ERR_ALIGNMENT,
-                 "w13_interleave: rows must be 16-byte aligned");
-  const int64_t total = 2 * F * (K / 16);
-  int64_t blocks = (total + 255) / 256;
-  if (blocks > 4096) blocks = 4096;
-  zib::gemm::w13_interleave_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
-      (const uint8_t*)w1, (const uint8_t*)w3, ldw, (uint8_t*)w13, F, K);
-  return zib_check_launch("w13_interleave");
-}
 
 extern "C" int zib_gemm_w8a8_swiglu_had_w13(const void* q, int64_t ldq, const void* w13, int64_t ldw,
                                             const void* sx, const void* sw1, const void* sw3, void* x_rot,

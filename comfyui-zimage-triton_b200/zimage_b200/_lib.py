@@ -41,7 +41,6 @@ SIGNATURES: dict[str, list] = {
     "zib_gemm_w8a8_acc_i32": [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _VP],
     "zib_gemm_w8a8_swiglu_had": [_VP, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP],
     "zib_gemm_w8a8_swiglu_had_w13": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP],
-    "zib_w13_interleave": [_VP, _VP, _I64, _VP, _I64, _I64, _VP],
     "zib_gemm_w8a8_qk_norm_rope": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP,
                                    _F32, _F32, _VP, _VP, _I64, _I64, _I64, _VP],
     "zib_gemm_set_variant": [_I32],

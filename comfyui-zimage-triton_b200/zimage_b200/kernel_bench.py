@@ -164,18 +164,16 @@ def case_gemm_swiglu(M, F_, K):
 
 
 def case_gemm_swiglu_w13(M, F_, K):
-    q, w1, w3 = _i8(M, K), _i8(F_, K, seed=1), _i8(F_, K, seed=3)
+    q, w13 = _i8(M, K), _i8(2 * F_, K, seed=1)   # [w1; w3]: the two weights as halves of one tensor
     sx, s1, s3 = _bf16(M).abs() * 1e-2, _bf16(F_, seed=2).abs() * 1e-3, _bf16(F_, seed=4).abs() * 1e-3
-    w13 = torch.empty(2 * F_, K, dtype=torch.int8, device="cuda")
     st = _lib.stream_of(q)
-    _lib.call("zib_w13_interleave", w1.data_ptr(), w3.data_ptr(), K, w13.data_ptr(), F_, K, st)
     y = _empty(M, F_)
 
     def run():
         _lib.call("zib_gemm_w8a8_swiglu_had_w13", q.data_ptr(), K, w13.data_ptr(), K, sx.data_ptr(),
                   s1.data_ptr(), s3.data_ptr(), y.data_ptr(), F_, M, F_, K, st)
 
-    return run, 2 * M * 2 * F_ * K, f"{M}x(2x{F_})x{K} int8 (w1/w3 interleaved) -> SwiGLU -> rot128 bf16"
+    return run, 2 * M * 2 * F_ * K, f"{M}x(2x{F_})x{K} int8 (w1/w3 halves of one tensor) -> SwiGLU -> rot128 bf16"
 
 
 def case_gemm_qk_rope(M, K):
@@ -208,7 +206,7 @@ def case_weight_prep(N=3 * D, K=D):
 
 def case_cfg3_ffn_block(M=S, Dm=D, Fm=F):
     """The SwiGLU FFN block at 4608 rows as the fused block path runs it: RMSNorm * (1 + scale)
-    -> rotate -> int8; w1/w3 GEMM + SwiGLU + rotation (interleaved weight); int8 quantise; w2 GEMM."""
+    -> rotate -> int8; w1/w3 GEMM + SwiGLU + rotation (w1/w3 halves of one tensor); int8 quantise; w2 GEMM."""
     x, w, raw = _bf16(M, Dm), torch.ones(Dm, device="cuda"), _bf16(1, 4 * Dm, seed=1) * 0.1
     w13, w2 = _i8(2 * Fm, Dm, seed=2), _i8(Dm, Fm, seed=3)
     s1, s3, s2 = (torch.rand(n, device="cuda").to(torch.bfloat16) * 1e-3 for n in (Fm, Fm, Dm))

@@ -259,6 +259,7 @@ def _block_cache(block: nn.Module):
              attn.q_norm, attn.k_norm)
     if not all(getattr(n, "weight", None) is not None for n in norms):
         return None
+    w13 = _w13_halves(ff)
     key = tuple((n.weight.data_ptr(), n.weight._version) for n in norms) + tuple(
         (l._w_int8.data_ptr(), l._w_int8._version, l._w_scale.data_ptr()) for l in lins)
     c = block.__dict__.get("_zib_cache")
@@ -271,23 +272,35 @@ def _block_cache(block: nn.Module):
         "eps_an1": _eps(block.attention_norm1), "eps_an2": _eps(block.attention_norm2),
         "eps_fn1": _eps(block.ffn_norm1), "eps_fn2": _eps(block.ffn_norm2),
         "eps_q": _eps(attn.q_norm), "eps_k": _eps(attn.k_norm),
-        "F": F_, "w13": _w13_interleaved(ff.w1._w_int8, ff.w3._w_int8), "key": key,
+        "F": F_, "w13": w13, "key": key,
     }
     block.__dict__["_zib_cache"] = c
     return c
 
 
-def _w13_interleaved(w1: torch.Tensor, w3: torch.Tensor) -> torch.Tensor | None:
-    """w1 and w3 as one int8 [2F, K] tensor of alternating 32-row blocks, the weight
-    layout of zib_gemm_w8a8_swiglu_had_w13 (one TMA copy per CTA and k-block instead
-    of four); None when the two weights do not share a 16-byte-aligned row layout."""
+def _w13_halves(ff: nn.Module) -> torch.Tensor | None:
+    """The [2F, K] int8 tensor whose halves are w1's and w3's ``_w_int8`` (the weight layout of
+    zib_gemm_w8a8_swiglu_had_w13), or None when the two weights cannot share one.
+
+    The first call moves both weights into one tensor and makes the modules' buffers views of
+    its halves (no second copy of either weight); afterwards the halves are found again as
+    long as the buffers stay those views.  In-place writes into the buffers (a LoRA refresh)
+    keep the layout.
+    """
+    w1, w3 = ff.w1._w_int8, ff.w3._w_int8
     F_, K_ = w1.shape
-    if (w1.stride(1) != 1 or w3.stride(1) != 1 or w1.stride(0) != w3.stride(0) or K_ % 16
-            or w1.stride(0) % 16 or w1.data_ptr() % 16 or w3.data_ptr() % 16 or F_ % 32):
+    if (w3.shape != w1.shape or w1.stride(1) != 1 or w3.stride(1) != 1 or w1.stride(0) != K_
+            or w3.stride(0) != K_ or K_ % 16 or w1.data_ptr() % 16 or w3.data_ptr() % 16
+            or w1.device != w3.device):
         return None
-    w13 = torch.empty(2 * F_, K_, dtype=torch.int8, device=w1.device)
-    _lib.call("zib_w13_interleave", w1.data_ptr(), w3.data_ptr(), w1.stride(0), w13.data_ptr(), F_, K_,
-              _lib.stream_of(w1))
+    esz = w1.element_size()
+    if w3.data_ptr() == w1.data_ptr() + F_ * K_ * esz and w1._base is not None and w1._base is w3._base:
+        base = w1._base
+        if base.dim() == 2 and tuple(base.shape) == (2 * F_, K_) and base.data_ptr() == w1.data_ptr():
+            return base
+    w13 = torch.cat([w1, w3], 0)
+    ff.w1._buffers["_w_int8"] = w13[:F_]
+    ff.w3._buffers["_w_int8"] = w13[F_:]
     return w13
 
 

@@ -290,7 +290,7 @@ def refresh_int8_weights(model: nn.Module) -> int:
     replaced or written in place, e.g. by a LoRA patch or its removal.  The new
     int8 weights and scales are written into the existing ``_w_int8`` / ``_w_scale``
     buffers, so every view of them (the stacked adaLN weights) and every cache
-    keyed on their versions (the fused block's interleaved FFN weight) follows.
+    keyed on their versions (the fused block's FFN weight, held as halves of one tensor) follows.
     Returns the number of layers re-quantised.
     """
     n = 0

@@ -108,24 +108,16 @@ ZIB_API int zib_gemm_w8a8_swiglu_had(const void* q, int64_t ldq, const void* w1,
                              void* x_rot, int64_t ldo, int64_t M, int64_t F, int64_t K,
                              void* stream);
 
-/* zib_gemm_w8a8_swiglu_had with w1 and w3 in one int8 [2F, K] tensor (row
- * stride ldw) of alternating 32-row blocks: rows 64g..64g+31 = w1 rows
- * 32g..32g+31, rows 64g+32..64g+63 = w3 rows 32g..32g+31 (zib_w13_interleave
- * builds it once per weight).  Each CTA then stages its 128 weight rows of a
- * k-block with one TMA copy from one tensor instead of four 32-row copies from
- * two.  Same arithmetic and output, bit for bit.  Same reference interfaces as
- * zib_gemm_w8a8_swiglu_had (a layout of the prepared weights, no reference
- * counterpart of its own). */
+/* zib_gemm_w8a8_swiglu_had with w1 and w3 as the two halves of one int8 [2F, K]
+ * tensor (row stride ldw): rows 0..F-1 = w1, rows F..2F-1 = w3, i.e. the
+ * two-weight call with w3 = w13 + F * ldw.  Each CTA then stages its 64 rows of
+ * each weight per k-block with one 3-D TMA copy instead of two.  Same
+ * arithmetic and output, bit for bit; w1 and w3 stay usable as the [F, K]
+ * halves.  Same reference interfaces as zib_gemm_w8a8_swiglu_had (a layout of
+ * the prepared weights, no reference counterpart of its own). */
 ZIB_API int zib_gemm_w8a8_swiglu_had_w13(const void* q, int64_t ldq, const void* w13, int64_t ldw,
                                  const void* sx, const void* sw1, const void* sw3, void* x_rot,
                                  int64_t ldo, int64_t M, int64_t F, int64_t K, void* stream);
-
-/* Builds the [2F, K] interleaved weight of zib_gemm_w8a8_swiglu_had_w13 (row
- * stride K) from w1 and w3 (int8 [F, K], row stride ldw) on the device.
- * F % 32 == 0, K and ldw multiples of 16.  No reference counterpart (weight
- * layout of the fused FFN GEMM). */
-ZIB_API int zib_w13_interleave(const void* w1, const void* w3, int64_t ldw, void* w13, int64_t F,
-                       int64_t K, void* stream);
 
 /* QKV projection with the per-head Q/K RMSNorm and the interleaved RoPE fused
  * into the GEMM epilogue.  Replaces the int8 qkv linear (int8_linear.py:133-137)

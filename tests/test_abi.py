@@ -56,13 +56,11 @@ def test_host_validation_before_launch():
     # M not a multiple of the sequence length
     assert lib.zib_gemm_w8a8_qk_norm_rope(16, 128, 16, 128, 16, 16, 16, 768, 9, 768, 128, 16, 16, 1e-5, 1e-5,
                                           16, 16, 0, 8, 2, None) == _lib.ZIB_ERR_INVALID_ARG
-    # interleaved-[w1|w3] SwiGLU GEMM and its weight builder: ragged features, null weight, ragged K
+    # the one-tensor [w1; w3] SwiGLU GEMM: ragged features, null weight
     assert lib.zib_gemm_w8a8_swiglu_had_w13(16, 128, 16, 128, 16, 16, 16, 16, 200, 8, 200, 128, None) == \
         _lib.ZIB_ERR_INVALID_ARG
     assert lib.zib_gemm_w8a8_swiglu_had_w13(16, 128, None, 128, 16, 16, 16, 16, 128, 8, 128, 128, None) == \
         _lib.ZIB_ERR_INVALID_ARG
-    assert lib.zib_w13_interleave(16, 16, 128, 16, 48, 128, None) == _lib.ZIB_ERR_INVALID_ARG
-    assert lib.zib_w13_interleave(16, 16, 136, 16, 64, 136, None) == _lib.ZIB_ERR_ALIGNMENT
     # misaligned output of the SwiGLU epilogue
     assert lib.zib_gemm_w8a8_swiglu_had(16, 128, 16, 16, 128, 16, 16, 16, 18, 128, 8, 128, 128, None) == \
         _lib.ZIB_ERR_ALIGNMENT

@@ -74,7 +74,7 @@ def _model(params, lora_aware):
 
 def test_refresh_reaches_the_fused_block_path(cuda):
     """Patched w1 of block 0 and adaLN of block 1 after quantisation: one refresh and the fused
-    block path (interleaved FFN weight, stacked adaLN) gives the outputs of a model quantised
+    block path (w1/w3 as halves of one tensor, stacked adaLN) gives the outputs of a model quantised
     from the patched weights."""
     from oracle import model as omodel
     from zimage_b200.quantization import refresh_int8_weights

@@ -112,7 +112,9 @@ def test_block_fused_equals_composed_and_matches_oracle(cuda):
         finally:
             pc.ENABLE_FUSED_BLOCK = True
     assert "_zib_cache" in m.layers[0].__dict__
-    assert m.layers[0].__dict__["_zib_cache"]["w13"] is not None  # interleaved [w1|w3] FFN weight in use
+    w13 = m.layers[0].__dict__["_zib_cache"]["w13"]
+    assert w13 is not None  # w1 and w3 as the halves of one [2F, K] tensor, no second copy
+    assert m.layers[0].feed_forward.w1._w_int8.data_ptr() == w13.data_ptr()
     assert torch.equal(y_fused, y_comp)
     # oracle with its own weight prep and fp32 attention: within the attention-numerics band
     p = omodel.prep_layer(params[0], quant_adaln=True)
@@ -121,7 +123,7 @@ def test_block_fused_equals_composed_and_matches_oracle(cuda):
 
 
 def test_fused_block_follows_in_place_weight_updates(cuda):
-    """The fused path's interleaved [w1|w3] copy is rebuilt when w1 or w3 change in place."""
+    """The fused path follows in-place changes of w1 or w3 (the halves of one tensor)."""
     from zimage_b200.patching import patching_comfyui as pc
 
     dim, heads, ffn = 1024, 8, 2816

@@ -103,17 +103,32 @@ def test_registration_names():
     assert mod.NODE_DISPLAY_NAME_MAPPINGS == {"ZImageTritonApply": "ZImage Triton Accelerate"}
 
 
-def test_interleaved_ffn_weight_needs_a_shared_aligned_row_layout():
-    """The fused block path keeps the two-weight SwiGLU GEMM when w1 and w3 cannot be
-    interleaved in 32-row blocks (checked on the host, before any device call)."""
-    from zimage_b200.patching.patching_comfyui import _w13_interleaved
+def test_ffn_weights_become_halves_of_one_tensor():
+    """The fused block path puts w1 and w3 into one [2F, K] tensor once and makes the modules'
+    buffers views of its halves (no second copy); it finds the halves again afterwards, and
+    keeps the two-weight GEMM when the weights cannot share a tensor (checked on the host)."""
+    import types
 
-    w = torch.zeros(96, 128, dtype=torch.int8)
-    assert _w13_interleaved(w[:48], w[48:]) is None                        # F not a multiple of 32
-    assert _w13_interleaved(w[:, :120], w[:, 8:]) is None                  # K not a multiple of 16
-    wide = torch.zeros(64, 160, dtype=torch.int8)
-    assert _w13_interleaved(w[:64], wide[:, :128]) is None                 # different row strides
-    assert _w13_interleaved(w[:32, ::2].contiguous(), w[:32].t()[:64, :32].t()) is None  # column-strided
+    from zimage_b200.patching.patching_comfyui import _w13_halves
+
+    def ffn(w1, w3):
+        ff = types.SimpleNamespace(w1=torch.nn.Module(), w3=torch.nn.Module())
+        ff.w1.register_buffer("_w_int8", w1)
+        ff.w3.register_buffer("_w_int8", w3)
+        return ff
+
+    g = torch.Generator().manual_seed(0)
+    w1 = torch.randint(-127, 128, (64, 128), generator=g, dtype=torch.int8)
+    w3 = torch.randint(-127, 128, (64, 128), generator=g, dtype=torch.int8)
+    ff = ffn(w1.clone(), w3.clone())
+    w13 = _w13_halves(ff)
+    assert w13.shape == (128, 128) and torch.equal(w13, torch.cat([w1, w3]))
+    assert ff.w1._w_int8.data_ptr() == w13.data_ptr() and torch.equal(ff.w1._w_int8, w1)
+    assert ff.w3._w_int8.data_ptr() == w13.data_ptr() + 64 * 128 and torch.equal(ff.w3._w_int8, w3)
+    assert _w13_halves(ff) is w13                                            # found again, no new copy
+    assert _w13_halves(ffn(w1[:, :120], w3[:, :120])) is None                # K not a multiple of 16
+    assert _w13_halves(ffn(w1[:, ::2], w3[:, ::2])) is None                  # column-strided
+    assert _w13_halves(ffn(w1[:32], w3)) is None                             # different shapes
 
 
 def test_weight_fingerprint_sees_in_place_updates():
