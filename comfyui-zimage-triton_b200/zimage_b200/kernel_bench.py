@@ -260,6 +260,7 @@ CASES = {
     "gemm_qkv_qk_rope": (lambda: case_gemm_qk_rope(M_TOK, D), "int8"),
     "gemm_w13_swiglu_had": (lambda: case_gemm_swiglu(M_TOK, F, D), "int8"),
     "gemm_w13_swiglu_had_w13": (lambda: case_gemm_swiglu_w13(M_TOK, F, D), "int8"),
+    "gemm_w13_swiglu_had_w13_m18432": (lambda: case_gemm_swiglu_w13(2 * M_TOK, F, D), "int8"),
     "sdpa_torch": (lambda: case_sdpa(), "bf16"),
 }
 
