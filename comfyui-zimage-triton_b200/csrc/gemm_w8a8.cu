@@ -109,6 +109,9 @@ struct Params {
   // [0, tail_start) are whole tiles; the remaining tiles run as `splits` units
   // each over a slice of K, whose int32 partial tiles meet in `ws`
   int num_units, tail_start, splits;
+  // half tiles (pair kernel, plain and int32 epilogues, whole-K units only): the
+  // tail tiles [tail_start, num_tiles) run as two units of 128 output columns each
+  int halves;
   int32_t* ws;        // [tail tile][cta rank][split][128 x 256] int32 partials
   int* counters;      // [tail tile][cta rank] arrivals, back to 0 after the last one
 };
@@ -409,21 +412,21 @@ __device__ __forceinline__ void epi_chunk(const Params& p, int row, int n0, cons
   }
 }
 
-// plain dequant (+bias) or raw int32: this thread's row, columns [256/NQ * cq, +256/NQ)
+// plain dequant (+bias) or raw int32: this thread's row, accumulator columns [32 * nch * cq, +32 * nch)
+// of a unit whose column 0 is output column n_base
 template <int EPI, class Rel>
-__device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
+__device__ __forceinline__ void epi_plain(const Params& p, const EpiCtx& c, int n_base, int nch, const Rel& rel) {
   const int row = c.row_base + c.quarter * 32 + c.lane;
   const bool row_ok = row < p.M;
   uint16_t sxb = 0;
   if (EPI == EPI_BF16 && row_ok) sxb = p.sx[row];
   const uint32_t sx2 = (uint32_t)sxb | ((uint32_t)sxb << 16);
   const float sxf = __uint_as_float((uint32_t)sxb << 16);
-  constexpr int CH = 8 / Cfg<EPI>::NQ;  // 32-column chunks per warp
 #pragma unroll 1
-  for (int ch = c.cq * CH; ch < c.cq * CH + CH; ++ch) {
+  for (int ch = c.cq * nch; ch < c.cq * nch + nch; ++ch) {
     uint32_t r[32];
     tmem_row32(c.t_row + (uint32_t)(ch * 32), r);
-    const int n0 = nb * BN + ch * 32;
+    const int n0 = n_base + ch * 32;
     if (!row_ok || n0 >= p.N) continue;
     epi_chunk<EPI>(p, row, n0, r, sx2, sxf);
   }
@@ -665,7 +668,7 @@ template <int EPI, class Rel>
 __device__ __forceinline__ void epilogue_tile(const Params& p, const EpiCtx& c, int nb, const Rel& rel) {
   if (EPI == EPI_SWIGLU) epi_swiglu(p, c, nb, rel);
   else if (EPI == EPI_QKROPE) epi_qkrope(p, c, nb, rel);
-  else epi_plain<EPI>(p, c, nb, rel);
+  else epi_plain<EPI>(p, c, nb * BN, 8 / Cfg<EPI>::NQ, rel);
 }
 
 // Stage the B rows of tile nb for this CTA (`part` 0/1 = which 128 tile
@@ -790,14 +793,17 @@ __global__ void __launch_bounds__(256) gemm_w8a8_skinny_kernel(const int8_t* __r
   }
 }
 
-// Work unit u -> tile, K-block range and split index (-1: the whole tile).
+// Work unit u -> tile, K-block range, split index (-1: the whole K range) and
+// half (-1: all 256 columns; 0 / 1: columns [0, 128) / [128, 256) of the tile).
 struct Unit {
-  int tile, kb0, kb1, split;
+  int tile, kb0, kb1, split, half;
 };
 __device__ __forceinline__ Unit unit_of(const Params& p, int u) {
-  if (u < p.tail_start) return Unit{u, 0, p.num_kb, -1};
-  const int v = u - p.tail_start, sp = v % p.splits;
-  return Unit{p.tail_start + v / p.splits, sp * p.num_kb / p.splits, (sp + 1) * p.num_kb / p.splits, sp};
+  if (u < p.tail_start) return Unit{u, 0, p.num_kb, -1, -1};
+  const int v = u - p.tail_start;
+  if (p.halves) return Unit{p.tail_start + (v >> 1), 0, p.num_kb, -1, v & 1};
+  const int sp = v % p.splits;
+  return Unit{p.tail_start + v / p.splits, sp * p.num_kb / p.splits, (sp + 1) * p.num_kb / p.splits, sp, -1};
 }
 
 // --- kernels -------------------------------------------------------------------
@@ -1000,12 +1006,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           const uint32_t fb = smem_u32(&full_bar[stage]);
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * P_STAGE_BYTES);
+          // a half unit stages 64 weight rows per CTA (the tensor map tmap_b2 has 64-row boxes)
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], w.half < 0 ? 2 * P_STAGE_BYTES : 3 * HALF_BYTES);
           const uint32_t fb_leader = leader ? fb : mapa_rank(fb, 0);
           uint8_t* st = smem + stage * P_STAGE_BYTES;
           tma_load_2d_pair(st, &tmap_a, fb_leader, kb * BK, mb * 256 + (int)rank * 128);
-          load_b_part<EPI>(st + HALF_BYTES, &tmap_b, &tmap_b2, nb, (int)rank, kb * BK, nullptr, fb_leader, true,
-                           p.w13);
+          if ((EPI == EPI_BF16 || EPI == EPI_I32) && w.half >= 0)
+            tma_load_2d_pair(st + HALF_BYTES, &tmap_b2, fb_leader, kb * BK, nb * 256 + w.half * 128 + (int)rank * 64);
+          else
+            load_b_part<EPI>(st + HALF_BYTES, &tmap_b, &tmap_b2, nb, (int)rank, kb * BK, nullptr, fb_leader, true,
+                             p.w13);
           pend_mask |= 1u << stage;
           pend_parity = (pend_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -1030,6 +1040,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
         if (!mbar_wait_bounded(&tempty_bar[accb], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(accb * BN);
+        const uint32_t idesc = w.half < 0 ? idesc_i8(256, 256) : idesc_i8(256, 128);
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
@@ -1038,7 +1049,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k)
             umma_i8_pair(d_tmem, adesc + (uint64_t)((k * UMMA_K) >> 4), bdesc + (uint64_t)((k * UMMA_K) >> 4),
-                         idesc_i8(256, 256), (kb != w.kb0 || k != 0) ? 1u : 0u);
+                         idesc, (kb != w.kb0 || k != 0) ? 1u : 0u);
           umma_commit_pair(&empty_bar[stage], (uint16_t)3);  // frees the stage in both CTAs
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -1077,6 +1088,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg<EPI>::THREADS, 1
       const ReleaseLeader rel{mapa_rank(smem_u32(&tempty_bar[accb]), 0)};
       if constexpr (EPI == EPI_BF16 || EPI == EPI_I32) {
         if (w.split >= 0) epi_split<EPI>(p, c, nb, w.tile - p.tail_start, w.split, (int)rank, rel);
+        else if (w.half >= 0) epi_plain<EPI>(p, c, nb * BN + w.half * 128, 4 / Cfg<EPI>::NQ, rel);
         else epilogue_tile<EPI>(p, c, nb, rel);
       } else {
         epilogue_tile<EPI>(p, c, nb, rel);
@@ -1316,6 +1328,20 @@ static void plan_split(Params& p, int clusters) {
   p.counters = w.ctr;
 }
 
+// Half units for a short last wave (pair kernel, plain and int32 epilogues,
+// whole-K tiles).  R = T mod C tiles of the last wave on C CTA pairs leave
+// C - R pairs idle for a whole tile; when 2R <= C they run as 2R units of 128
+// output columns each, so the last wave takes about half as long (config 1,
+// 1024 x 11520 x 3840: 180 tiles on 74 pairs, 2.5 tile times instead of 3).
+static void plan_halves(Params& p, int clusters) {
+  const int T = p.num_tiles, C = clusters;
+  const int R = T % C;
+  if (!g_split_enabled || R == 0 || 2 * R > C) return;
+  p.tail_start = T - R;
+  p.halves = 1;
+  p.num_units = p.tail_start + 2 * R;
+}
+
 // M <= 8 rows: the skinny kernel (one launch, CTAs sized for four per SM).
 template <int EPI>
 static int launch_skinny(const void* q, int64_t ldq, const void* w, int64_t ldw, const Params& p, void* stream,
@@ -1369,7 +1395,8 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
   } else {
     st = make_map(&tb, w, K, w_rows, ldw, b_box);
     if (st) return st;
-    st = make_map(&tb2, two_b ? w2 : w, K, w_rows, ldw, b_box);
+    // plain / int32: the second map stages the 64 weight rows per CTA of a half unit
+    st = make_map(&tb2, two_b ? w2 : w, K, w_rows, ldw, EPI == EPI_SWIGLU ? b_box : 64u);
     if (st) return st;
   }
 
@@ -1402,18 +1429,20 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
     p.num_mb = (int)((M + 255) / 256);
     p.num_tiles = p.num_mb * p.num_nb;
     int clusters = sms / 2;
-    if (clusters > p.num_tiles) clusters = p.num_tiles;
     p.num_units = p.num_tiles;
     p.tail_start = p.num_tiles;
     p.splits = 1;
+    p.halves = 0;
     if (EPI == EPI_BF16 || EPI == EPI_I32) {
       if (static_splits > 0) {
-        const int st = plan_split_static(p, clusters, static_splits, what);
+        const int st = plan_split_static(p, clusters < p.num_tiles ? clusters : p.num_tiles, static_splits, what);
         if (st) return st;
       } else {
         plan_split(p, clusters);
+        if (p.splits == 1) plan_halves(p, clusters);
       }
     }
+    if (clusters > p.num_units) clusters = p.num_units;
     gemm_w8a8_pair_kernel<EPI><<<2 * clusters, Cfg<EPI>::THREADS, smem_bytes, (cudaStream_t)stream>>>(ta, tb, tb2, p);
   } else {
     p.num_mb = (int)((M + 127) / 128);

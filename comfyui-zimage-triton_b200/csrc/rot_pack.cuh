@@ -320,5 +320,28 @@ __device__ __forceinline__ uint2 quant_chunk(const uint4& d, float rcp) {
                     pack_s8(q[5], q[4], pack_s8(q[7], q[6], 0u)));
 }
 
+// quant_chunk for a row whose |max| is finite (every bf16(v / s) finite, |v / s| < 2^22):
+// rne to an integer by one packed fp32 add of 1.5 * 2^23 (the sum's unit in the last place is 1,
+// so the add rounds v / s to the nearest integer, ties to even, exactly like cvt.rni), whose
+// low bits, less those of 1.5 * 2^23, are the integer; two values per add instead of one
+// conversion each on the narrow conversion pipe.
+__device__ __forceinline__ uint2 quant_chunk_rne(const uint4& d, float rcp) {
+  constexpr float kRne = 12582912.0f;  // 1.5 * 2^23
+  constexpr int kRneBits = 0x4B400000;
+  const f2 R = mk(rcp, rcp), M = mk(kRne, kRne);
+  const uint32_t w[4] = {d.x, d.y, d.z, d.w};
+  int q[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t b = to_bf16x2(mul(from_bf16x2(w[k]), R));
+    float lo, hi;
+    split(add(from_bf16x2(b), M), lo, hi);
+    q[2 * k] = __float_as_int(lo) - kRneBits;
+    q[2 * k + 1] = __float_as_int(hi) - kRneBits;
+  }
+  return make_uint2(pack_s8(q[1], q[0], pack_s8(q[3], q[2], 0u)),
+                    pack_s8(q[5], q[4], pack_s8(q[7], q[6], 0u)));
+}
+
 }  // namespace px
 }  // namespace zib

@@ -299,66 +299,66 @@ __global__ void __launch_bounds__(1024) swiglu_kernel(
 
 // ---------------------------------------------------------------------------
 // K3: per-head RMSNorm + interleaved RoPE, d = 128 (fused_qknorm_rope.py:85-151)
-// 16 lanes per (token, head) row, 8 values (4 pairs) per lane.
+// One warp per token: its two half-warps take heads h0 + 2i (h0 = 0, 1), 16
+// lanes per (token, head) row with 8 values (4 pairs) each, so that a warp's
+// loads and stores cover two adjacent heads (512 contiguous bytes when the
+// heads are packed) and the token's cos / sin, shared by all its heads, are
+// loaded once instead of once per head.  RB rows per half-warp in flight.
 // ---------------------------------------------------------------------------
-template <bool NORM, int R>
-__global__ void __launch_bounds__(256, 3) qknorm_rope_kernel(
+template <bool NORM>
+__global__ void __launch_bounds__(256) qknorm_rope_kernel(
     const uint16_t* __restrict__ x, int64_t x_sb, int64_t x_ss, int64_t x_sh,
     uint16_t* __restrict__ out, int64_t o_sb, int64_t o_ss, int64_t o_sh,
     const float* __restrict__ cosp, const float* __restrict__ sinp, int64_t cs_b,
-    const float* __restrict__ w, int64_t S, int64_t H, int64_t total_rows, float eps) {
-  // 16 lanes per (token, head) row, 8 values (4 pairs) per lane; each half-warp
-  // handles R rows spaced 16 apart so the block's loads stay contiguous and
-  // every thread has R independent loads in flight.  Row indices are split
-  // with 32-bit divisions (the host checks that they fit).
+    const float* __restrict__ w, int64_t S, int64_t H, int64_t tokens, float eps) {
+  constexpr int RB = 5;
   const int lane = threadIdx.x & 31;
   const int sub = lane & 15;
-  const int hw = threadIdx.x >> 4;
-  const uint32_t base = blockIdx.x * (16u * R);
-  const uint32_t H32 = (uint32_t)H, S32 = (uint32_t)S;
-  uint4 xv[R];
-  float4 c4[R], s4[R];
-  int64_t oo[R];
-  bool ok[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const uint32_t rowg = base + r * 16u + (uint32_t)hw;
-    ok[r] = rowg < (uint64_t)total_rows;
-    const uint32_t rr = ok[r] ? rowg : 0u;
-    const uint32_t t = rr / H32, h = rr - t * H32;
-    const uint32_t b = t / S32, s = t - b * S32;
-    xv[r] = *reinterpret_cast<const uint4*>(x + b * x_sb + s * x_ss + h * x_sh + sub * 8);
-    c4[r] = __ldg(reinterpret_cast<const float4*>(cosp + b * cs_b + s * 64 + sub * 4));
-    s4[r] = __ldg(reinterpret_cast<const float4*>(sinp + b * cs_b + s * 64 + sub * 4));
-    oo[r] = b * o_sb + s * o_ss + h * o_sh + sub * 8;
-  }
+  const int h0 = lane >> 4;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   float4 wa = make_float4(0.f, 0.f, 0.f, 0.f), wb = wa;
   if (NORM) {
     wa = __ldg(reinterpret_cast<const float4*>(w + sub * 8));
     wb = __ldg(reinterpret_cast<const float4*>(w + sub * 8 + 4));
   }
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens; t += warps) {
+    const int64_t b = t / S, s = t - b * S;
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(cosp + b * cs_b + s * 64 + sub * 4));
+    const float4 s4 = __ldg(reinterpret_cast<const float4*>(sinp + b * cs_b + s * 64 + sub * 4));
+    const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+    const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+    const uint16_t* xt = x + b * x_sb + s * x_ss + sub * 8;
+    uint16_t* ot = out + b * o_sb + s * o_ss + sub * 8;
+    for (int64_t hb = h0; hb < H; hb += 2 * RB) {
+      uint4 xv[RB];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    uint4 v = xv[r];
-    if (NORM) {
-      // the row's canonical sum of squares (chunk sums added exactly across the 16 lanes),
-      // then bf16(bf16(x * rstd) * w) two lanes per instruction
-      double ss = px::sumsq_chunk(v);
+      for (int r = 0; r < RB; ++r) {
+        const int64_t h = hb + 2 * r;
+        xv[r] = h < H ? *reinterpret_cast<const uint4*>(xt + h * x_sh) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-      v = px::norm_w(v, rstd_from_sum(ss, 128, eps), wa, wb);
+      for (int r = 0; r < RB; ++r) {
+        uint4 v = xv[r];
+        if (NORM) {
+          // the row's canonical sum of squares (chunk sums added exactly across the 16 lanes),
+          // then bf16(bf16(x * rstd) * w) two lanes per instruction
+          double ss = px::sumsq_chunk(v);
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+          v = px::norm_w(v, rstd_from_sum(ss, 128, eps), wa, wb);
+        }
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // pair rotation: fma(a, c, -(b s)), fma(b, c, a s)
+          const float a = __uint_as_float(wv[k] << 16), bb = __uint_as_float(wv[k] & 0xFFFF0000u);
+          o[k] = px::to_bf16x2(px::mk(__fmaf_rn(a, cv[k], -__fmul_rn(bb, sv[k])),
+                                      __fmaf_rn(bb, cv[k], __fmul_rn(a, sv[k]))));
+        }
+        const int64_t h = hb + 2 * r;
+        if (h < H) *reinterpret_cast<uint4*>(ot + h * o_sh) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
     }
-    const float cv[4] = {c4[r].x, c4[r].y, c4[r].z, c4[r].w};
-    const float sv[4] = {s4[r].x, s4[r].y, s4[r].z, s4[r].w};
-    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {  // pair rotation: fma(a, c, -(b s)), fma(b, c, a s)
-      const float a = __uint_as_float(wv[k] << 16), bb = __uint_as_float(wv[k] & 0xFFFF0000u);
-      o[k] = px::to_bf16x2(px::mk(__fmaf_rn(a, cv[k], -__fmul_rn(bb, sv[k])),
-                                  __fmaf_rn(bb, cv[k], __fmul_rn(a, sv[k]))));
-    }
-    if (ok[r]) *reinterpret_cast<uint4*>(out + oo[r]) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -1097,7 +1097,19 @@ extern "C" int zib_act_quant(const void* x, int64_t ldx, void* q, int64_t ldq, v
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(K / 8, &l), ZIB_ERR_TOO_LARGE, "act_quant: K=%lld exceeds 65536", (long long)K);
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = wr::dispatch(K, [&](auto Rc, int cpl) {
+  bool launched = false;
+  int rg_R = 0, rg_cpl = 0;
+  if (wr::rg_shape(K, &rg_R, &rg_cpl)) {
+    auto go = [&](auto k, int R) {
+      k<<<wr::grid_rg(k, 32 * wr::warps_of(R), wr::warps_of(R) / R, M), 32 * wr::warps_of(R), 0, st>>>(
+          (const uint16_t*)x, ldx, (int8_t*)q, ldq, (uint16_t*)sx, (uint16_t*)x_rot, M);
+    };
+    if (rg_R == 3) hadamard ? go(wr::act_quant_rg<3, 5, true>, 3) : go(wr::act_quant_rg<3, 5, false>, 3);
+    else hadamard ? go(wr::act_quant_rg<4, 10, true>, 4) : go(wr::act_quant_rg<4, 10, false>, 4);
+    launched = true;
+  }
+  if (!launched)
+  launched = wr::dispatch(K, [&](auto Rc, int cpl) {
     constexpr int R = decltype(Rc)::value;
     auto k = hadamard ? wr::act_quant_wr<R, true> : wr::act_quant_wr<R, false>;
     wr::set_smem(k, wr::smem_for(R, cpl, 1));
@@ -1193,7 +1205,16 @@ extern "C" int zib_rmsnorm_mod_quant(const void* x, int64_t ldx, const float* w,
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "rmsnorm_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = wr::dispatch(n, [&](auto Rc, int cpl) {
+  bool launched = false;
+  if (n == 3840) {  // the register-resident kernel (teams of three warps, five chunks per lane)
+    auto k = hadamard ? wr::rmsnorm_mod_quant_rg<3, 5, true> : wr::rmsnorm_mod_quant_rg<3, 5, false>;
+    k<<<wr::grid_rg(k, 96, 1, rows), 96, 0, st>>>((const uint16_t*)x, ldx, w, (const uint16_t*)scale,
+                                                  (const uint16_t*)shift, ld_mod, rows_per_batch, (int8_t*)q,
+                                                  ldq, (uint16_t*)sx, n, eps, rows);
+    launched = true;
+  }
+  if (!launched)
+  launched = wr::dispatch(n, [&](auto Rc, int cpl) {
     constexpr int R = decltype(Rc)::value;
     auto k = hadamard ? wr::rmsnorm_wr<R, 2, true> : wr::rmsnorm_wr<R, 2, false>;
     wr::set_smem(k, wr::smem_for(R, cpl, 1));
@@ -1269,7 +1290,17 @@ extern "C" int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, cons
   RowLaunch l;
   ZIB_HOST_CHECK(row_launch(n / 8, &l), ZIB_ERR_TOO_LARGE, "norm_gate_residual_mod_quant: n too large");
   cudaStream_t st = (cudaStream_t)stream;
-  bool launched = wr::dispatch<true>(n, [&](auto Rc, int cpl) {
+  bool launched = false;
+  if (n == 3840) {  // the register-resident kernel (teams of three warps, five chunks per lane)
+    auto k = hadamard ? wr::ngr_rg<5, true> : wr::ngr_rg<5, false>;
+    k<<<wr::grid_rg(k, 96, 1, rows), 96, 0, st>>>(
+        (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
+        (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
+        (uint16_t*)sx, n, eps, eps2, rows);
+    launched = true;
+  }
+  if (!launched)
+  launched = wr::dispatch<true>(n, [&](auto Rc, int cpl) {
     constexpr int R = decltype(Rc)::value;
     constexpr int nb = wr::ngr_buffers(R);
     auto k = hadamard ? wr::ngr_wr<R, true, true> : wr::ngr_wr<R, true, false>;
@@ -1365,20 +1396,19 @@ extern "C" int zib_qknorm_rope(const void* x, int64_t x_sb, int64_t x_ss, int64_
                      x_sb % 8 == 0 && x_ss % 8 == 0 && x_sh % 8 == 0 && o_sb % 8 == 0 && o_ss % 8 == 0 &&
                      o_sh % 8 == 0 && cs_b % 4 == 0,
                  ZIB_ERR_ALIGNMENT, "qknorm_rope: operands must be 16-byte aligned");
-  const int64_t rows = B * S * H;
-  if (rows == 0) return ZIB_OK;
-  ZIB_HOST_CHECK(rows < (1ll << 31), ZIB_ERR_TOO_LARGE, "qknorm_rope: more than 2^31 rows");
-  constexpr int R = 4;
-  const int rows_per_block = 16 * R;  // 256 threads, 4 rows per half-warp
-  const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
-  ZIB_HOST_CHECK(blocks < (1ll << 31), ZIB_ERR_TOO_LARGE, "qknorm_rope: too many rows");
+  const int64_t tokens = B * S;
+  if (tokens == 0 || H == 0) return ZIB_OK;
+  // one warp per token, 8 warps per CTA, as many CTAs as fit (a grid-stride loop takes the rest)
+  const int64_t need = (tokens + 7) / 8;
+  const int64_t cap = (int64_t)pipe::num_sms() * 8;
+  const unsigned blocks = (unsigned)(need < cap ? need : cap);
   cudaStream_t st = (cudaStream_t)stream;
   if (w) {
-    qknorm_rope_kernel<true, R><<<(unsigned)blocks, 256, 0, st>>>(
-        (const uint16_t*)x, x_sb, x_ss, x_sh, (uint16_t*)out, o_sb, o_ss, o_sh, cosp, sinp, cs_b, w, S, H, rows, eps);
+    qknorm_rope_kernel<true><<<blocks, 256, 0, st>>>(
+        (const uint16_t*)x, x_sb, x_ss, x_sh, (uint16_t*)out, o_sb, o_ss, o_sh, cosp, sinp, cs_b, w, S, H, tokens, eps);
   } else {
-    qknorm_rope_kernel<false, R><<<(unsigned)blocks, 256, 0, st>>>(
-        (const uint16_t*)x, x_sb, x_ss, x_sh, (uint16_t*)out, o_sb, o_ss, o_sh, cosp, sinp, cs_b, w, S, H, rows, eps);
+    qknorm_rope_kernel<false><<<blocks, 256, 0, st>>>(
+        (const uint16_t*)x, x_sb, x_ss, x_sh, (uint16_t*)out, o_sb, o_ss, o_sh, cosp, sinp, cs_b, w, S, H, tokens, eps);
   }
   return zib_check_launch("qknorm_rope");
 }

@@ -217,8 +217,13 @@ __device__ __forceinline__ void quant_row(const Team<R>& t, const uint4* sl, int
   const float s = act_scale(__uint_as_float(m << 16));
   const float rcp = __fdiv_rn(1.0f, s);
   int8_t* qr = q + row * ldq + t.first(cpl);
+  if (m < 0x7F80u) {  // finite |max| (a row-uniform branch)
 #pragma unroll 1
-  for (int k = 0; k < cpl; ++k) *reinterpret_cast<uint2*>(qr + 256 * k) = px::quant_chunk(sl[32 * k], rcp);
+    for (int k = 0; k < cpl; ++k) *reinterpret_cast<uint2*>(qr + 256 * k) = px::quant_chunk_rne(sl[32 * k], rcp);
+  } else {
+#pragma unroll 1
+    for (int k = 0; k < cpl; ++k) *reinterpret_cast<uint2*>(qr + 256 * k) = px::quant_chunk(sl[32 * k], rcp);
+  }
   if (t.wig == 0 && t.lane == 0) sx[row] = float_to_bf16_bits(s);
 }
 
@@ -386,6 +391,183 @@ __global__ void __launch_bounds__(32 * warps_of(R)) ngr_wr(
     }
     __syncwarp();
   }
+}
+
+// --- register-resident rows ------------------------------------------------------------
+//
+// The same kernels for the two row widths of the DiT step (3840 features: teams
+// of three warps, five chunks per lane; 10240: teams of four, ten chunks), with
+// the row held in registers: every input chunk of a row is loaded once, at the
+// start of the row, with all of them in flight together; nothing is staged in
+// shared memory (which only carries the team reductions), and the chunk loops
+// are unrolled (CPL is a template argument).  The chunk ownership, the
+// arithmetic and its order are those of the shared-memory kernels above, so
+// the results are the same bits.  Measured on B200 (kernel medians, L2 flushed):
+// the fused norm kernel at [9216, 3840] 85 -> 72 us (staged in shared memory it
+// ran at 80% of the L1 data pipe: each staged row written once and read four
+// times), the plain quantiser at [9216, 10240] 65 -> 51 us, the rotating one at
+// [9216, 3840] 39 -> 37 us, norm + modulation + quantisation 57 -> 51 us.  The
+// SwiGLU quantiser (two 10240-wide inputs) measured slower this way and keeps
+// the shared-memory kernel.  A 128-group per quad of lanes (32 elements per
+// lane, a quarter of the transform's shuffles) measured slower again: its
+// 64-byte runs per lane take four times the L1 wavefronts per load.
+
+// a 16-byte load of streamed data (read once): not kept in L1, where the norm
+// weights and modulation vectors that every row reads stay
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+
+// Team size and chunks per lane of the register-resident kernels for a row of n bf16
+__host__ __device__ constexpr bool rg_shape(int64_t n, int* R, int* cpl) {
+  if (n == 3840) { *R = 3; *cpl = 5; return true; }
+  if (n == 10240) { *R = 4; *cpl = 10; return true; }
+  return false;
+}
+
+// quant_row on the team's rotated chunks held in registers
+template <int R, int CPL>
+__device__ __forceinline__ void quant_regs(const Team<R>& t, const uint4 (&v)[CPL], uint32_t m2, uint32_t* redu,
+                                           int64_t row, int8_t* __restrict__ q, int64_t ldq,
+                                           uint16_t* __restrict__ sx) {
+  uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
+  m = t.umax(m, redu);
+  const float s = act_scale(__uint_as_float(m << 16));
+  const float rcp = __fdiv_rn(1.0f, s);
+  int8_t* qr = q + row * ldq + t.first(CPL);
+  if (m < 0x7F80u) {  // finite |max| (a row-uniform branch)
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) *reinterpret_cast<uint2*>(qr + 256 * k) = px::quant_chunk_rne(v[k], rcp);
+  } else {
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) *reinterpret_cast<uint2*>(qr + 256 * k) = px::quant_chunk(v[k], rcp);
+  }
+  if (t.wig == 0 && t.lane == 0) sx[row] = float_to_bf16_bits(s);
+}
+
+// act_quant_wr with the row in registers
+template <int R, int CPL, bool HAD>
+__global__ void __launch_bounds__(32 * warps_of(R)) act_quant_rg(const uint16_t* __restrict__ x, int64_t ldx,
+                                                            int8_t* __restrict__ q, int64_t ldq,
+                                                            uint16_t* __restrict__ sx, uint16_t* __restrict__ xr,
+                                                            int64_t rows) {
+  __shared__ uint32_t redu[warps_of(R)];
+  const Team<R> t;
+  const int64_t f0 = t.first(CPL);
+  const int64_t step = (int64_t)gridDim.x * (warps_of(R) / R);
+  for (int64_t row = (int64_t)blockIdx.x * (warps_of(R) / R) + t.grp; row < rows; row += step) {
+    const uint16_t* xp = x + row * ldx + f0;
+    uint4 v[CPL];
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) v[k] = ld_stream(xp + 256 * k);
+    px::AbsMax m;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      rot_amax<HAD>(v[k], m, t.lane);
+      if (xr) *reinterpret_cast<uint4*>(xr + row * ldq + f0 + 256 * k) = v[k];  // optional copy
+    }
+    quant_regs<R, CPL>(t, v, m.packed(), redu, row, q, ldq, sx);
+  }
+}
+
+// ngr_wr<3, true, HAD> (norm + gate + residual, then norm * (1+s) (+shift) ->
+// rotate / quantise) with the rows x and r in registers
+template <int CPL, bool HAD>
+__global__ void __launch_bounds__(96) ngr_rg(
+    const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ r, int64_t ldr,
+    const uint16_t* __restrict__ gate, int64_t ld_gate, int64_t rows_per_batch, const float* __restrict__ w,
+    uint16_t* __restrict__ y, int64_t ldy, const float* __restrict__ w2, const uint16_t* __restrict__ scale,
+    const uint16_t* __restrict__ shift, int64_t ld_mod, int8_t* __restrict__ q, int64_t ldq,
+    uint16_t* __restrict__ sx, int64_t n, float eps, float eps2, int64_t rows) {
+  constexpr int R = 3;
+  static_assert(warps_of(R) == R, "one team per CTA");
+  __shared__ double redd[R];
+  __shared__ uint32_t redu[R];
+  const Team<R> t;
+  const int64_t f0 = t.first(CPL);
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    uint4 a[CPL], e[CPL];
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) a[k] = ld_stream(x + row * ldx + f0 + 256 * k);
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) e[k] = ld_stream(r + row * ldr + f0 + 256 * k);
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) ss += px::sumsq_chunk(a[k]);
+    const float rstd = rstd_from_sum(t.sum(ss, redd), (int)n, eps);
+    const int64_t b = batch_of(row, rows_per_batch);
+    const uint16_t* gl = gate + b * ld_gate + f0;
+    uint16_t* yr = y + row * ldy + f0;
+    double ss2 = 0.0;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      const uint4 nv = px::norm_w(a[k], rstd, w + f0 + 256 * k);
+      const uint4 g = ld_nc(gl + 256 * k);
+      // RN_bf16(r + g * a), one rounding, as in ngr_wr
+      a[k] = make_uint4(hfma2(g.x, nv.x, e[k].x), hfma2(g.y, nv.y, e[k].y), hfma2(g.z, nv.z, e[k].z),
+                        hfma2(g.w, nv.w, e[k].w));
+      *reinterpret_cast<uint4*>(yr + 256 * k) = a[k];
+      ss2 += px::sumsq_chunk(a[k]);
+    }
+    const float rstd2 = rstd_from_sum(t.sum(ss2, redd), (int)n, eps2);
+    const int64_t mo = b * ld_mod + f0;
+    px::AbsMax m;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      a[k] = modulate(px::norm_w(a[k], rstd2, w2 + f0 + 256 * k), ld_nc(scale + mo + 256 * k),
+                      shift ? ld_nc(shift + mo + 256 * k) : make_uint4(0, 0, 0, 0), shift != nullptr);
+      rot_amax<HAD>(a[k], m, t.lane);
+    }
+    quant_regs<R, CPL>(t, a, m.packed(), redu, row, q, ldq, sx);
+  }
+}
+
+// rmsnorm_wr<R, 2, HAD> (norm * (1+s) (+shift) -> rotate / quantise) with the row in registers
+template <int R, int CPL, bool HAD>
+__global__ void __launch_bounds__(32 * warps_of(R)) rmsnorm_mod_quant_rg(
+    const uint16_t* __restrict__ x, int64_t ldx, const float* __restrict__ w, const uint16_t* __restrict__ scale,
+    const uint16_t* __restrict__ shift, int64_t ld_mod, int64_t rows_per_batch, int8_t* __restrict__ q, int64_t ldq,
+    uint16_t* __restrict__ sx, int64_t n, float eps, int64_t rows) {
+  __shared__ double redd[warps_of(R)];
+  __shared__ uint32_t redu[warps_of(R)];
+  const Team<R> t;
+  const int64_t f0 = t.first(CPL);
+  const int64_t step = (int64_t)gridDim.x * (warps_of(R) / R);
+  for (int64_t row = (int64_t)blockIdx.x * (warps_of(R) / R) + t.grp; row < rows; row += step) {
+    uint4 a[CPL];
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) a[k] = ld_stream(x + row * ldx + f0 + 256 * k);
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) ss += px::sumsq_chunk(a[k]);
+    const float rstd = rstd_from_sum(t.sum(ss, redd), (int)n, eps);
+    const int64_t mo = batch_of(row, rows_per_batch) * ld_mod + f0;
+    px::AbsMax m;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      a[k] = modulate(px::norm_w(a[k], rstd, w + f0 + 256 * k), ld_nc(scale + mo + 256 * k),
+                      shift ? ld_nc(shift + mo + 256 * k) : make_uint4(0, 0, 0, 0), shift != nullptr);
+      rot_amax<HAD>(a[k], m, t.lane);
+    }
+    quant_regs<R, CPL>(t, a, m.packed(), redu, row, q, ldq, sx);
+  }
+}
+
+// CTAs for a register-resident kernel (no dynamic shared memory): all that fit, at most one per team-row
+template <class K>
+static int grid_rg(K kernel, int threads, int rows_per_cta, int64_t rows) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  const int64_t need = (rows + rows_per_cta - 1) / rows_per_cta;
+  const int64_t g = (int64_t)per_sm * pipe::num_sms();
+  return (int)(need < g ? need : g);
 }
 
 // out = bf16(bf16(silu(g)) * u) (swiglu.py:51-58); QUANT: then rotate (HAD) and

@@ -66,12 +66,28 @@ def test_act_quant_midpoint_rows_bitexact(cuda):
     assert torch.equal(q2, q) and torch.equal(sx2, sx)
 
 
-@pytest.mark.parametrize("M,K", [(3, 200), (64, 3840), (17, 8)])
+@pytest.mark.parametrize("M,K", [(3, 200), (64, 3840), (17, 8), (300, 10240), (1, 10240)])
 def test_act_quant_plain_bitexact(cuda, M, K):
     x = seeded_x(M, K, seed=7)
     q, sx, _ = _act_quant(x, had=False, want_rot=False)
     oq, osx = ops.act_quant_plain(x)
     assert torch.equal(q, oq) and torch.equal(sx, osx.flatten())
+
+
+@pytest.mark.parametrize("K", [3840, 10240, 256])
+def test_act_quant_plain_ties_round_half_even(cuda, K):
+    """Rows with |max| 127 (x_scale exactly 1) whose values sit on every half-integer tie in
+    (-127, 127): the quantiser's integer rounding is round-half-even, as torch.round."""
+    ties = torch.arange(-127, 127, dtype=torch.float32) + 0.5
+    row = torch.zeros(K)
+    row[0] = 127.0
+    row[1:1 + ties.numel()] = ties
+    row[1 + ties.numel():] = torch.linspace(-126.9, 126.9, K - 1 - ties.numel())
+    x = torch.stack([row, -row, row.roll(7)]).to(torch.bfloat16)
+    q, sx, _ = _act_quant(x, had=False, want_rot=False)
+    oq, osx = ops.act_quant_plain(x)
+    assert torch.equal(sx, osx.flatten()) and float(sx[0]) == 1.0
+    assert torch.equal(q, oq)
 
 
 def test_bounded_wait_expires_and_the_context_stays_usable(cuda):
@@ -417,6 +433,30 @@ def test_rmsnorm_mod_and_quant_bitexact(cuda):
     assert torch.equal(q.cpu(), oq)
 
 
+@pytest.mark.parametrize("had,with_shift", [(False, True), (True, True)])
+def test_rmsnorm_mod_quant_shift_and_plain_bitexact(cuda, had, with_shift):
+    """The 3840-wide norm + modulation + quantisation (quad-layout kernel) over 500 rows of two
+    batches, with the shift, with and without the rotation."""
+    B, S, D = 2, 250, 3840
+    x = seeded_x(B * S, D, seed=14).reshape(B, S, D)
+    w = _norm_w(D, 15)
+    gen = torch.Generator().manual_seed(16)
+    scale = (torch.randn(B, D, generator=gen) * 0.1).to(torch.bfloat16)
+    shift = (torch.randn(B, D, generator=gen) * 0.1).to(torch.bfloat16) if with_shift else None
+    want = ops.modulate(ops.rms_norm(x, w, 1e-5), scale, shift).reshape(B * S, D)
+    oq, osx = ops.act_quant_had128(want)[:2] if had else ops.act_quant_plain(want)
+    xd, wd, sd = x.cuda().contiguous(), w.float().cuda(), scale.cuda()
+    hd = None if shift is None else shift.cuda()
+    q = torch.empty(B * S, D, dtype=torch.int8, device="cuda")
+    sx = torch.empty(B * S, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_rmsnorm_mod_quant", xd.data_ptr(), D, wd.data_ptr(), sd.data_ptr(),
+              None if hd is None else hd.data_ptr(), D, S, q.data_ptr(), D, sx.data_ptr(), B * S, D, 1e-5,
+              1 if had else 0, _lib.stream_of(xd))
+    torch.cuda.synchronize()
+    assert torch.equal(sx.cpu(), osx.flatten())
+    assert torch.equal(q.cpu(), oq)
+
+
 def test_norm_gate_residual_and_fused_quant_bitexact(cuda):
     from zimage_b200 import triton_fused_norm_gate_residual
 
@@ -442,6 +482,43 @@ def test_norm_gate_residual_and_fused_quant_bitexact(cuda):
     assert torch.equal(y2.cpu().reshape(B, S, D), want)
     nxt = ops.modulate(ops.rms_norm(want, w2, 1e-6), s)
     oq, osx, _ = ops.act_quant_had128(nxt.reshape(B * S, D))
+    assert torch.equal(sx.cpu(), osx.flatten())
+    assert torch.equal(q.cpu(), oq)
+
+
+@pytest.mark.parametrize("rows,had,with_shift", [(1, True, False), (600, True, True), (257, False, False)])
+def test_norm_gate_residual_mod_quant_rows_bitexact(cuda, rows, had, with_shift):
+    """The fused norm kernel at the step width (3840, the register-resident kernel) over many
+    rows of two batches, with and without the rotation and the shift."""
+    D = 3840
+    B = 2 if rows > 1 else 1
+    per = (rows + B - 1) // B
+    x = seeded_x(rows, D, seed=41 + rows)
+    r = seeded_x(rows, D, seed=42 + rows)
+    x[0] *= 300.0  # a large row next to ordinary ones
+    gen = torch.Generator().manual_seed(43)
+    g = torch.tanh(torch.randn(B, D, generator=gen)).to(torch.bfloat16)
+    s = (torch.randn(B, D, generator=gen) * 0.1).to(torch.bfloat16)
+    h = (torch.randn(B, D, generator=gen) * 0.1).to(torch.bfloat16) if with_shift else None
+    w, w2 = _norm_w(D, 5), _norm_w(D, 6)
+    bidx = torch.arange(rows) // per
+    # each row as its own [1, 1, D] batch item of the oracle, with its batch's vectors
+    want = ops.norm_gate_residual(x.reshape(rows, 1, D), r.reshape(rows, 1, D), g[bidx], w, 1e-5)
+    nxt = ops.modulate(ops.rms_norm(want, w2, 1e-6), s[bidx], None if h is None else h[bidx])
+    want, nxt = want.reshape(rows, D), nxt.reshape(rows, D)
+    oq, osx = ops.act_quant_had128(nxt)[:2] if had else ops.act_quant_plain(nxt)
+    xd, rd, gd, sd = x.cuda(), r.cuda(), g.cuda(), s.cuda()
+    hd = None if h is None else h.cuda()
+    wd, w2d = w.float().cuda(), w2.float().cuda()
+    y = torch.empty(rows, D, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(rows, D, dtype=torch.int8, device="cuda")
+    sx = torch.empty(rows, dtype=torch.bfloat16, device="cuda")
+    _lib.call("zib_norm_gate_residual_mod_quant", xd.data_ptr(), D, rd.data_ptr(), D, gd.data_ptr(), D, per,
+              wd.data_ptr(), y.data_ptr(), D, w2d.data_ptr(), sd.data_ptr(),
+              None if hd is None else hd.data_ptr(), D, q.data_ptr(), D, sx.data_ptr(), rows, D, 1e-5, 1e-6,
+              1 if had else 0, _lib.stream_of(xd))
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu(), want)
     assert torch.equal(sx.cpu(), osx.flatten())
     assert torch.equal(q.cpu(), oq)
 
