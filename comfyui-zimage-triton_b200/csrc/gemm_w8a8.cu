@@ -88,6 +88,7 @@ struct Params {
   int M, N, K;  // N: output columns (SWIGLU: features)
   int num_mb, num_nb, num_kb, num_tiles;
   int n_fast;  // tile order: 0 = M-blocks fastest (B read once), 1 = N-blocks fastest (A read once)
+  int group;   // blocks of the fast index per group (the tiles sweep one group at a time)
   const uint16_t* sx;
   const uint16_t* sw;   // per weight row (SWIGLU: w1 scales)
   const uint16_t* sw2;  // SWIGLU: w3 scales
@@ -95,6 +96,7 @@ struct Params {
   const uint16_t* bias;
   uint16_t* y;
   int64_t ldy;
+  int st32;  // y rows 32-byte aligned (y and ldy): the plain epilogue stores whole 32-byte sectors
   int32_t* acc;
   int64_t ldacc;
   // QKROPE
@@ -367,6 +369,20 @@ __device__ __forceinline__ void epi_chunk(const Params& p, int row, int n0, cons
         *reinterpret_cast<int4*>(dst + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
     } else {
       for (int j = 0; j < 32 && n0 + j < p.N; ++j) dst[j] = (int)r[j];
+    }
+  } else if (full && !p.bias && p.st32) {
+    // one 32-byte store per 16 columns: whole L2 sectors instead of two half-sector writes
+    uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 16) {
+      const uint4 wa = ldg_u4(p.sw + n0 + j), wb = ldg_u4(p.sw + n0 + j + 8);
+      const uint32_t o0 = dequant2(r[j], r[j + 1], sx2, wa.x), o1 = dequant2(r[j + 2], r[j + 3], sx2, wa.y);
+      const uint32_t o2 = dequant2(r[j + 4], r[j + 5], sx2, wa.z), o3 = dequant2(r[j + 6], r[j + 7], sx2, wa.w);
+      const uint32_t o4 = dequant2(r[j + 8], r[j + 9], sx2, wb.x), o5 = dequant2(r[j + 10], r[j + 11], sx2, wb.y);
+      const uint32_t o6 = dequant2(r[j + 12], r[j + 13], sx2, wb.z), o7 = dequant2(r[j + 14], r[j + 15], sx2, wb.w);
+      asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + j), "r"(o0), "r"(o1),
+                   "r"(o2), "r"(o3), "r"(o4), "r"(o5), "r"(o6), "r"(o7)
+                   : "memory");
     }
   } else if (full && !p.bias) {
     uint16_t* dst = p.y + (int64_t)row * p.ldy + n0;
@@ -699,14 +715,23 @@ __device__ __forceinline__ void load_b_part(uint8_t* dst, const CUtensorMap* b0,
 
 // Tile t -> (M-block, N-block).  Consecutive tiles run concurrently on the
 // persistent CTAs, so the fastest-varying block index decides which operand
-// stays resident in L2 while the other one streams.
+// stays resident in L2 while the other one streams.  The fast index runs in
+// groups of p.group blocks: the tiles sweep every block of the slow index for
+// one group before the next group, so the resident part of that operand is
+// one group's rows, not all of them (M = 18432: A is 70.8 MB, more than stays
+// in L2 next to the streamed outputs).
 __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mb, int& nb) {
+  const int nfast = p.n_fast ? p.num_nb : p.num_mb, nslow = p.n_fast ? p.num_mb : p.num_nb;
+  const int per_group = p.group * nslow;
+  const int g = tile / per_group, r = tile - g * per_group;
+  const int gsize = min(p.group, nfast - g * p.group);  // the last group may be smaller
+  const int f = g * p.group + r % gsize, sl = r / gsize;
   if (p.n_fast) {
-    mb = tile / p.num_nb;
-    nb = tile % p.num_nb;
+    nb = f;
+    mb = sl;
   } else {
-    mb = tile % p.num_mb;
-    nb = tile / p.num_mb;
+    mb = f;
+    nb = sl;
   }
 }
 
@@ -1180,6 +1205,18 @@ static int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t o
 
 // 0 = automatic (2-CTA pairs when M > 128), 1 = 1-CTA tiles, 2 = 2-CTA pairs
 static int g_gemm_variant = 0;
+constexpr int64_t kGroupBudgetDefault = 48ll << 20;
+static int64_t g_group_budget = kGroupBudgetDefault;
+
+// Blocks of the fast index per group: as few groups as keep one group's rows of the
+// re-read operand within the L2 budget, of balanced sizes.
+static int group_blocks(int64_t nfast, int64_t block_bytes) {
+  int64_t per = g_group_budget / block_bytes;
+  if (per < 1) per = 1;
+  if (per >= nfast) return (int)nfast;
+  const int64_t ngroups = (nfast + per - 1) / per;
+  return (int)((nfast + ngroups - 1) / ngroups);
+}
 
 static int num_sms_for_current_device() {
   int dev = 0;
@@ -1420,14 +1457,17 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
     }
     attr_set[pair][EPI][dev] = true;
   }
-  // The operand that is read once per wave of concurrent tiles is the one whose
-  // block index varies fastest: stream the smaller one, keep the larger one resident.
+  // The operand whose block index varies fastest is re-read by every wave of concurrent
+  // tiles (it has to stay resident in L2); the other one streams once.  The smaller
+  // operand takes the fast index, in groups that fit the L2 budget.
   const int64_t a_bytes = M * K, b_bytes = (int64_t)w_rows * K * (EPI == EPI_SWIGLU ? 2 : 1);
   p.n_fast = a_bytes > b_bytes ? 1 : 0;
+  p.st32 = p.y && ((uintptr_t)p.y & 31) == 0 && (p.ldy & 15) == 0;
   const int sms = num_sms_for_current_device();
   if (pair) {
     p.num_mb = (int)((M + 255) / 256);
     p.num_tiles = p.num_mb * p.num_nb;
+    p.group = group_blocks(p.n_fast ? p.num_nb : p.num_mb, 256 * K);  // 256 rows per block either way
     int clusters = sms / 2;
     p.num_units = p.num_tiles;
     p.tail_start = p.num_tiles;
@@ -1447,6 +1487,7 @@ static int launch(const void* q, int64_t ldq, const void* w, const void* w2, int
   } else {
     p.num_mb = (int)((M + 127) / 128);
     p.num_tiles = p.num_mb * p.num_nb;
+    p.group = group_blocks(p.n_fast ? p.num_nb : p.num_mb, (p.n_fast ? 256 : 128) * K);
     p.num_units = p.num_tiles;
     p.tail_start = p.num_tiles;
     p.splits = 1;
@@ -1666,6 +1707,15 @@ void zib_gemm_split_reset() {
   }
   cudaSetDevice(dev);
   cudaGetLastError();
+}
+
+extern "C" int zib_gemm_set_group_budget(int64_t bytes) {
+  if (bytes < 0) {
+    zib_set_error("gemm_set_group_budget: bytes must be >= 0");
+    return ZIB_ERR_INVALID_ARG;
+  }
+  zib::gemm::g_group_budget = bytes > 0 ? bytes : zib::gemm::kGroupBudgetDefault;
+  return ZIB_OK;
 }
 
 extern "C" int zib_gemm_set_variant(int variant) {

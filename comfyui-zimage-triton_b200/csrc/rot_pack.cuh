@@ -137,9 +137,9 @@ __device__ __forceinline__ f2 exp_pair(f2 x) {
             __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23)));
 }
 
-// bf16(g * sigmoid(g)) of the bf16 pair g2 (swiglu.py:51-55), sigmoid = the
+// g * sigmoid(g) in fp32 of the bf16 pair g2 (swiglu.py:51-55), sigmoid = the
 // correctly rounded reciprocal of 1 + exp(-g), 0 where exp(-g) overflows fp32
-__device__ __forceinline__ uint32_t silu_bf16x2(uint32_t g2) {
+__device__ __forceinline__ f2 silu_f32x2(uint32_t g2) {
   const f2 g = from_bf16x2(g2);
   const f2 e = exp_pair(mul(g, mk(-1.0f, -1.0f)));
   float d0, d1, g0, g1;
@@ -147,8 +147,11 @@ __device__ __forceinline__ uint32_t silu_bf16x2(uint32_t g2) {
   split(g, g0, g1);
   const float s0 = -g0 > kExpOverflow ? 0.0f : __frcp_rn(d0);
   const float s1 = -g1 > kExpOverflow ? 0.0f : __frcp_rn(d1);
-  return to_bf16x2(mul(g, mk(s0, s1)));
+  return mul(g, mk(s0, s1));
 }
+
+// bf16(g * sigmoid(g)) of the bf16 pair g2
+__device__ __forceinline__ uint32_t silu_bf16x2(uint32_t g2) { return to_bf16x2(silu_f32x2(g2)); }
 
 // (a + b, a - b) for the bf16 pair w = (a low, b high), each rounded once to fp32
 __device__ __forceinline__ f2 bfly0(uint32_t w) {

@@ -591,8 +591,9 @@ __global__ void __launch_bounds__(32 * warps_of(R)) swiglu_wr(
 #pragma unroll 4
     for (int k = 0; k < cpl; ++k) {
       const uint4 gv = ld_nc(gr + 256 * k), uv = ld_nc(ur + 256 * k);
-      const uint4 v = make_uint4(hmul2(px::silu_bf16x2(gv.x), uv.x), hmul2(px::silu_bf16x2(gv.y), uv.y),
-                                 hmul2(px::silu_bf16x2(gv.z), uv.z), hmul2(px::silu_bf16x2(gv.w), uv.w));
+      const uint4 v =
+          make_uint4(hmul2(px::silu_bf16x2(gv.x), uv.x), hmul2(px::silu_bf16x2(gv.y), uv.y),
+                     hmul2(px::silu_bf16x2(gv.z), uv.z), hmul2(px::silu_bf16x2(gv.w), uv.w));
       if (!QUANT) {
         *reinterpret_cast<uint4*>(out + row * ldo + f0 + 256 * k) = v;
       } else {

@@ -45,6 +45,7 @@ SIGNATURES: dict[str, list] = {
                                    _F32, _F32, _VP, _VP, _I64, _I64, _I64, _VP],
     "zib_gemm_set_variant": [_I32],
     "zib_gemm_set_split": [_I32],
+    "zib_gemm_set_group_budget": [_I64],
     "zib_gemm_set_split_workspace": [_I32, _VP, _I64, _VP, _I64],
     "zib_gemm_w8a8_static_scratch": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _I32, _VP],
     "zib_weight_prep": [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _VP],

@@ -261,6 +261,9 @@ CASES = {
     "gemm_w13_swiglu_had": (lambda: case_gemm_swiglu(M_TOK, F, D), "int8"),
     "gemm_w13_swiglu_had_w13": (lambda: case_gemm_swiglu_w13(M_TOK, F, D), "int8"),
     "gemm_w13_swiglu_had_w13_m18432": (lambda: case_gemm_swiglu_w13(2 * M_TOK, F, D), "int8"),
+    "gemm_qkv_qk_rope_m18432": (lambda: case_gemm_qk_rope(2 * M_TOK, D), "int8"),
+    "gemm_out_m18432": (lambda: case_gemm(2 * M_TOK, D, D), "int8"),
+    "gemm_w2_m18432": (lambda: case_gemm(2 * M_TOK, D, F), "int8"),
     "sdpa_torch": (lambda: case_sdpa(), "bf16"),
 }
 

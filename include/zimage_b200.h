@@ -147,8 +147,17 @@ ZIB_API int zib_gemm_set_variant(int variant);
  * tiles run as 2-4 units over slices of K whose int32 partials are summed by
  * the last unit to finish (bit-identical results).  It needs the workspace
  * that the caller registers with zib_gemm_set_split_workspace; without one
- * the GEMM runs unsplit.  No reference counterpart (tuning knob). */
+ * the GEMM runs unsplit.  The same switch governs the half-width tail: a last
+ * wave of at most half as many tiles as CTA pairs (and no split) runs as twice
+ * as many units of 128 output columns.  No reference counterpart (tuning knob). */
 ZIB_API int zib_gemm_set_split(int enable);
+
+/* L2 budget of the GEMM tile order for subsequent zib_gemm_w8a8* calls on this
+ * process, in bytes (0 restores the default, 48 MiB): the operand that every
+ * wave of concurrent tiles re-reads is swept in groups of blocks whose rows fit
+ * the budget, all tiles of one group before the next.  Results are identical
+ * for every budget.  No reference counterpart (tuning knob). */
+ZIB_API int zib_gemm_set_group_budget(int64_t bytes);
 
 /* Registers the caller's split-K workspace for `device` (NULL, NULL
  * unregisters): `ws` (16-byte aligned) holds ws_bytes / 256 KB partial-tile

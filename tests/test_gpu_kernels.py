@@ -523,6 +523,27 @@ def test_norm_gate_residual_mod_quant_rows_bitexact(cuda, rows, had, with_shift)
     assert torch.equal(q.cpu(), oq)
 
 
+@pytest.mark.parametrize("M,N,K,budget", [(1536, 2304, 512, 1 << 18), (1792, 2304, 512, 3 << 17),
+                                          (2048, 1024, 768, 1 << 18), (700, 4096, 384, 1 << 17),
+                                          (384, 768, 256, 0)])
+def test_gemm_grouped_tile_order_bitexact(cuda, gemm_variant, M, N, K, budget):
+    """Tile orders that sweep the re-read operand in groups (a small L2 budget forces several
+    groups of balanced and unbalanced sizes, both operand orders): the same int32 accumulators
+    and outputs as the oracle."""
+    lib = _lib.load()
+    q, w = _rand_i8((M, K), 71 + M), _rand_i8((N, K), 72 + N)
+    try:
+        assert lib.zib_gemm_set_group_budget(budget) == 0
+        acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+        qd, wd = q.cuda(), w.cuda()
+        _lib.call("zib_gemm_w8a8_acc_i32", qd.data_ptr(), K, wd.data_ptr(), K, acc.data_ptr(), N, M, N, K,
+                  _lib.stream_of(qd))
+        torch.cuda.synchronize()
+    finally:
+        assert lib.zib_gemm_set_group_budget(0) == 0
+    assert torch.equal(acc.cpu(), ops.gemm_acc_i32(q, w))
+
+
 def test_swiglu_and_fused_quant(cuda):
     from zimage_b200 import triton_swiglu_forward
 
