@@ -108,6 +108,21 @@ __device__ __forceinline__ uint4 norm_w(const uint4& d, float rstd, const float*
   return norm_w(d, rstd, __ldg(reinterpret_cast<const float4*>(w)), __ldg(reinterpret_cast<const float4*>(w + 4)));
 }
 
+// bf16(bf16(v * rstd) * w) with the chunk's 8 weights as bf16 values: their product with a bf16
+// value is exact in fp32, so one packed bf16 multiply (one rounding of the exact product) gives
+// the result of norm_w on the same weights held as fp32
+__device__ __forceinline__ uint4 norm_w16(const uint4& d, float rstd, const uint4& w) {
+  const f2 RS = mk(rstd, rstd);
+  const uint32_t v[4] = {d.x, d.y, d.z, d.w}, wv[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t n = to_bf16x2(mul(from_bf16x2(v[k]), RS));
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o[k]) : "r"(n), "r"(wv[k]));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // zib_expf on both lanes: the same clamp, range reduction, Horner steps and
 // exponent insertion, each packed operation rounding each lane once
 __device__ __forceinline__ f2 exp_pair(f2 x) {

@@ -1292,7 +1292,7 @@ extern "C" int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, cons
   cudaStream_t st = (cudaStream_t)stream;
   bool launched = false;
   if (n == 3840) {  // the register-resident kernel (teams of three warps, five chunks per lane)
-    auto k = hadamard ? wr::ngr_rg<5, true> : wr::ngr_rg<5, false>;
+    auto k = hadamard ? wr::ngr_rg<5, true, false> : wr::ngr_rg<5, false, false>;
     k<<<wr::grid_rg(k, 96, 1, rows), 96, 0, st>>>(
         (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
         (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
@@ -1323,6 +1323,31 @@ extern "C" int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, cons
             w, (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
             (uint16_t*)sx, n, eps, eps2)));
   return zib_check_launch("norm_gate_residual_mod_quant");
+}
+
+extern "C" int zib_norm_gate_residual_mod_quant_w16(const void* x, int64_t ldx, const void* r, int64_t ldr,
+                                                    const void* gate, int64_t ld_gate, int64_t rows_per_batch,
+                                                    const void* w, void* y, int64_t ldy,
+                                                    const void* w2, const void* scale, const void* shift,
+                                                    int64_t ld_mod, void* q, int64_t ldq, void* sx,
+                                                    int64_t rows, int64_t n, float eps, float eps2,
+                                                    int hadamard, void* stream) {
+  ZIB_HOST_CHECK(x && r && gate && w && y && w2 && scale && q && sx, ZIB_ERR_INVALID_ARG,
+                 "norm_gate_residual_mod_quant_w16: null pointer");
+  ZIB_HOST_CHECK(rows >= 0 && n == 3840 && rows_per_batch > 0, ZIB_ERR_INVALID_ARG,
+                 "norm_gate_residual_mod_quant_w16: rows of 3840 features only (n=%lld)", (long long)n);
+  ZIB_HOST_CHECK(ldx % 8 == 0 && ldr % 8 == 0 && ldy % 8 == 0 && ld_gate % 8 == 0 && ld_mod % 8 == 0 &&
+                     ldq % 8 == 0 && aligned16(x) && aligned16(r) && aligned16(y) && aligned16(gate) &&
+                     aligned16(w) && aligned16(w2) && aligned16(scale) && aligned16(q) && (!shift || aligned16(shift)),
+                 ZIB_ERR_ALIGNMENT, "norm_gate_residual_mod_quant_w16: misaligned operand");
+  if (rows == 0) return ZIB_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  auto k = hadamard ? wr::ngr_rg<5, true, true> : wr::ngr_rg<5, false, true>;
+  k<<<wr::grid_rg(k, 96, 1, rows), 96, 0, st>>>(
+      (const uint16_t*)x, ldx, (const uint16_t*)r, ldr, (const uint16_t*)gate, ld_gate, rows_per_batch, w,
+      (uint16_t*)y, ldy, w2, (const uint16_t*)scale, (const uint16_t*)shift, ld_mod, (int8_t*)q, ldq,
+      (uint16_t*)sx, n, eps, eps2, rows);
+  return zib_check_launch("norm_gate_residual_mod_quant_w16");
 }
 
 extern "C" int zib_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out,

@@ -474,13 +474,21 @@ __global__ void __launch_bounds__(32 * warps_of(R)) act_quant_rg(const uint16_t*
   }
 }
 
+// the chunk's norm with the weights at element offset e of w: fp32 (norm_w) or bf16 (W16: norm_w16)
+template <bool W16>
+__device__ __forceinline__ uint4 norm_any(const uint4& d, float rstd, const void* __restrict__ w, int64_t e) {
+  if (W16) return px::norm_w16(d, rstd, ld_nc(reinterpret_cast<const uint16_t*>(w) + e));
+  return px::norm_w(d, rstd, reinterpret_cast<const float*>(w) + e);
+}
+
 // ngr_wr<3, true, HAD> (norm + gate + residual, then norm * (1+s) (+shift) ->
-// rotate / quantise) with the rows x and r in registers
-template <int CPL, bool HAD>
+// rotate / quantise) with the rows x and r in registers; W16: the norm weights w, w2 are
+// bf16 (half the L1 traffic of fp32 weights, which take two half-sector loads per chunk)
+template <int CPL, bool HAD, bool W16>
 __global__ void __launch_bounds__(96) ngr_rg(
     const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ r, int64_t ldr,
-    const uint16_t* __restrict__ gate, int64_t ld_gate, int64_t rows_per_batch, const float* __restrict__ w,
-    uint16_t* __restrict__ y, int64_t ldy, const float* __restrict__ w2, const uint16_t* __restrict__ scale,
+    const uint16_t* __restrict__ gate, int64_t ld_gate, int64_t rows_per_batch, const void* __restrict__ w,
+    uint16_t* __restrict__ y, int64_t ldy, const void* __restrict__ w2, const uint16_t* __restrict__ scale,
     const uint16_t* __restrict__ shift, int64_t ld_mod, int8_t* __restrict__ q, int64_t ldq,
     uint16_t* __restrict__ sx, int64_t n, float eps, float eps2, int64_t rows) {
   constexpr int R = 3;
@@ -505,7 +513,7 @@ __global__ void __launch_bounds__(96) ngr_rg(
     double ss2 = 0.0;
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
-      const uint4 nv = px::norm_w(a[k], rstd, w + f0 + 256 * k);
+      const uint4 nv = norm_any<W16>(a[k], rstd, w, f0 + 256 * k);
       const uint4 g = ld_nc(gl + 256 * k);
       // RN_bf16(r + g * a), one rounding, as in ngr_wr
       a[k] = make_uint4(hfma2(g.x, nv.x, e[k].x), hfma2(g.y, nv.y, e[k].y), hfma2(g.z, nv.z, e[k].z),
@@ -518,7 +526,7 @@ __global__ void __launch_bounds__(96) ngr_rg(
     px::AbsMax m;
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
-      a[k] = modulate(px::norm_w(a[k], rstd2, w2 + f0 + 256 * k), ld_nc(scale + mo + 256 * k),
+      a[k] = modulate(norm_any<W16>(a[k], rstd2, w2, f0 + 256 * k), ld_nc(scale + mo + 256 * k),
                       shift ? ld_nc(shift + mo + 256 * k) : make_uint4(0, 0, 0, 0), shift != nullptr);
       rot_amax<HAD>(a[k], m, t.lane);
     }

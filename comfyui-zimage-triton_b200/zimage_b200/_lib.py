@@ -57,6 +57,9 @@ SIGNATURES: dict[str, list] = {
                                _VP],
     "zib_norm_gate_residual_mod_quant": [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _VP, _VP, _I64, _VP, _VP,
                                          _VP, _I64, _VP, _I64, _VP, _I64, _I64, _F32, _F32, _I32, _VP],
+    "zib_norm_gate_residual_mod_quant_w16": [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _VP, _VP, _I64, _VP,
+                                             _VP, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _F32, _F32, _I32,
+                                             _VP],
     "zib_swiglu": [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP],
     "zib_swiglu_quant": [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I32, _VP],
     "zib_qknorm_rope": [_VP, _I64, _I64, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _I64, _VP, _I64, _I64,

@@ -71,19 +71,23 @@ def case_rmsnorm_mod_quant(M=M_TOK, Dm=D):
     return run, M * Dm * 2 + M * Dm + M * 2 + Dm * 4 + B * Dm * 2, f"[{M},{Dm}] norm*mod -> int8"
 
 
-def case_norm_gate_residual_mod_quant(M=M_TOK, Dm=D):
+def case_norm_gate_residual_mod_quant(M=M_TOK, Dm=D, w16=False):
+    """w16: the entry with bf16 norm weights (the fused block path's, for bf16 modules)."""
     x, r = _bf16(M, Dm), _bf16(M, Dm, seed=1)
     gates, raw = _bf16(B, 2, Dm, seed=2) * 0.3, _bf16(B, 4 * Dm, seed=3) * 0.1
-    w = torch.ones(Dm, device="cuda")
+    w = torch.ones(Dm, device="cuda", dtype=torch.bfloat16 if w16 else torch.float32)
     y, q, sx = _empty(M, Dm), _empty(M, Dm, dtype=torch.int8), _empty(M)
     st = _lib.stream_of(x)
+    entry = "zib_norm_gate_residual_mod_quant_w16" if w16 else "zib_norm_gate_residual_mod_quant"
 
     def run():
-        _lib.call("zib_norm_gate_residual_mod_quant", x.data_ptr(), Dm, r.data_ptr(), Dm, gates.data_ptr(), 2 * Dm,
+        _lib.call(entry, x.data_ptr(), Dm, r.data_ptr(), Dm, gates.data_ptr(), 2 * Dm,
                   M // B, w.data_ptr(), y.data_ptr(), Dm, w.data_ptr(), raw.data_ptr(), None, 4 * Dm, q.data_ptr(),
                   Dm, sx.data_ptr(), M, Dm, 1e-5, 1e-5, 1, st)
 
-    return run, 3 * M * Dm * 2 + M * Dm + M * 2 + 2 * Dm * 4 + 2 * B * Dm * 2, f"[{M},{Dm}] x,r -> y + int8"
+    wbytes = 2 * Dm * w.element_size()
+    return (run, 3 * M * Dm * 2 + M * Dm + M * 2 + wbytes + 2 * B * Dm * 2,
+            f"[{M},{Dm}] x,r -> y + int8" + (" (bf16 norm weights)" if w16 else ""))
 
 
 def case_norm_gate_residual(M=M_TOK, Dm=D):
@@ -244,6 +248,7 @@ CASES = {
     "act_quant_plain_k10240": (lambda: case_act_quant(M_TOK, F, had=0), "hbm"),
     "rmsnorm_mod_quant": (lambda: case_rmsnorm_mod_quant(), "hbm"),
     "norm_gate_residual_mod_quant": (lambda: case_norm_gate_residual_mod_quant(), "hbm"),
+    "norm_gate_residual_mod_quant_w16": (lambda: case_norm_gate_residual_mod_quant(w16=True), "hbm"),
     "norm_gate_residual": (lambda: case_norm_gate_residual(), "hbm"),
     "swiglu_quant": (lambda: case_swiglu_quant(), "hbm"),
     "swiglu": (lambda: case_swiglu(), "hbm"),

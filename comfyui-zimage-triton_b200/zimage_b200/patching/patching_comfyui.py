@@ -239,6 +239,17 @@ def _f32(w: torch.Tensor) -> torch.Tensor:
     return w.detach().to(torch.float32).contiguous()
 
 
+def _bf16_exact(w: torch.Tensor) -> torch.Tensor | None:
+    """The norm weight as a contiguous bf16 tensor when every value is a bf16 value (always for
+    bf16 parameters), else None: the fused norm kernel's bf16-weight entry gives the same results
+    as its fp32 entry for such weights."""
+    w = w.detach()
+    if w.dtype == torch.bfloat16:
+        return w.contiguous()
+    h = w.to(torch.bfloat16)
+    return h.contiguous() if torch.equal(h.to(w.dtype), w) else None
+
+
 def _block_cache(block: nn.Module):
     """Per-block tensors of the fused path, or None when the block does not qualify.
 
@@ -269,6 +280,8 @@ def _block_cache(block: nn.Module):
         "an1": _f32(block.attention_norm1.weight), "an2": _f32(block.attention_norm2.weight),
         "fn1": _f32(block.ffn_norm1.weight), "fn2": _f32(block.ffn_norm2.weight),
         "qn": _f32(attn.q_norm.weight), "kn": _f32(attn.k_norm.weight),
+        "an1_h": _bf16_exact(block.attention_norm1.weight), "an2_h": _bf16_exact(block.attention_norm2.weight),
+        "fn1_h": _bf16_exact(block.ffn_norm1.weight), "fn2_h": _bf16_exact(block.ffn_norm2.weight),
         "eps_an1": _eps(block.attention_norm1), "eps_an2": _eps(block.attention_norm2),
         "eps_fn1": _eps(block.ffn_norm1), "eps_fn2": _eps(block.ffn_norm2),
         "eps_q": _eps(attn.q_norm), "eps_k": _eps(attn.k_norm),
@@ -335,6 +348,15 @@ def _gemm(q8, sx, lin_w, lin_s, y, M, N, K, stream):
                 sx.data_ptr(), lin_s.data_ptr(), None, y.data_ptr(), y.stride(0), M, N, K, stream)
 
 
+def _ngr_entry(D: int, ca: dict, a: str, cb: dict, b: str):
+    """Entry point and weights of the fused norm + gate + residual + next norm + quantisation: the
+    bf16-weight entry when both norm weights hold bf16 values and the row width is its 3840."""
+    wa, wb = ca[a + "_h"], cb[b + "_h"]
+    if D == 3840 and wa is not None and wb is not None:
+        return "zib_norm_gate_residual_mod_quant_w16", wa, wb
+    return "zib_norm_gate_residual_mod_quant", ca[a], cb[b]
+
+
 def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freqs_cis: torch.Tensor,
                         adaln_input: torch.Tensor) -> torch.Tensor:
     """One S3-DiT block on the fused kernels; arithmetic of patching_comfyui.py:340-415."""
@@ -395,10 +417,10 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
     x1 = torch.empty(M, D, dtype=bf, device=dev)
     q8f = torch.empty(M, D, dtype=i8, device=dev)
     sxf = torch.empty(M, dtype=bf, device=dev)
-    _lib.call("zib_norm_gate_residual_mod_quant", attn_out.data_ptr(), D, x.data_ptr(), D, gates.data_ptr(),
-              gates.stride(0), S, c["an2"].data_ptr(), x1.data_ptr(), D, c["fn1"].data_ptr(),
-              raw.data_ptr() + 2 * D * esz, None, raw.stride(0), q8f.data_ptr(), D, sxf.data_ptr(), M, D,
-              float(c["eps_an2"]), float(c["eps_fn1"]), 1, stream)
+    ngr, wa, wb = _ngr_entry(D, c, "an2", c, "fn1")
+    _lib.call(ngr, attn_out.data_ptr(), D, x.data_ptr(), D, gates.data_ptr(), gates.stride(0), S, wa.data_ptr(),
+              x1.data_ptr(), D, wb.data_ptr(), raw.data_ptr() + 2 * D * esz, None, raw.stride(0), q8f.data_ptr(), D,
+              sxf.data_ptr(), M, D, float(c["eps_an2"]), float(c["eps_fn1"]), 1, stream)
     # w1 and w3 GEMMs + SwiGLU + w2-input rotation in one launch, then quantise   (swiglu.py:51-58)
     x_rot = torch.empty(M, F_, dtype=bf, device=dev)
     w13 = c.get("w13")
@@ -427,11 +449,10 @@ def fused_block_forward(block: nn.Module, c: dict, x: torch.Tensor, x_mask, freq
     raw_n, gates_n = _adaln(nxt, adaln_input, B, D, stream)
     q8n = torch.empty(M, D, dtype=i8, device=dev)
     sxn = torch.empty(M, dtype=bf, device=dev)
-    _lib.call("zib_norm_gate_residual_mod_quant", ffn_out.data_ptr(), D, x1.data_ptr(), D,
-              gates.data_ptr() + D * esz, gates.stride(0), S, c["fn2"].data_ptr(), x2.data_ptr(), D,
-              cn["an1"].data_ptr(), raw_n.data_ptr(), None, raw_n.stride(0), q8n.data_ptr(), D, sxn.data_ptr(), M, D,
-              float(c["eps_fn2"]),
-              float(cn["eps_an1"]), 1, stream)
+    ngr, wa, wb = _ngr_entry(D, c, "fn2", cn, "an1")
+    _lib.call(ngr, ffn_out.data_ptr(), D, x1.data_ptr(), D, gates.data_ptr() + D * esz, gates.stride(0), S,
+              wa.data_ptr(), x2.data_ptr(), D, wb.data_ptr(), raw_n.data_ptr(), None, raw_n.stride(0),
+              q8n.data_ptr(), D, sxn.data_ptr(), M, D, float(c["eps_fn2"]), float(cn["eps_an1"]), 1, stream)
     out = x2.view(B, S, D)
     _HANDOFF = {"block": nxt, "x": (out.data_ptr(), out._version, tuple(out.shape)),
                 "adaln": (adaln_input.data_ptr(), adaln_input._version),

@@ -250,6 +250,19 @@ ZIB_API int zib_norm_gate_residual_mod_quant(const void* x, int64_t ldx, const v
                                      int64_t ld_mod, void* q, int64_t ldq, void* sx,
                                      int64_t rows, int64_t n, float eps, float eps2,
                                      int hadamard, void* stream);
+/* zib_norm_gate_residual_mod_quant with the norm weights w, w2 given as bf16 (the
+ * modules' own bf16 parameters) instead of fp32 copies: the same results for the same
+ * weight values (the product of a bf16 weight and a bf16 value is exact in fp32 in the
+ * normal range, so one bf16 rounding of it equals the fp32 product rounded to bf16),
+ * half the weight traffic.  Rows of n = 3840 features only; ZIB_ERR_INVALID_ARG
+ * otherwise.  Same reference lines as above. */
+ZIB_API int zib_norm_gate_residual_mod_quant_w16(const void* x, int64_t ldx, const void* r, int64_t ldr,
+                                         const void* gate, int64_t ld_gate, int64_t rows_per_batch,
+                                         const void* w, void* y, int64_t ldy,
+                                         const void* w2, const void* scale, const void* shift,
+                                         int64_t ld_mod, void* q, int64_t ldq, void* sx,
+                                         int64_t rows, int64_t n, float eps, float eps2,
+                                         int hadamard, void* stream);
 
 /* SwiGLU: out = bf16( bf16(silu_fp32(gate)) * up ) (kernels/swiglu.py:20-59, :62-110).
  * gate/up/out: bf16 [rows, n] with strides ldg/ldu/ldo. */

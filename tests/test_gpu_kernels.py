@@ -544,6 +544,35 @@ def test_gemm_grouped_tile_order_bitexact(cuda, gemm_variant, M, N, K, budget):
     assert torch.equal(acc.cpu(), ops.gemm_acc_i32(q, w))
 
 
+@pytest.mark.parametrize("had,with_shift", [(True, False), (False, True)])
+def test_norm_gate_residual_mod_quant_bf16_weights_equal_fp32(cuda, had, with_shift):
+    """The bf16-weight entry gives the fp32 entry's outputs for the same (bf16-valued) weights."""
+    rows, D, S = 700, 3840, 350
+    x, r = seeded_x(rows, D, seed=81).cuda(), seeded_x(rows, D, seed=82).cuda()
+    gen = torch.Generator().manual_seed(83)
+    g = torch.tanh(torch.randn(2, D, generator=gen)).to(torch.bfloat16).cuda()
+    sc = (torch.randn(2, D, generator=gen) * 0.1).to(torch.bfloat16).cuda()
+    sh = (torch.randn(2, D, generator=gen) * 0.1).to(torch.bfloat16).cuda() if with_shift else None
+    w, w2 = _norm_w(D, 84).cuda(), _norm_w(D, 85).cuda()
+    outs = []
+    for entry, wa, wb in (("zib_norm_gate_residual_mod_quant", w.float(), w2.float()),
+                          ("zib_norm_gate_residual_mod_quant_w16", w, w2)):
+        y = torch.empty(rows, D, dtype=torch.bfloat16, device="cuda")
+        q = torch.empty(rows, D, dtype=torch.int8, device="cuda")
+        sx = torch.empty(rows, dtype=torch.bfloat16, device="cuda")
+        _lib.call(entry, x.data_ptr(), D, r.data_ptr(), D, g.data_ptr(), D, S, wa.data_ptr(), y.data_ptr(), D,
+                  wb.data_ptr(), sc.data_ptr(), None if sh is None else sh.data_ptr(), D, q.data_ptr(), D,
+                  sx.data_ptr(), rows, D, 1e-5, 1e-6, 1 if had else 0, _lib.stream_of(x))
+        torch.cuda.synchronize()
+        outs.append((y.cpu(), q.cpu(), sx.cpu()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    with pytest.raises(ValueError):  # other row widths are refused
+        _lib.call("zib_norm_gate_residual_mod_quant_w16", x.data_ptr(), 1024, r.data_ptr(), 1024, g.data_ptr(),
+                  1024, S, w.data_ptr(), x.data_ptr(), 1024, w2.data_ptr(), sc.data_ptr(), None, 1024,
+                  x.data_ptr(), 1024, x.data_ptr(), rows, 1024, 1e-5, 1e-6, 1, _lib.stream_of(x))
+
+
 def test_swiglu_and_fused_quant(cuda):
     from zimage_b200 import triton_swiglu_forward
 
