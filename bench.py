@@ -64,6 +64,7 @@ NCU_TRAFFIC = {("zib_gemm_w8a8_swiglu_had_w13", 9216): 290541312,
                ("zib_gemm_w8a8_swiglu_had_w13", 18432): 290568960 + 356516096}
 WORKLOAD = (f"Z-Image 30-layer S3-DiT (dim 3840, 30 heads, FFN 10240, 2+2 refiner blocks), 1024x1024, "
             f"{N_IMAGES}-image batch sharded by image, Base: {BASE_STEPS}-step Euler, CFG {BASE_CFG}, shift {SHIFT}, "
+            f"scheduler simple (Turbo: {TURBO_STEPS}-step res_multistep, CFG 1.0), "
             f"micro-batches of {MICRO} images; linears W8A8+Hadamard128, bf16 SDPA")
 CONFIG = {"workload": WORKLOAD, "global_batch": N_IMAGES, "seq_len": SEQ, "cfg_rows_per_image": 2,
           "l2": "no flush: 5.4 GB int8 weights streamed per micro-batch step >> 126 MB L2"}
@@ -416,7 +417,7 @@ def run_ours(args) -> None:
 
     t_cap = time.time()
     base = FlowSampler(model, (LAT_C, LAT_HW, LAT_HW), (N_TXT, CAP_DIM), micro_batch=MICRO, cfg=BASE_CFG,
-                       steps=BASE_STEPS, shift=SHIFT, device=dev)
+                       steps=BASE_STEPS, shift=SHIFT, device=dev, sampler="euler", scheduler="simple")
     capture_s = time.time() - t_cap
     lat = lat0.clone()
 
@@ -424,12 +425,12 @@ def run_ours(args) -> None:
         """Step i of the schedule over this rank's micro-batches (one graph replay each)."""
         for k in range(n_mb):
             sl = slice(k * MICRO, (k + 1) * MICRO)
-            lat[sl].copy_(base.step(lat[sl], caps[k], i % BASE_STEPS))
+            lat[sl].copy_(base.step(lat[sl], caps[k], i % BASE_STEPS, mb=k))
 
     # launches of this library per micro-batch step, counted on an eager step
     launches0 = _lib.LAUNCHES
     with torch.no_grad():
-        base._step(lat[:MICRO].clone(), caps[0], base._sigmas_dev[0:2])
+        base.eager_step(lat[:MICRO].clone(), caps[0], 0, mb=-1)
     launches_per_mb = _lib.LAUNCHES - launches0
     torch.cuda.synchronize()
 
@@ -468,7 +469,7 @@ def run_ours(args) -> None:
     xs = lat[:MICRO].clone()
     with torch.no_grad():
         for i in range(gemm_steps):
-            base._step(xs, caps[0], base._sigmas_dev[i:i + 2])
+            base.eager_step(xs, caps[0], i, mb=-1)
     torch.cuda.synchronize()
     gem = pc.GEMM_EVENTS
     pc.GEMM_EVENTS = None
@@ -494,7 +495,7 @@ def run_ours(args) -> None:
     for i in range(args.steps):
         for k in range(n_mb):
             sl = slice(k * MICRO, (k + 1) * MICRO)
-            y = base.graph(lat_pin[sl], caps_pin[k], base._sigmas_dev[(i % BASE_STEPS):(i % BASE_STEPS) + 2])
+            y = base.step(lat_pin[sl], caps_pin[k], i % BASE_STEPS, mb=k)
             lat_pin[sl].copy_(y, non_blocking=True)
     gather_images(lat_pin.to(dev, non_blocking=True), N_IMAGES)
     f1.record()
@@ -510,7 +511,7 @@ def run_ours(args) -> None:
     # Turbo: one full 4-step generation without guidance (after one untimed generation)
     del base
     turbo = FlowSampler(model, (LAT_C, LAT_HW, LAT_HW), (N_TXT, CAP_DIM), micro_batch=MICRO, cfg=1.0,
-                        steps=TURBO_STEPS, shift=SHIFT, device=dev)
+                        steps=TURBO_STEPS, shift=SHIFT, device=dev, sampler="res_multistep", scheduler="simple")
     tlat = lat0.clone()
     cond_d = cond_h.to(dev)
     turbo.sample(tlat, cond_d)

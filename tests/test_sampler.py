@@ -30,6 +30,99 @@ def test_flow_sigmas_schedule():
         flow_sigmas(0)
 
 
+def test_simple_schedule():
+    """ComfyUI's ``simple`` scheduler over the AuraFlow-shifted table: the steps pick table
+    entries 1000 - int(j * 1000 / steps); equal to the linear schedule when steps divides 1000."""
+    from zimage_b200.sampler import flow_sigmas, schedule_sigmas, simple_sigmas
+
+    assert torch.allclose(simple_sigmas(4, 3.0), flow_sigmas(4, 3.0), rtol=0, atol=1e-7)
+    s = simple_sigmas(30, 3.0)
+    assert s.shape == (31,) and float(s[0]) == 1.0 and float(s[-1]) == 0.0
+    assert bool((s[1:] < s[:-1]).all())
+    for j in (1, 7, 29):
+        t = (1000 - int(j * (1000 / 30))) / 1000
+        assert abs(float(s[j]) - 3 * t / (1 + 2 * t)) < 1e-6
+    assert float(s[1]) != float(flow_sigmas(30, 3.0)[1])  # 0.967 of the table, not 1 - 1/30
+    with pytest.raises(ValueError):
+        schedule_sigmas(4, 3.0, "karras")
+
+
+def _cpu_sampler(model, sampler, steps, shift=3.0):
+    from zimage_b200.sampler import FlowSampler
+
+    return FlowSampler(model, (1, 2, 2), (1, 4), micro_batch=1, cfg=1.0, steps=steps, shift=shift,
+                       device="cpu", use_graph=False, sampler=sampler)
+
+
+@pytest.mark.parametrize("sampler", ["euler", "res_multistep"])
+def test_samplers_exact_for_a_constant_denoised_estimate(sampler):
+    """A model whose denoised estimate D = x - sigma v is a constant: the flow is
+    x(sigma) = D + sigma / sigma_0 (x_0 - D), which both samplers follow to fp32 rounding."""
+    D = torch.tensor([[[[0.5, -1.0], [2.0, 0.25]]]])
+
+    def model(x, t, cap):
+        sigma = 1.0 - t[0]
+        return (x - D) / sigma
+
+    s = _cpu_sampler(model, sampler, steps=8)
+    x0 = torch.tensor([[[[1.0, 3.0], [-2.0, 0.0]]]])
+    x = x0.clone()
+    cap = torch.zeros(1, 1, 4, dtype=torch.bfloat16)
+    for i in range(7):
+        x = s.step(x, cap, i)
+        want = D + float(s.sigmas[i + 1]) / float(s.sigmas[0]) * (x0 - D)
+        assert torch.allclose(x, want, atol=2e-6), (i, x, want)
+    x = s.step(x, cap, 7)
+    assert torch.allclose(x, D, atol=2e-6)
+
+
+def test_res_multistep_is_second_order():
+    """D linear in lambda = -log sigma (D = A + B lambda): the exact flow is
+    x(lambda) = A + B (lambda - 1) + (x_0 - A + B) e^-lambda.  After the first (Euler) step the
+    multistep update interpolates D exactly, so its error stays far below Euler's."""
+    A, B = torch.tensor(0.3), torch.tensor(0.8)
+
+    def model(x, t, cap):
+        sigma = 1.0 - t[0]
+        lam = -torch.log(sigma)
+        return (x - (A + B * lam)) / sigma
+
+    x0 = torch.full((1, 1, 2, 2), 1.5)
+    cap = torch.zeros(1, 1, 4, dtype=torch.bfloat16)
+    errs = {}
+    for sampler in ("euler", "res_multistep"):
+        s = _cpu_sampler(model, sampler, steps=30)
+        x = x0.clone()
+        for i in range(29):  # up to the last nonzero sigma (lambda finite)
+            x = s.step(x, cap, i)
+        lam = -torch.log(s.sigmas[29].double())
+        exact = A.double() + B.double() * (lam - 1) + (1.5 - A.double() + B.double()) * torch.exp(-lam)
+        errs[sampler] = float((x.double() - exact).abs().max())
+    assert errs["res_multistep"] < errs["euler"] / 5, errs
+
+
+def test_step_coefficients():
+    from zimage_b200.sampler import step_coefficients
+
+    sig = torch.tensor([1.0, 0.9, 0.75, 0.5, 0.0])
+    e = step_coefficients(sig, "euler")
+    assert torch.allclose(e[:, 1], torch.ones(4)) and torch.allclose(e[:, 2], sig[1:] - sig[:-1])
+    assert torch.equal(e[:, 3], torch.zeros(4))
+    r = step_coefficients(sig, "res_multistep")
+    assert torch.equal(r[0], e[0]) and torch.equal(r[3], e[3])  # Euler first and into sigma = 0
+    assert bool((r[1:3, 3] != 0).all())
+    # a constant D: a + (1 - a) ... the update reproduces x -> D + (s'/s)(x - D)
+    for i in (1, 2):
+        s0, s1 = float(sig[i]), float(sig[i + 1])
+        a, b, c = (float(v) for v in r[i, 1:])
+        # x = 1, D = 0 (v = 1 / s0): new x = a + b / s0 + c * 0 = s1 / s0
+        assert abs(a + b / s0 - s1 / s0) < 1e-6
+        # x = 0, D = 1 (v = -1 / s0): new x = -b / s0 + c = 1 - s1 / s0
+        assert abs(-b / s0 + c - (1 - s1 / s0)) < 1e-6
+    with pytest.raises(ValueError):
+        step_coefficients(sig, "dpmpp_2m")
+
+
 @pytest.mark.parametrize("n_images,micro", [(16, 2), (8, 2), (12, 4)])
 def test_micro_batches_do_not_depend_on_the_world_size(n_images, micro):
     """Every rank's images split into the same micro-batches (same image pairs in the same
