@@ -257,6 +257,7 @@ CASES = {
     "qknorm_rope": (lambda: case_qknorm_rope(), "hbm"),
     "weight_prep": (lambda: case_weight_prep(), "hbm"),
     "gemm_cfg1_qkv_m1024": (lambda: case_gemm(1024, 3 * D, D), "int8"),
+    "gemm_one_tile": (lambda: case_gemm(256, 256, 128), "int8"),  # the launch's fixed cost
     "gemm_adaln_stack": (lambda: case_gemm(2, 30 * 4 * D, 256), "int8"),
     "gemm_qkv": (lambda: case_gemm(M_TOK, 3 * D, D), "int8"),
     "gemm_out": (lambda: case_gemm(M_TOK, D, D), "int8"),

@@ -244,6 +244,48 @@ def weight_fingerprint(w: torch.Tensor) -> tuple:
     return (w.data_ptr(), w._version, hash(flat[idx].float().cpu().numpy().tobytes()))
 
 
+class _HostMover:
+    """Moves CUDA tensors into ordinary (pageable) host memory through two pinned staging
+    buffers: each chunk's device-to-host copy runs at pinned-memory speed while the host copies
+    the previous chunk out of the other buffer.  A pageable ``.to("cpu")`` goes through the
+    driver's own staging and measured 2.0 GB/s on a B200 machine for the 12.3 GB of bf16
+    linear weights of the 30-layer model."""
+
+    def __init__(self, chunk_bytes: int = 64 << 20):
+        self.chunk = chunk_bytes
+        self.stage: list[torch.Tensor] = []
+        self.done: list[torch.cuda.Event] = []
+
+    def move(self, t: torch.Tensor) -> torch.Tensor:
+        if not t.is_cuda or t.numel() == 0:
+            return t.to(device="cpu")
+        if not self.stage:
+            self.stage = [torch.empty(self.chunk, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+            self.done = [torch.cuda.Event(), torch.cuda.Event()]
+        src = t.detach().contiguous().reshape(-1).view(torch.uint8)
+        dst = torch.empty(t.shape, dtype=t.dtype, device="cpu")
+        out = dst.reshape(-1).view(torch.uint8)
+        stream = torch.cuda.current_stream(t.device)
+        pending: list[tuple[int, int] | None] = [None, None]
+        n, c = src.numel(), self.chunk
+        for i, off in enumerate(range(0, n, c)):
+            k = i % 2
+            if pending[k] is not None:  # the buffer's previous chunk: wait for it, then drain it
+                self.done[k].synchronize()
+                o, m = pending[k]
+                out[o:o + m].copy_(self.stage[k][:m])
+            m = min(c, n - off)
+            self.stage[k][:m].copy_(src[off:off + m], non_blocking=True)
+            self.done[k].record(stream)
+            pending[k] = (off, m)
+        for k in sorted(range(2), key=lambda j: pending[j][0] if pending[j] else -1):
+            if pending[k] is not None:
+                self.done[k].synchronize()
+                o, m = pending[k]
+                out[o:o + m].copy_(self.stage[k][:m])
+        return dst
+
+
 def apply_int8_quantization(model: nn.Module, min_dim: int = _MIN_DIM, mode: str = "w8a8",
                             skip_sensitive: bool = True, policy: str | None = None,
                             lora_aware: bool = False) -> dict[str, int]:
@@ -259,13 +301,14 @@ def apply_int8_quantization(model: nn.Module, min_dim: int = _MIN_DIM, mode: str
     Returns {"quantized", "skipped", "sensitive", "had_skipped"}.
     """
     plan, stats = select_layers(model, min_dim, mode, skip_sensitive, policy)
+    mover = _HostMover()
     for name, module, had in plan:
         in_f, out_f = module.in_features, module.out_features
         w_int8, w_scale = quantize_weight(module.weight.data, had)
         target = module.weight.device
         module.register_buffer("_w_int8", w_int8.to(target))
         module.register_buffer("_w_scale", w_scale.to(device=target, dtype=module.weight.dtype))
-        module.weight.data = module.weight.data.to(device="cpu")
+        module.weight.data = mover.move(module.weight.data)
         module._int8_src = weight_fingerprint(module.weight)
 
         module.forward = _make_w8a8_forward(module, had)

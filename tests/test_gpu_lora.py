@@ -50,6 +50,21 @@ def test_refresh_requantises_a_patched_linear(cuda):
     assert torch.equal(lin._w_int8.cpu(), ops.weight_prep(w0)[0])
 
 
+@pytest.mark.parametrize("shape,dtype,chunk", [((1000, 333), torch.bfloat16, 4096), ((64, 64), torch.float32, 1 << 20),
+                                               ((3, 5, 7), torch.bfloat16, 16)])
+def test_source_weights_reach_host_memory_unchanged(cuda, shape, dtype, chunk):
+    """apply_int8_quantization moves each quantised layer's source weight to ordinary host memory
+    through pinned staging chunks (odd sizes, many chunks, one chunk): the same bits, pageable."""
+    from zimage_b200.quantization.int8_linear import _HostMover
+
+    g = torch.Generator().manual_seed(len(shape))
+    w = torch.randn(shape, generator=g).to(dtype)
+    wd = w.cuda()
+    got = _HostMover(chunk_bytes=chunk).move(wd)
+    assert got.device.type == "cpu" and not got.is_pinned()
+    assert got.dtype == dtype and got.shape == w.shape and torch.equal(got, w)
+
+
 def _model(params, lora_aware):
     import nodes
     from zimage_b200.nextdit import NextDiT, load_layer_params
