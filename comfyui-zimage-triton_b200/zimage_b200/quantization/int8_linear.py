@@ -278,7 +278,7 @@ class _HostMover:
             self.stage[k][:m].copy_(src[off:off + m], non_blocking=True)
             self.done[k].record(stream)
             pending[k] = (off, m)
-        for k in sorted(range(2), key=lambda j: pending[j][0] if pending[j] else -1):
+        for k in (0, 1):  # the last chunk of each buffer
             if pending[k] is not None:
                 self.done[k].synchronize()
                 o, m = pending[k]
