@@ -595,6 +595,10 @@ def run_ours(args) -> None:
                                         f"no ncu capture at {m_launch} rows"),
                      "all_gemms_tops": None if gemm_tops is None else round(gemm_tops, 1),
                      "gemm_kernels": kernels,
+                     # the datasheet peak holds at the 1965 MHz boost clock; the step runs power-capped
+                     "frac_at_step_clock": None if (achieved is None or not clocks.get("sm_mhz")) else round(
+                         achieved / (INT8_DATASHEET_TOPS * clocks["sm_mhz"] / (clocks.get("sm_max_mhz") or 1965.0)), 4),
+                     "step_clock_basis": "datasheet peak x median SM clock of the timed region / max SM clock",
                      "timing": "CUDA events around each GEMM launch in eager micro-batch steps right after "
                                "the graph-timed region"},
         "e2e": {"value": round(e2e_ms / args.steps / N_IMAGES, 3), "unit": "ms",
