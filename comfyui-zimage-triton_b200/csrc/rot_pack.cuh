@@ -152,6 +152,18 @@ __device__ __forceinline__ f2 exp_pair(f2 x) {
             __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23)));
 }
 
+// RN(1/d), d >= 1: Markstein's method (P. Markstein, "Computation of elementary functions on the
+// IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): the hardware reciprocal
+// approximation r0 (within one ulp) corrected once with the exact residual e = 1 - d r0 (an fma)
+// as r0 + r0 e (an fma, one rounding).  Reciprocals below the normal range take the IEEE
+// reciprocal.  Equal to it on every d the SiLU forms (checked exhaustively over all bf16 gates).
+__device__ __forceinline__ float rcp_rn_pos(float d) {
+  if (!(d < 8.50705917e37f)) return __frcp_rn(d);  // 2^126: 1/d would leave the normal range
+  float r0;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(d));
+  return __fmaf_rn(r0, __fmaf_rn(-d, r0, 1.0f), r0);
+}
+
 // g * sigmoid(g) in fp32 of the bf16 pair g2 (swiglu.py:51-55), sigmoid = the
 // correctly rounded reciprocal of 1 + exp(-g), 0 where exp(-g) overflows fp32
 __device__ __forceinline__ f2 silu_f32x2(uint32_t g2) {
@@ -160,8 +172,8 @@ __device__ __forceinline__ f2 silu_f32x2(uint32_t g2) {
   float d0, d1, g0, g1;
   split(add(mk(1.0f, 1.0f), e), d0, d1);
   split(g, g0, g1);
-  const float s0 = -g0 > kExpOverflow ? 0.0f : __frcp_rn(d0);
-  const float s1 = -g1 > kExpOverflow ? 0.0f : __frcp_rn(d1);
+  const float s0 = -g0 > kExpOverflow ? 0.0f : rcp_rn_pos(d0);
+  const float s1 = -g1 > kExpOverflow ? 0.0f : rcp_rn_pos(d1);
   return mul(g, mk(s0, s1));
 }
 

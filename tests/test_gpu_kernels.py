@@ -573,6 +573,26 @@ def test_norm_gate_residual_mod_quant_bf16_weights_equal_fp32(cuda, had, with_sh
                   x.data_ptr(), 1024, x.data_ptr(), rows, 1024, 1e-5, 1e-6, 1, _lib.stream_of(x))
 
 
+def test_swiglu_silu_on_every_bf16_gate(cuda):
+    """bf16(bf16(silu(g)) * 1) for every finite bf16 gate g (all 65,280 of them) equals the
+    oracle's fp32 SiLU rounded to bf16: the kernels' SiLU is exact on its whole input domain."""
+    import numpy as np
+
+    g = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    g = g[torch.isfinite(g.float())].reshape(255, 256)  # 256-wide rows: the warp-per-row kernel's form
+    up = torch.ones_like(g)
+    out = torch.empty_like(g, device="cuda")
+    gd, ud = g.cuda(), up.cuda()
+    _lib.call("zib_swiglu", gd.data_ptr(), 256, ud.data_ptr(), 256, out.data_ptr(), 256, 255, 256,
+              _lib.stream_of(gd))
+    torch.cuda.synchronize()
+    gf = g.float().numpy()
+    with np.errstate(over="ignore"):
+        want = torch.from_numpy((gf * ops.sigmoid_f32(gf)).astype(np.float32)).to(torch.bfloat16)
+    bad = (out.cpu() != want).nonzero()
+    assert bad.numel() == 0, [(float(g[i, j]), float(out[i, j]), float(want[i, j])) for i, j in bad[:8]]
+
+
 def test_swiglu_and_fused_quant(cuda):
     from zimage_b200 import triton_swiglu_forward
 
