@@ -218,6 +218,48 @@ def test_step_bitexact_given_attention_library_outputs(cuda):
         assert max_abs(o, ref) <= 2e-2
 
 
+def test_step_follows_in_place_norm_weight_updates(cuda):
+    """Full width, 2 layers: the fused norm kernels read the norm modules' current weights.  A
+    bf16 weight scaled in place, an fp32 weight holding bf16 values (bf16-weight entry, on a
+    copy), then that weight moved off the bf16 grid in place (fp32 entry) each give the oracle's
+    bits for the weights of the moment."""
+    dim, heads, ffn, L = 3840, 30, 10240, 2
+    m, params = _small_model(L, dim, heads, ffn, seed=4)
+    _patch(m)
+    x, t, fm, fc = _inputs(2, 8, 8, 16, dim, seed=9)
+    b0, b1 = m.layers
+
+    def check():
+        rec, restore = _record_attention()
+        try:
+            with torch.no_grad():
+                y = m(x.cuda(), t.cuda(), fm.cuda()).cpu()
+        finally:
+            restore()
+        layers = _gpu_weights_into(params, m)
+        for blk, q in zip(m.layers, layers):
+            for k in ("attention_norm1", "attention_norm2", "ffn_norm1", "ffn_norm2"):
+                q[k] = getattr(blk, k).weight.detach().cpu()
+        assert torch.equal(y, omodel.step_forward(layers, x, fc, t, n_heads=heads, attn=_replay(rec)))
+        return y
+
+    y0 = check()
+    with torch.no_grad():
+        b1.attention_norm1.weight.mul_(1.25)
+    y1 = check()
+    assert not torch.equal(y1, y0)
+    w = b0.ffn_norm2.weight
+    b0.ffn_norm2.weight = torch.nn.Parameter(w.detach().float() * 0.5, requires_grad=False)
+    y2 = check()
+    assert not torch.equal(y2, y1)
+    assert b0.__dict__["_zib_cache"]["fn2_h"] is not None
+    with torch.no_grad():
+        b0.ffn_norm2.weight.add_(2.0 ** -12)
+    y3 = check()
+    assert not torch.equal(y3, y2)
+    assert b0.__dict__["_zib_cache"]["fn2_h"] is None
+
+
 def test_step_vs_fp32_attention_oracle(cuda):
     """Against an oracle with fp32 attention the only difference is the attention library's
     bf16 numerics, which the W8A8 re-quantisation of its output amplifies.  Measured:
