@@ -55,7 +55,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         subprocess.run(cmd, check=True)
         objs.append(str(o))
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs, "-lcuda" if False else "-lcudart_static",
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs, "-lcudart_static",
            "-Xcompiler", "-fPIC"]
     subprocess.run(cmd, check=True)
     os.replace(tmp, OUT)
